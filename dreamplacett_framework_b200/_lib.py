@@ -1,0 +1,102 @@
+"""ctypes binding of libepb200.so (include/epb.h).
+
+The library is the product's compute path; there is no fallback.  Loading
+fails with an exception when the shared object is missing.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG, "libepb200.so")
+
+EPB_OK = 0
+EPB_EINVAL = 1
+EPB_ECUDA = 2
+EPB_ENCCL = 3
+EPB_ETIMEOUT = 4
+EPB_EOVERFLOW = 5
+EPB_ENOSTATE = 6
+EPB_FLAG_NONFINITE_CELL = 0x1
+EPB_FLAG_SATURATED = 0x2
+
+# Every symbol include/epb.h declares (the CPU tests check the exports).
+EXPORTS = (
+    "epb_version", "epb_status_string", "epb_create", "epb_destroy", "epb_last_error",
+    "epb_geometry", "epb_set_initial_density", "epb_forward", "epb_backward",
+    "epb_scatter_fixed", "epb_dct_solve", "epb_gather", "epb_error_flags",
+)
+
+
+class EpbConfig(ctypes.Structure):
+    _fields_ = [
+        ("num_bins_x", ctypes.c_int32), ("num_bins_y", ctypes.c_int32),
+        ("xl", ctypes.c_double), ("yl", ctypes.c_double),
+        ("xh", ctypes.c_double), ("yh", ctypes.c_double),
+        ("fixed_point_bits", ctypes.c_int32), ("device", ctypes.c_int32),
+        ("flags", ctypes.c_int32), ("reserved", ctypes.c_int32),
+    ]
+
+
+class EpbCells(ctypes.Structure):
+    _fields_ = [
+        ("x", ctypes.c_void_p), ("y", ctypes.c_void_p),
+        ("size_x", ctypes.c_void_p), ("size_y", ctypes.c_void_p),
+        ("offset_x", ctypes.c_void_p), ("offset_y", ctypes.c_void_p),
+        ("ratio", ctypes.c_void_p),
+        ("begin0", ctypes.c_int64), ("end0", ctypes.c_int64),
+        ("begin1", ctypes.c_int64), ("end1", ctypes.c_int64),
+    ]
+
+
+class EpbError(RuntimeError):
+    def __init__(self, status, message):
+        super().__init__(f"epb status {status}: {message}")
+        self.status = status
+
+
+_lib = None
+
+
+def load():
+    """Load and prototype libepb200.so; raises when it is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(
+            f"libepb200.so not found at {LIB_PATH}: build it with "
+            "`python -m dreamplacett_framework_b200.build` (no CPU fallback exists)")
+    L = ctypes.CDLL(LIB_PATH)
+    vp, i32, i64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64
+    cp = ctypes.POINTER(EpbCells)
+    L.epb_version.restype = ctypes.c_char_p
+    L.epb_status_string.argtypes = [ctypes.c_int]
+    L.epb_status_string.restype = ctypes.c_char_p
+    L.epb_create.argtypes = [ctypes.POINTER(EpbConfig), ctypes.POINTER(vp)]
+    L.epb_destroy.argtypes = [vp]
+    L.epb_last_error.argtypes = [vp]
+    L.epb_last_error.restype = ctypes.c_char_p
+    L.epb_geometry.argtypes = [vp, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_float),
+                               ctypes.POINTER(i32)]
+    L.epb_set_initial_density.argtypes = [vp, vp, vp]
+    L.epb_forward.argtypes = [vp, cp, vp, vp, vp, vp, vp, vp]
+    L.epb_backward.argtypes = [vp, cp, vp, vp, vp, vp]
+    L.epb_scatter_fixed.argtypes = [vp, cp, vp, vp]
+    L.epb_dct_solve.argtypes = [vp, vp, vp, vp, vp, vp, vp]
+    L.epb_gather.argtypes = [vp, cp, vp, vp, vp, vp, vp, vp]
+    L.epb_error_flags.argtypes = [vp, vp, ctypes.POINTER(ctypes.c_uint32)]
+    for name in EXPORTS:
+        if name not in ("epb_version", "epb_status_string", "epb_last_error"):
+            getattr(L, name).restype = ctypes.c_int
+    _lib = L
+    return L
+
+
+def check(handle, status):
+    if status != EPB_OK:
+        L = load()
+        msg = L.epb_last_error(handle) if handle else None
+        msg = msg.decode() if msg else L.epb_status_string(status).decode()
+        raise EpbError(status, msg or L.epb_status_string(status).decode())

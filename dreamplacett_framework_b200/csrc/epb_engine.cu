@@ -1,0 +1,475 @@
+// epb_engine.cu -- host engine and C ABI of libepb200.so.
+//
+// Replaces the reference's out-of-process server
+// (host/density_scatter_ttnn_server_host.cpp: argv parse :324-339, sizing
+// :405-460, per-iteration loop :1326-1824, TTNNDCTSolver :225-306) with an
+// in-process, stream-ordered engine on device pointers.  See include/epb.h for
+// the per-function mapping.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/epb.h"
+#include "epb_kernels.cuh"
+
+using namespace epb;
+
+struct epb_handle {
+    int dev = 0;
+    int M = 0, N = 0;
+    double xl = 0, yl = 0, xh = 0, yh = 0;
+    float bsx = 0, bsy = 0;
+    int S = 0;
+    double dscale = 0;          // 2^-S / bin_area
+    long long* grid = nullptr;  // int64 [M*N], kept zeroed between forwards
+    bool grid_dirty = false;
+    float* init = nullptr;      // normalised initial density [M*N]
+    bool has_init = false;
+    float* t1 = nullptr;        // [M*N]
+    float* gx = nullptr;        // [M*N]
+    float* gy = nullptr;
+    float* gp = nullptr;
+    float2* fxy = nullptr;      // interleaved fields of the last forward
+    bool have_fields = false;
+    float2 *twM = nullptr, *qwM = nullptr, *twN = nullptr, *qwN = nullptr;
+    float *wu = nullptr, *wv = nullptr;
+    double* partials = nullptr;
+    unsigned* counter = nullptr;
+    double* energy_d = nullptr;
+    unsigned* flags = nullptr;
+    std::string err;
+};
+
+namespace {
+
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = true;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+int fail(epb_handle* h, int code, const std::string& msg) {
+    if (h) h->err = msg;
+    return code;
+}
+
+int cuda_fail(epb_handle* h, cudaError_t e, const char* what) {
+    return fail(h, EPB_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+#define EPB_CUDA(h, call)                                                  \
+    do {                                                                   \
+        cudaError_t e_ = (call);                                           \
+        if (e_ != cudaSuccess) return cuda_fail((h), e_, #call);           \
+    } while (0)
+
+#define EPB_LAUNCHED(h, what)                                              \
+    do {                                                                   \
+        cudaError_t e_ = cudaGetLastError();                               \
+        if (e_ != cudaSuccess) return cuda_fail((h), e_, what);            \
+    } while (0)
+
+bool pow2_in_range(int v) { return v >= 16 && v <= 4096 && (v & (v - 1)) == 0; }
+
+GridGeom geom(const epb_handle* h) {
+    GridGeom g;
+    g.M = h->M; g.N = h->N;
+    g.xl = (float)h->xl; g.yl = (float)h->yl;
+    g.bsx = h->bsx; g.bsy = h->bsy;
+    g.ibsx = (float)(1.0 / (double)h->bsx);
+    g.ibsy = (float)(1.0 / (double)h->bsy);
+    return g;
+}
+
+int make_view(epb_handle* h, const epb_cells* c, CellView& v) {
+    if (!c) return fail(h, EPB_EINVAL, "cells is NULL");
+    const int64_t n0 = c->end0 - c->begin0, n1 = c->end1 - c->begin1;
+    if (c->begin0 < 0 || c->begin1 < 0 || n0 < 0 || n1 < 0)
+        return fail(h, EPB_EINVAL, "cell ranges must satisfy 0 <= begin <= end");
+    if (n0 + n1 > 0 && (!c->x || !c->y || !c->size_x || !c->size_y))
+        return fail(h, EPB_EINVAL, "x, y, size_x and size_y must be non-NULL");
+    v.x = c->x; v.y = c->y; v.sx = c->size_x; v.sy = c->size_y;
+    v.ox = c->offset_x; v.oy = c->offset_y; v.ratio = c->ratio;
+    v.b0 = c->begin0; v.n0 = n0; v.b1 = c->begin1; v.n = n0 + n1;
+    return EPB_OK;
+}
+
+unsigned cell_blocks(int64_t n) {
+    int64_t b = (n + 255) / 256;
+    if (b < 1) b = 1;
+    if (b > (1 << 20)) b = 1 << 20;  // grid-stride beyond this
+    return (unsigned)b;
+}
+
+// twiddles exp(-2 pi i t / L) and quarter-wave (cos, sin)(pi k / 2L), fp64 -> fp32
+void host_tables(int L, std::vector<float2>& tw, std::vector<float2>& qw) {
+    tw.resize(L); qw.resize(L);
+    for (int t = 0; t < L; ++t) {
+        const double a = 2.0 * M_PI * (double)t / (double)L;
+        tw[t] = make_float2((float)std::cos(a), (float)(-std::sin(a)));
+        const double b = M_PI * (double)t / (2.0 * (double)L);
+        qw[t] = make_float2((float)std::cos(b), (float)std::sin(b));
+    }
+}
+
+template <typename T>
+int dev_alloc(epb_handle* h, T** p, size_t count) {
+    cudaError_t e = cudaMalloc((void**)p, count * sizeof(T));
+    if (e != cudaSuccess) { *p = nullptr; return cuda_fail(h, e, "cudaMalloc"); }
+    return EPB_OK;
+}
+
+void free_all(epb_handle* h) {
+    void* ptrs[] = {h->grid, h->init, h->t1, h->gx, h->gy, h->gp, h->fxy, h->twM, h->qwM,
+                    h->twN, h->qwN, h->wu, h->wv, h->partials, h->counter, h->energy_d, h->flags};
+    for (void* p : ptrs)
+        if (p) cudaFree(p);
+}
+
+// ----- kernel dispatch on the transform length -----
+
+template <int L>
+int set_smem(epb_handle* h, const void* fn, size_t bytes) {
+    if (bytes > 48 * 1024) EPB_CUDA(h, cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+    return EPB_OK;
+}
+
+template <int L>
+int launch_row_fwd_t(epb_handle* h, bool from_fixed, const float* rho_in, float* rho_out, cudaStream_t st) {
+    using C = RowFwdCfg<L>;
+    const unsigned blocks = (unsigned)((h->M + C::ROWS - 1) / C::ROWS);
+    const float* init = h->has_init && from_fixed ? h->init : nullptr;
+    if (from_fixed) {
+        auto fn = k_row_fwd<L, true>;
+        if (int rc = set_smem<L>(h, (const void*)fn, C::SMEM)) return rc;
+        fn<<<blocks, kFftThreads, C::SMEM, st>>>(h->grid, nullptr, init, h->dscale, h->M, rho_out, h->t1,
+                                                h->twN, h->qwN, h->flags);
+    } else {
+        auto fn = k_row_fwd<L, false>;
+        if (int rc = set_smem<L>(h, (const void*)fn, C::SMEM)) return rc;
+        fn<<<blocks, kFftThreads, C::SMEM, st>>>(nullptr, rho_in, nullptr, h->dscale, h->M, rho_out, h->t1,
+                                                h->twN, h->qwN, h->flags);
+    }
+    EPB_LAUNCHED(h, "k_row_fwd launch");
+    return EPB_OK;
+}
+
+template <int L>
+int launch_col_t(epb_handle* h, const ColArgs& a, cudaStream_t st) {
+    using C = ColCfg<L>;
+    const unsigned blocks = (unsigned)((h->N + C::W - 1) / C::W);
+    auto fn = k_col<L>;
+    if (int rc = set_smem<L>(h, (const void*)fn, C::SMEM)) return rc;
+    fn<<<blocks, kFftThreads, C::SMEM, st>>>(a);
+    EPB_LAUNCHED(h, "k_col launch");
+    return EPB_OK;
+}
+
+template <int L>
+int launch_row_inv_t(epb_handle* h, const RowInvArgs& a, cudaStream_t st) {
+    using C = RowInvCfg<L>;
+    const unsigned blocks = (unsigned)((h->M + C::ROWS - 1) / C::ROWS);
+    auto fn = k_row_inv<L>;
+    if (int rc = set_smem<L>(h, (const void*)fn, C::SMEM)) return rc;
+    fn<<<blocks, kFftThreads, C::SMEM, st>>>(a);
+    EPB_LAUNCHED(h, "k_row_inv launch");
+    return EPB_OK;
+}
+
+#define EPB_DISPATCH_L(Lval, CALL)                                          \
+    switch (Lval) {                                                         \
+        case 16: return CALL(16);                                           \
+        case 32: return CALL(32);                                           \
+        case 64: return CALL(64);                                           \
+        case 128: return CALL(128);                                         \
+        case 256: return CALL(256);                                         \
+        case 512: return CALL(512);                                         \
+        case 1024: return CALL(1024);                                       \
+        case 2048: return CALL(2048);                                       \
+        case 4096: return CALL(4096);                                       \
+        default: return fail(h, EPB_EINVAL, "unsupported transform length"); \
+    }
+
+int launch_row_fwd(epb_handle* h, bool from_fixed, const float* rho_in, float* rho_out, cudaStream_t st) {
+#define CALL_RF(L) launch_row_fwd_t<L>(h, from_fixed, rho_in, rho_out, st)
+    EPB_DISPATCH_L(h->N, CALL_RF)
+#undef CALL_RF
+}
+
+int launch_col(epb_handle* h, const ColArgs& a, cudaStream_t st) {
+#define CALL_C(L) launch_col_t<L>(h, a, st)
+    EPB_DISPATCH_L(h->M, CALL_C)
+#undef CALL_C
+}
+
+int launch_row_inv(epb_handle* h, const RowInvArgs& a, cudaStream_t st) {
+#define CALL_RI(L) launch_row_inv_t<L>(h, a, st)
+    EPB_DISPATCH_L(h->N, CALL_RI)
+#undef CALL_RI
+}
+
+int col_blocks(int M, int N) {
+    int W = 4;
+    switch (M) {
+        case 16: W = ColCfg<16>::W; break;
+        case 32: W = ColCfg<32>::W; break;
+        case 64: W = ColCfg<64>::W; break;
+        case 128: W = ColCfg<128>::W; break;
+        case 256: W = ColCfg<256>::W; break;
+        case 512: W = ColCfg<512>::W; break;
+        case 1024: W = ColCfg<1024>::W; break;
+        case 2048: W = ColCfg<2048>::W; break;
+        case 4096: W = ColCfg<4096>::W; break;
+    }
+    return (N + W - 1) / W;
+}
+
+// DCT solve from the state in t1 (after the row-forward pass).
+int solve_from_t1(epb_handle* h, cudaStream_t st, float* potential, float* field_x, float* field_y,
+                  float* energy) {
+    ColArgs ca;
+    ca.t1 = h->t1; ca.gx = h->gx; ca.gy = h->gy; ca.gp = h->gp;
+    ca.wu = h->wu; ca.wv = h->wv; ca.tw = h->twM; ca.qw = h->qwM;
+    ca.partials = h->partials; ca.counter = h->counter; ca.energy_d = h->energy_d;
+    ca.energy_out = energy; ca.N = h->N; ca.want_phi = potential != nullptr;
+    ca.energy_scale = (double)h->M * (double)h->N / 4.0;
+    if (int rc = launch_col(h, ca, st)) return rc;
+    RowInvArgs ra;
+    ra.gx = h->gx; ra.gy = h->gy; ra.gp = h->gp;
+    ra.fx = field_x; ra.fy = field_y; ra.phi = potential; ra.fxy = h->fxy;
+    ra.tw = h->twN; ra.qw = h->qwN; ra.M = h->M; ra.want_phi = potential != nullptr;
+    if (int rc = launch_row_inv(h, ra, st)) return rc;
+    h->have_fields = true;
+    return EPB_OK;
+}
+
+int scatter_into(epb_handle* h, const CellView& v, cudaStream_t st, long long* grid) {
+    if (v.n == 0) return EPB_OK;
+    const float qscale = ldexpf(1.0f, h->S);
+    k_scatter<<<cell_blocks(v.n), 256, 0, st>>>(v, geom(h), qscale, (unsigned long long*)grid, h->flags);
+    EPB_LAUNCHED(h, "k_scatter launch");
+    return EPB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* epb_version(void) { return "epb200 1.0 (sm_100a)"; }
+
+const char* epb_status_string(int s) {
+    switch (s) {
+        case EPB_OK: return "ok";
+        case EPB_EINVAL: return "invalid argument";
+        case EPB_ECUDA: return "CUDA error";
+        case EPB_ENCCL: return "NCCL error";
+        case EPB_ETIMEOUT: return "timeout";
+        case EPB_EOVERFLOW: return "fixed-point density saturated";
+        case EPB_ENOSTATE: return "no forward state";
+        default: return "unknown status";
+    }
+}
+
+int epb_create(const epb_config* cfg, epb_handle** out) {
+    if (!out) return EPB_EINVAL;
+    *out = nullptr;
+    if (!cfg) return EPB_EINVAL;
+    if (!pow2_in_range(cfg->num_bins_x) || !pow2_in_range(cfg->num_bins_y)) return EPB_EINVAL;
+    if (!(cfg->xh > cfg->xl) || !(cfg->yh > cfg->yl) || !std::isfinite(cfg->xl) || !std::isfinite(cfg->xh) ||
+        !std::isfinite(cfg->yl) || !std::isfinite(cfg->yh))
+        return EPB_EINVAL;
+    if (cfg->flags != 0 || cfg->fixed_point_bits > 60) return EPB_EINVAL;
+    epb_handle* h = new epb_handle();
+    h->dev = cfg->device;
+    h->M = cfg->num_bins_x; h->N = cfg->num_bins_y;
+    h->xl = cfg->xl; h->yl = cfg->yl; h->xh = cfg->xh; h->yh = cfg->yh;
+    // fp32 bin sizes as the reference server computes them (host:411)
+    h->bsx = ((float)cfg->xh - (float)cfg->xl) / (float)h->M;
+    h->bsy = ((float)cfg->yh - (float)cfg->yl) / (float)h->N;
+    if (cfg->fixed_point_bits > 0) {
+        h->S = cfg->fixed_point_bits;
+    } else {
+        const double area = (cfg->xh - cfg->xl) * (cfg->yh - cfg->yl);
+        int ib = (int)std::ceil(std::log2(area > 1.0 ? area : 1.0)) + 1;
+        if (ib < 32) ib = 32;
+        h->S = 63 - ib;
+    }
+    h->dscale = std::ldexp(1.0, -h->S) / ((double)h->bsx * (double)h->bsy);
+
+    DeviceGuard guard(h->dev);
+    if (!guard.ok) { delete h; return EPB_ECUDA; }
+    const size_t MN = (size_t)h->M * h->N;
+    int rc = EPB_OK;
+    const int ncolb = col_blocks(h->M, h->N);
+    if (!rc) rc = dev_alloc(h, &h->grid, MN);
+    if (!rc) rc = dev_alloc(h, &h->init, MN);
+    if (!rc) rc = dev_alloc(h, &h->t1, MN);
+    if (!rc) rc = dev_alloc(h, &h->gx, MN);
+    if (!rc) rc = dev_alloc(h, &h->gy, MN);
+    if (!rc) rc = dev_alloc(h, &h->gp, MN);
+    if (!rc) rc = dev_alloc(h, &h->fxy, MN);
+    if (!rc) rc = dev_alloc(h, &h->twM, (size_t)h->M);
+    if (!rc) rc = dev_alloc(h, &h->qwM, (size_t)h->M);
+    if (!rc) rc = dev_alloc(h, &h->twN, (size_t)h->N);
+    if (!rc) rc = dev_alloc(h, &h->qwN, (size_t)h->N);
+    if (!rc) rc = dev_alloc(h, &h->wu, (size_t)h->M);
+    if (!rc) rc = dev_alloc(h, &h->wv, (size_t)h->N);
+    if (!rc) rc = dev_alloc(h, &h->partials, (size_t)ncolb);
+    if (!rc) rc = dev_alloc(h, &h->counter, 1);
+    if (!rc) rc = dev_alloc(h, &h->energy_d, 1);
+    if (!rc) rc = dev_alloc(h, &h->flags, 1);
+    if (rc) { free_all(h); delete h; return rc; }
+
+    std::vector<float2> tw, qw;
+    std::vector<float> w;
+    cudaError_t e = cudaSuccess;
+    host_tables(h->M, tw, qw);
+    if (e == cudaSuccess) e = cudaMemcpy(h->twM, tw.data(), tw.size() * sizeof(float2), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(h->qwM, qw.data(), qw.size() * sizeof(float2), cudaMemcpyHostToDevice);
+    host_tables(h->N, tw, qw);
+    if (e == cudaSuccess) e = cudaMemcpy(h->twN, tw.data(), tw.size() * sizeof(float2), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(h->qwN, qw.data(), qw.size() * sizeof(float2), cudaMemcpyHostToDevice);
+    // wu = 2 pi u / M ; wv = 2 pi v / N * (bsx / bsy)   (host:254-256)
+    w.resize(h->M);
+    for (int u = 0; u < h->M; ++u) w[u] = (float)(2.0 * M_PI * u / h->M);
+    if (e == cudaSuccess) e = cudaMemcpy(h->wu, w.data(), w.size() * sizeof(float), cudaMemcpyHostToDevice);
+    w.resize(h->N);
+    const double asp = (double)(h->bsx / h->bsy);
+    for (int v = 0; v < h->N; ++v) w[v] = (float)(2.0 * M_PI * v / h->N * asp);
+    if (e == cudaSuccess) e = cudaMemcpy(h->wv, w.data(), w.size() * sizeof(float), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemset(h->grid, 0, MN * sizeof(long long));
+    if (e == cudaSuccess) e = cudaMemset(h->counter, 0, sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMemset(h->flags, 0, sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMemset(h->energy_d, 0, sizeof(double));
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) { free_all(h); delete h; return EPB_ECUDA; }
+    *out = h;
+    return EPB_OK;
+}
+
+int epb_destroy(epb_handle* h) {
+    if (!h) return EPB_EINVAL;
+    {
+        DeviceGuard guard(h->dev);
+        cudaDeviceSynchronize();
+        free_all(h);
+    }
+    delete h;
+    return EPB_OK;
+}
+
+const char* epb_last_error(const epb_handle* h) { return h ? h->err.c_str() : "null handle"; }
+
+int epb_geometry(const epb_handle* h, float* bsx, float* bsy, int32_t* bits) {
+    if (!h) return EPB_EINVAL;
+    if (bsx) *bsx = h->bsx;
+    if (bsy) *bsy = h->bsy;
+    if (bits) *bits = h->S;
+    return EPB_OK;
+}
+
+int epb_set_initial_density(epb_handle* h, const float* init_norm, epb_stream stream) {
+    if (!h) return EPB_EINVAL;
+    DeviceGuard guard(h->dev);
+    if (!init_norm) { h->has_init = false; return EPB_OK; }
+    EPB_CUDA(h, cudaMemcpyAsync(h->init, init_norm, (size_t)h->M * h->N * sizeof(float),
+                                cudaMemcpyDeviceToDevice, (cudaStream_t)stream));
+    h->has_init = true;
+    return EPB_OK;
+}
+
+int epb_forward(epb_handle* h, const epb_cells* cells, epb_stream stream, float* density, float* potential,
+                float* field_x, float* field_y, float* energy) {
+    if (!h) return EPB_EINVAL;
+    CellView v;
+    if (int rc = make_view(h, cells, v)) return rc;
+    DeviceGuard guard(h->dev);
+    cudaStream_t st = (cudaStream_t)stream;
+    if (h->grid_dirty) {
+        EPB_CUDA(h, cudaMemsetAsync(h->grid, 0, (size_t)h->M * h->N * sizeof(long long), st));
+        h->grid_dirty = false;
+    }
+    h->grid_dirty = true;  // until the row pass has consumed and re-zeroed it
+    if (int rc = scatter_into(h, v, st, h->grid)) return rc;
+    if (int rc = launch_row_fwd(h, true, nullptr, density, st)) return rc;
+    h->grid_dirty = false;
+    return solve_from_t1(h, st, potential, field_x, field_y, energy);
+}
+
+int epb_backward(epb_handle* h, const epb_cells* cells, const float* grad_out, epb_stream stream,
+                 float* grad_x, float* grad_y) {
+    if (!h) return EPB_EINVAL;
+    if (!h->have_fields) return fail(h, EPB_ENOSTATE, "epb_backward before epb_forward");
+    CellView v;
+    if (int rc = make_view(h, cells, v)) return rc;
+    if (v.n > 0 && (!grad_x || !grad_y)) return fail(h, EPB_EINVAL, "grad_x/grad_y must be non-NULL");
+    if (v.n == 0) return EPB_OK;
+    DeviceGuard guard(h->dev);
+    k_gather<<<cell_blocks(v.n), 256, 0, (cudaStream_t)stream>>>(v, geom(h), h->fxy, nullptr, nullptr, grad_out,
+                                                               grad_x, grad_y, h->flags);
+    EPB_LAUNCHED(h, "k_gather launch");
+    return EPB_OK;
+}
+
+int epb_scatter_fixed(epb_handle* h, const epb_cells* cells, epb_stream stream, int64_t* grid) {
+    if (!h) return EPB_EINVAL;
+    if (!grid) return fail(h, EPB_EINVAL, "grid is NULL");
+    CellView v;
+    if (int rc = make_view(h, cells, v)) return rc;
+    DeviceGuard guard(h->dev);
+    cudaStream_t st = (cudaStream_t)stream;
+    EPB_CUDA(h, cudaMemsetAsync(grid, 0, (size_t)h->M * h->N * sizeof(int64_t), st));
+    return scatter_into(h, v, st, (long long*)grid);
+}
+
+int epb_dct_solve(epb_handle* h, const float* density, epb_stream stream, float* potential, float* field_x,
+                  float* field_y, float* energy) {
+    if (!h) return EPB_EINVAL;
+    if (!density) return fail(h, EPB_EINVAL, "density is NULL");
+    DeviceGuard guard(h->dev);
+    cudaStream_t st = (cudaStream_t)stream;
+    if (int rc = launch_row_fwd(h, false, density, nullptr, st)) return rc;
+    return solve_from_t1(h, st, potential, field_x, field_y, energy);
+}
+
+int epb_gather(epb_handle* h, const epb_cells* cells, const float* field_x, const float* field_y,
+               const float* grad_out, epb_stream stream, float* grad_x, float* grad_y) {
+    if (!h) return EPB_EINVAL;
+    if (!field_x || !field_y) return fail(h, EPB_EINVAL, "field maps must be non-NULL");
+    CellView v;
+    if (int rc = make_view(h, cells, v)) return rc;
+    if (v.n > 0 && (!grad_x || !grad_y)) return fail(h, EPB_EINVAL, "grad_x/grad_y must be non-NULL");
+    if (v.n == 0) return EPB_OK;
+    DeviceGuard guard(h->dev);
+    k_gather<<<cell_blocks(v.n), 256, 0, (cudaStream_t)stream>>>(v, geom(h), nullptr, field_x, field_y, grad_out,
+                                                               grad_x, grad_y, h->flags);
+    EPB_LAUNCHED(h, "k_gather launch");
+    return EPB_OK;
+}
+
+int epb_error_flags(epb_handle* h, epb_stream stream, uint32_t* flags) {
+    if (!h) return EPB_EINVAL;
+    DeviceGuard guard(h->dev);
+    unsigned f = 0;
+    cudaStream_t st = (cudaStream_t)stream;
+    EPB_CUDA(h, cudaMemcpyAsync(&f, h->flags, sizeof(unsigned), cudaMemcpyDeviceToHost, st));
+    EPB_CUDA(h, cudaStreamSynchronize(st));
+    EPB_CUDA(h, cudaMemsetAsync(h->flags, 0, sizeof(unsigned), st));
+    EPB_CUDA(h, cudaStreamSynchronize(st));
+    if (flags) *flags = f;
+    if (f & EPB_FLAG_SATURATED) return fail(h, EPB_EOVERFLOW, "fixed-point density saturated");
+    return EPB_OK;
+}
+
+}  // extern "C"

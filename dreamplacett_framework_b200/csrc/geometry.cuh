@@ -1,0 +1,90 @@
+// geometry.cuh -- per-cell bin footprint and overlap weights shared by the
+// scatter and gather kernels.
+//
+// Every fp32 operation is an explicit round-to-nearest intrinsic so nvcc can
+// not contract a multiply-add into an FMA: the contributions must equal the
+// CPU restatement bit for bit (the fixed-point density is bit-exact).
+//
+// Reference semantics (paths relative to ayadavTT/DREAMPlaceTT-Framework):
+//   bin index  kernels/v4_compute.cpp:85-126  floor((v - origin) * inv_bs),
+//              clamped at 0, corrected so origin + k*bs <= v < origin + (k+1)*bs
+//   overlap    kernels/v4_compute.cpp:128-176 max(0, min(v+s, left+bs) - max(v, left)),
+//              left = origin + k*bs
+#pragma once
+#include <cstdint>
+
+namespace epb {
+
+struct GridGeom {
+    int M, N;                 // bins along x (rows) and y (columns)
+    float xl, yl, bsx, bsy;   // origin and fp32 bin sizes
+    float ibsx, ibsy;         // fp32(1 / bin size)
+};
+
+struct CellView {
+    const float* __restrict__ x;
+    const float* __restrict__ y;
+    const float* __restrict__ sx;
+    const float* __restrict__ sy;
+    const float* __restrict__ ox;   // nullable offsets
+    const float* __restrict__ oy;
+    const float* __restrict__ ratio; // nullable
+    int64_t b0, n0;  // first range: nodes b0 .. b0+n0-1
+    int64_t b1;      // second range starts at node b1
+    int64_t n;       // total cells (n0 + second range length)
+};
+
+__device__ __forceinline__ int64_t cell_node(const CellView& c, int64_t i) {
+    return i < c.n0 ? c.b0 + i : c.b1 + (i - c.n0);
+}
+
+__device__ __forceinline__ int bin_floor(float v, float origin, float bs, float ibs, int nb) {
+    float t = floorf(__fmul_rn(__fsub_rn(v, origin), ibs));
+    if (t < 0.0f) t = 0.0f;
+    if (t > (float)nb) t = (float)nb;
+    int k = (int)t;
+    float bl = __fadd_rn(origin, __fmul_rn((float)k, bs));
+    if (bl > v) k -= 1;
+    bl = __fadd_rn(origin, __fmul_rn((float)(k + 1), bs));
+    if (bl <= v) k += 1;
+    if (k < 0) k = 0;
+    return k;
+}
+
+__device__ __forceinline__ float bin_overlap(float v, float vend, float origin, float bs, int k) {
+    float left = __fadd_rn(origin, __fmul_rn((float)k, bs));
+    float lo = v > left ? v : left;
+    float right = __fadd_rn(left, bs);
+    float hi = vend < right ? vend : right;
+    float o = __fsub_rn(hi, lo);
+    return o < 0.0f ? 0.0f : o;
+}
+
+struct Footprint {
+    float x, y, ex, ey, r;
+    int kx0, kx1, ky0, ky1;
+};
+
+// Returns -1 for a non-finite cell (skipped and flagged), 0 when the cell
+// contributes nothing (non-positive size or off the die), 1 otherwise.
+__device__ __forceinline__ int cell_footprint(const CellView& c, const GridGeom& g, int64_t node,
+                                              Footprint& f) {
+    float x = __ldg(c.x + node), y = __ldg(c.y + node);
+    if (c.ox) x = __fadd_rn(x, __ldg(c.ox + node));
+    if (c.oy) y = __fadd_rn(y, __ldg(c.oy + node));
+    float sx = __ldg(c.sx + node), sy = __ldg(c.sy + node);
+    float r = c.ratio ? __ldg(c.ratio + node) : 1.0f;
+    if (!isfinite(x) || !isfinite(y) || !isfinite(sx) || !isfinite(sy) || !isfinite(r)) return -1;
+    if (!(sx > 0.0f) || !(sy > 0.0f)) return 0;
+    f.ex = __fadd_rn(x, sx);
+    f.ey = __fadd_rn(y, sy);
+    f.kx0 = bin_floor(x, g.xl, g.bsx, g.ibsx, g.M);
+    f.kx1 = min(bin_floor(f.ex, g.xl, g.bsx, g.ibsx, g.M), g.M - 1);
+    f.ky0 = bin_floor(y, g.yl, g.bsy, g.ibsy, g.N);
+    f.ky1 = min(bin_floor(f.ey, g.yl, g.bsy, g.ibsy, g.N), g.N - 1);
+    if (f.kx0 > f.kx1 || f.ky0 > f.ky1) return 0;
+    f.x = x; f.y = y; f.r = r;
+    return 1;
+}
+
+}  // namespace epb

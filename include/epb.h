@@ -1,0 +1,155 @@
+/*
+ * epb.h -- C ABI of the B200 electric-potential engine (libepb200.so).
+ *
+ * One handle owns the device state of one placement grid: fixed-point
+ * density grid, DCT scratch, twiddle tables, the fields of the last forward.
+ * All array pointers passed to these functions are DEVICE pointers on the
+ * handle's device (torch.Tensor.data_ptr() works), caller-owned; the engine
+ * allocates only its internal scratch, at epb_create.  Work is stream-ordered
+ * on the caller's cudaStream_t (0 = legacy default stream); no call blocks the
+ * host except epb_create, epb_destroy and epb_error_flags.  A handle is not
+ * thread-safe: use one handle per host thread / stream.
+ *
+ * Every function returns an epb_status; epb_last_error() gives the message of
+ * the last failure on a handle.
+ *
+ * What each entry point replaces in the reference project
+ * (ayadavTT/DREAMPlaceTT-Framework, paths relative to its root):
+ *   epb_create        host/density_scatter_ttnn_server_host.cpp:324-460 (server argv
+ *                     "M N NC_max ipc_dir xl yl xh yh", sizing) and :1252-1254
+ *                     (TTNNDCTSolver::init); integration/scatter_ttnn_client.py:293-390
+ *                     (ScatterTTNNClient.start).
+ *   epb_destroy       integration/scatter_ttnn_client.py:392-407 (stop: QUIT + wait).
+ *   epb_set_initial_density
+ *                     integration/scatter_ttnn_client.py:786-795 (one-time upload of
+ *                     initial_density_map / bin_area) and the fold at
+ *                     host/density_scatter_ttnn_server_host.cpp:1770-1777.
+ *   epb_forward       integration/scatter_ttnn_client.py:411-509 (ScatterTTNNClient.call)
+ *                     and the server iteration host/density_scatter_ttnn_server_host.cpp:
+ *                     1326-1824 (scatter, accumulate, fold, TTNNDCTSolver::solve :272-305),
+ *                     plus DREAMPlace's potential/energy (returned as 0 by the reference,
+ *                     scatter_ttnn_client.py:860).
+ *   epb_backward      DREAMPlace ElectricPotentialFunction.backward / electric_force
+ *                     (external; reads ctx.field_map_x/y saved at
+ *                     integration/scatter_ttnn_client.py:831-855).
+ *   epb_scatter_fixed the scatter + accumulate programs alone (kernels/v11_scatter_dm.cpp,
+ *                     kernels/v11_accum_dm.cpp; host:1630-1678) with the grid exposed
+ *                     for bit-exact checks (the reference's EXPORT_DENSITY_PATH dump,
+ *                     host:1687-1695).
+ *   epb_dct_solve     TTNNDCTSolver::solve alone (host:272-305), as used by the
+ *                     CPU_DCT=1 diagnostic split (scatter_ttnn_client.py:804-829).
+ *   epb_gather        the gather half of DREAMPlace's backward on given field maps.
+ *   epb_error_flags   the drop counter read-back (host:1633-1659); here it reports
+ *                     skipped non-finite cells and fixed-point saturation instead.
+ */
+#ifndef EPB_H
+#define EPB_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct epb_handle epb_handle;
+
+/* Opaque stream: pass a cudaStream_t (or torch.cuda.Stream.cuda_stream). */
+typedef void* epb_stream;
+
+typedef enum epb_status {
+    EPB_OK = 0,
+    EPB_EINVAL = 1,     /* bad argument (size, null pointer, unsupported grid) */
+    EPB_ECUDA = 2,      /* a CUDA runtime call failed */
+    EPB_ENCCL = 3,      /* reserved for the multi-GPU exchange */
+    EPB_ETIMEOUT = 4,   /* a bounded wait gave up */
+    EPB_EOVERFLOW = 5,  /* fixed-point density saturated (see epb_error_flags) */
+    EPB_ENOSTATE = 6    /* backward called before any forward */
+} epb_status;
+
+/* Bits of the device error word returned by epb_error_flags. */
+#define EPB_FLAG_NONFINITE_CELL 0x1u  /* a cell had a non-finite coordinate/size/ratio; it was skipped */
+#define EPB_FLAG_SATURATED      0x2u  /* a fixed-point bin left [0, 2^62) */
+
+typedef struct epb_config {
+    int32_t num_bins_x;        /* M: bins along x = grid rows (power of two, 16..4096) */
+    int32_t num_bins_y;        /* N: bins along y = grid columns (power of two, 16..4096) */
+    double xl, yl, xh, yh;     /* die box; bin size = fp32((xh-xl)/M), fp32((yh-yl)/N) */
+    int32_t fixed_point_bits;  /* S, fraction bits of the int64 density; <=0 selects
+                                  63 - max(32, ceil(log2(die area)) + 1) */
+    int32_t device;            /* CUDA device ordinal */
+    int32_t flags;             /* reserved, must be 0 */
+    int32_t reserved;
+} epb_config;
+
+/* Cells in DREAMPlace's node layout.  Cell i (0 <= i < n0 + n1, n0 = end0-begin0,
+ * n1 = end1-begin1) is node  i < n0 ? begin0 + i : begin1 + (i - n0).
+ * DREAMPlace orders nodes [movable | fixed terminals | fillers]; the two ranges
+ * select movable and fillers so terminals (already in the initial density) are
+ * skipped, as integration/scatter_ttnn_client.py:611-649 does by concatenation.
+ * The cell box used for binning is [x+offset_x, x+offset_x+size_x) and likewise
+ * in y; its contribution to a bin is (overlap_x * ratio) * overlap_y. */
+typedef struct epb_cells {
+    const float* x;          /* [num nodes] lower-left x (pos[0:num_nodes] in DREAMPlace) */
+    const float* y;          /* [num nodes] lower-left y (pos[num_nodes:2*num_nodes]) */
+    const float* size_x;     /* [num nodes] sizes used for binning (node_size_x_clamped) */
+    const float* size_y;
+    const float* offset_x;   /* nullable [num nodes]: added to x before binning */
+    const float* offset_y;   /* nullable */
+    const float* ratio;      /* nullable [num nodes]: per-node density scale (1 when NULL) */
+    int64_t begin0, end0;    /* first node range */
+    int64_t begin1, end1;    /* second node range; may be empty (begin1 == end1) */
+} epb_cells;
+
+const char* epb_version(void);
+const char* epb_status_string(int status);
+
+int epb_create(const epb_config* cfg, epb_handle** out);
+int epb_destroy(epb_handle* h);
+const char* epb_last_error(const epb_handle* h);
+
+/* Geometry the handle resolved: bin sizes (fp32), fixed-point bits. */
+int epb_geometry(const epb_handle* h, float* bin_size_x, float* bin_size_y, int32_t* fixed_point_bits);
+
+/* Store the normalised fixed-cell density (initial_density_map / bin_area,
+ * fp32 [M*N] device array) that every forward adds to the scattered density.
+ * NULL clears it.  The array is copied (stream-ordered). */
+int epb_set_initial_density(epb_handle* h, const float* init_norm, epb_stream stream);
+
+/* Electric-potential forward: scatter -> normalised density (+ initial
+ * density) -> DCT Poisson solve -> potential, fields, energy.  Output arrays
+ * are nullable [M*N] fp32 device arrays (row-major, index bx*N + by);
+ * energy is a nullable fp32 device scalar.  The fields are also kept inside
+ * the handle for epb_backward. */
+int epb_forward(epb_handle* h, const epb_cells* cells, epb_stream stream,
+                float* density, float* potential, float* field_x, float* field_y,
+                float* energy);
+
+/* Per-cell density gradient from the fields of the last epb_forward:
+ *   grad_x[node] = -g * ratio * sum_bins (overlap_x*overlap_y) * field_x[bin]
+ * with g = *grad_out (device scalar) or 1 when grad_out is NULL.  Only nodes in
+ * the cell ranges are written. */
+int epb_backward(epb_handle* h, const epb_cells* cells, const float* grad_out,
+                 epb_stream stream, float* grad_x, float* grad_y);
+
+/* Scatter only: overwrite grid[M*N] (int64 device array) with the fixed-point
+ * density sum of round_nearest_even(contribution * 2^S). */
+int epb_scatter_fixed(epb_handle* h, const epb_cells* cells, epb_stream stream, int64_t* grid);
+
+/* DCT solve only, from a normalised density map (fp32 [M*N], initial density
+ * NOT added).  Outputs nullable as in epb_forward. */
+int epb_dct_solve(epb_handle* h, const float* density, epb_stream stream,
+                  float* potential, float* field_x, float* field_y, float* energy);
+
+/* Gather only, from caller-supplied field maps. */
+int epb_gather(epb_handle* h, const epb_cells* cells, const float* field_x, const float* field_y,
+               const float* grad_out, epb_stream stream, float* grad_x, float* grad_y);
+
+/* Synchronise the stream, return the accumulated EPB_FLAG_* word and clear
+ * it.  Returns EPB_EOVERFLOW when EPB_FLAG_SATURATED is set. */
+int epb_error_flags(epb_handle* h, epb_stream stream, uint32_t* flags);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EPB_H */
