@@ -1,0 +1,391 @@
+"""Benchmark: electric-potential iterations/sec (scatter + DCT family + gather).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c3] [--impl b200|reference]
+
+One step = one electric-potential forward (density scatter, density map with
+the fixed-macro fold, DCT Poisson solve: potential, field_x, field_y, energy)
+plus the backward (per-cell gradients) over BASELINE config 3 by default:
+1.1M movable cells + 300k fillers + 1000 fixed macros on a 2048 x 2048 grid.
+Inputs are seeded synthetic stand-ins for the ISPD-2005 designs.
+
+Timing: W untimed warm-up steps, then exactly K steps bracketed by a barrier
+and torch.cuda.synchronize() on both sides.  Each step is timed with CUDA
+events on the launching stream and L2 is flushed (a write of twice its size)
+between steps, outside the events.  Multi-GPU runs report the max over ranks.
+
+`--impl reference` times the CPU path instead (the oracle port: OpenMP
+fixed-point density, scipy.fft DCT chain, OpenMP gather) on all host cores,
+rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "electric-potential iters/sec (scatter+DCT+gather) at 1.1M cells, 2048² grid"
+UNIT = "iters/s"
+
+# Algorithmic bytes per launch of each engine stage: every cell array and
+# every grid the stage must touch, counted once (n = scattered cells, B = bins).
+#   scatter : x,y,size_x,size_y,offset_x,offset_y,ratio (28 B/cell) + int64 grid (8 B/bin)
+#   row_fwd : int64 grid read + re-zero (16) + initial density (4) + density out (4) + row DCT out (4)
+#   column  : row DCT in (4) + three column-pass outputs (12)
+#   row_inv : three column-pass maps in (12) + potential, field_x, field_y (12) + interleaved fields (8)
+#   gather  : cell arrays (28 B/cell) + gradient out (8 B/cell) + interleaved fields (8 B/bin)
+STAGE_BYTES = {
+    "scatter": (28, 8),
+    "row_fwd": (0, 28),
+    "column": (0, 16),
+    "row_inv": (0, 32),
+    "gather": (36, 8),
+}
+
+
+def algorithmic_bytes(stage, n_cells, bins):
+    per_cell, per_bin = STAGE_BYTES[stage]
+    return per_cell * n_cells + per_bin * bins
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id):
+        self.gpu_id = gpu_id
+        self.lines = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu_id)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.perf_counter(), line.strip()))
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self, t0, t1):
+        sm, smax, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ts, line in self.lines:
+            if ts < t0 - 0.25 or ts > t1 + 0.25:
+                continue
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def gpu_smi_id(dev):
+    import torch
+    try:
+        p = torch.cuda.get_device_properties(dev)
+        return f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+    except Exception:
+        return dev.index
+
+
+# ----------------------------------------------------------------------------- reference arm
+
+def cpu_step_factory(p, nthreads):
+    """The CPU path of one step on placement p (oracle port)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import build_oracle
+    build_oracle.build_oracle()
+    import oracle as o
+    g = o.Geometry(p.num_bins_x, p.num_bins_y, p.xl, p.yl, p.xh, p.yh)
+    cells = o.Cells(p.x, p.y, p.size_x_clamped, p.size_y_clamped, p.offset_x, p.offset_y, p.ratio,
+                    ranges=p.ranges)
+    S = g.default_fixed_bits()
+    init = p.initial_density_norm()
+    ws = np.empty((nthreads - 1) * g.M * g.N, np.int64) if nthreads > 1 else None
+    gx = np.zeros(p.num_nodes, np.float32)
+    gy = np.zeros(p.num_nodes, np.float32)
+
+    def step():
+        grid, _ = o.density_fixed(cells, g, S, nthreads=nthreads, ws=ws)
+        rho, _ = o.fixed_to_density(grid, g, S, init)
+        sol = o.solve_fft(rho, g.bsx, g.bsy, workers=nthreads, dtype=np.float32)
+        o.gather(cells, g, sol["field_x"], sol["field_y"], 1.0, nthreads=nthreads, grad_x=gx, grad_y=gy)
+        return sol["energy"]
+    return step
+
+
+def cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+def time_cpu(step, max_seconds, max_steps=None, warmup=1):
+    for _ in range(warmup):
+        step()
+    n, t0 = 0, time.perf_counter()
+    while True:
+        step()
+        n += 1
+        el = time.perf_counter() - t0
+        if (max_steps is not None and n >= max_steps) or el >= max_seconds:
+            return n, el
+
+
+def run_reference(args, p):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    nthreads = os.cpu_count() or 1
+    step = cpu_step_factory(p, nthreads)
+    # bounded: at most --ref-seconds of timed CPU work however large K is
+    n, el = time_cpu(step, max_seconds=args.ref_seconds, max_steps=args.steps, warmup=min(args.warmup, 2))
+    value = n / el
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference",
+        "n_gpus": args.gpus, "steps": n, "warmup": min(args.warmup, 2), "ms_per_step": 1000.0 * el / n,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": workload_config(args, p),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": nthreads, "kind": "port",
+                         "sample": f"{n} full steps of {args.steps} requested (capped at {args.ref_seconds:.0f} s); "
+                                   f"oracle port: OpenMP int64 density + scipy.fft fp32 DCT chain + OpenMP gather; "
+                                   f"CPU {cpu_model()}"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- GPU arm
+
+def workload_config(args, p):
+    return {
+        "workload": f"{args.config}: {p.num_movable} movable + {p.num_filler} fillers + {p.num_terminals} fixed macros, "
+                    f"{p.num_bins_x}x{p.num_bins_y} bins, die {p.xh:.0f}^2; forward (density, potential, fields, "
+                    f"energy) + backward (per-cell gradients)",
+        "cells": p.num_cells, "bins": [p.num_bins_x, p.num_bins_y],
+        "density": "int64 fixed point (bit-exact), fp32 DCT/fields",
+        "l2": "flushed between timed steps (write of 2x L2 size)",
+        "parallelism": "single" if args.gpus == 1 else f"replicas{args.gpus}",
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=500)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--config", default="c3")
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
+    ap.add_argument("--ref-seconds", type=float, default=120.0, help="reference arm time cap")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    from dreamplacett_framework_b200 import synth
+    p = synth.make_placement(args.config)
+
+    if args.impl == "reference":
+        run_reference(args, p)
+        return
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from dreamplacett_framework_b200.engine import CellTensors, ElectricPotentialEngine
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    stream = torch.cuda.current_stream(dev)
+    to = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dev)
+    n = p.num_nodes
+    pos = torch.empty(2 * n, dtype=torch.float32, device=dev)
+    pos[:n].copy_(to(p.x))
+    pos[n:].copy_(to(p.y))
+    sx, sy, ox, oy, ratio = (to(a) for a in (p.size_x_clamped, p.size_y_clamped, p.offset_x, p.offset_y, p.ratio))
+    cells = CellTensors(pos[:n], pos[n:], sx, sy, ox, oy, ratio, ranges=p.ranges)
+    eng = ElectricPotentialEngine(p.num_bins_x, p.num_bins_y, p.xl, p.yl, p.xh, p.yh, device=dev)
+    eng.set_initial_density(to(p.initial_density_norm()))
+    M, N = p.num_bins_x, p.num_bins_y
+    outs = {k: torch.empty((M, N), dtype=torch.float32, device=dev)
+            for k in ("density", "potential", "field_x", "field_y")}
+    outs["energy"] = torch.empty(1, dtype=torch.float32, device=dev)
+    grad = torch.zeros(2 * n, dtype=torch.float32, device=dev)
+
+    def step():
+        eng.forward(cells, out=outs)
+        eng.backward(cells, grad_x=grad[:n], grad_y=grad[n:])
+
+    l2 = getattr(torch.cuda.get_device_properties(dev), "L2_cache_size", 126 * 2 ** 20)
+    flush = torch.empty(max(2 * l2, 256 * 2 ** 20) // 4, dtype=torch.float32, device=dev)
+
+    sampler = ClockSampler(gpu_smi_id(dev))
+    sampler.start()
+    time.sleep(0.5)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if eng.error_flags() != 0:
+        raise SystemExit("engine flagged non-finite cells during warm-up")
+
+    K = args.steps
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    eng.profile_start(K)
+    barrier()
+    torch.cuda.synchronize(dev)
+    t_wall0 = time.perf_counter()
+    for i in range(K):
+        flush.zero_()
+        ev[i][0].record(stream)
+        step()
+        ev[i][1].record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    t_wall1 = time.perf_counter()
+    stages = eng.profile_stop()
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    total_ms = sum(step_ms)
+    clocks = sampler.summary(t_wall0, t_wall1)
+
+    # --- end to end through the engine API with host buffers (pos in, grad + energy out)
+    pos_host = torch.empty(2 * n, dtype=torch.float32).pin_memory()
+    pos_host.copy_(pos.cpu())
+    grad_host = torch.empty(2 * n, dtype=torch.float32).pin_memory()
+    energy_host = torch.empty(1, dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        pos.copy_(pos_host, non_blocking=True)
+        step()
+        grad_host.copy_(grad, non_blocking=True)
+        energy_host.copy_(outs["energy"], non_blocking=True)
+
+    K_e2e = max(10, min(K, 200))
+    for _ in range(args.warmup):
+        e2e_step()
+    ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K_e2e)]
+    barrier()
+    torch.cuda.synchronize(dev)
+    for i in range(K_e2e):
+        ev2[i][0].record(stream)
+        e2e_step()
+        ev2[i][1].record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_ms = sum(a.elapsed_time(b) for a, b in ev2)
+    sampler.stop()
+    flags = eng.error_flags()
+
+    # --- max over ranks
+    vals = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    total_ms, e2e_ms = float(vals[0]), float(vals[1])
+
+    if rank == 0:
+        peak, peak_kind = load_peaks()
+        bins = M * N
+        kern = {}
+        for name, (ms, cnt) in stages.items():
+            if cnt == 0:
+                continue
+            avg_s = ms / cnt / 1000.0
+            b = algorithmic_bytes(name, p.num_cells, bins)
+            kern[name] = {"avg_us": avg_s * 1e6, "launches": cnt, "bytes": b,
+                          "gbs": b / avg_s / 1e9, "frac": b / avg_s / 1e9 / peak}
+        dom = max(kern, key=lambda k: kern[k]["avg_us"])
+        roof = {"bound": "hbm", "kernel": dom, "achieved": kern[dom]["gbs"], "peak": peak, "unit": "GB/s",
+                "frac": kern[dom]["frac"], "traffic": None, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"}
+        step_bytes = sum(algorithmic_bytes(k, p.num_cells, bins) for k in STAGE_BYTES)
+        value = world * K / (total_ms / 1000.0)
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": args.warmup,
+            "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (seeded stand-in for ISPD-2005 shapes)",
+            "config": workload_config(args, p),
+            "roofline": roof,
+            "kernels": kern,
+            "step_algorithmic_bytes": step_bytes,
+            "step_gbs": step_bytes / (total_ms / K / 1000.0) / 1e9,
+            "e2e": {"value": world * K_e2e / (e2e_ms / 1000.0), "unit": UNIT, "steps": K_e2e,
+                    "h2d_bytes_per_step": 2 * n * 4, "d2h_bytes_per_step": 2 * n * 4 + 4,
+                    "path": "engine API: pinned pos[2n] H2D, forward+backward, grad[2n] + energy D2H"},
+            "gpu_launches": 5 * K,
+            "clocks": clocks,
+            "error_flags": flags,
+            "wall_s_timed_region": t_wall1 - t_wall0,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            nthreads = os.cpu_count() or 1
+            cstep = cpu_step_factory(p, nthreads)
+            cn, cel = time_cpu(cstep, max_seconds=args.cpu_seconds, warmup=1)
+            line["cpu_baseline"] = {
+                "value": cn / cel, "unit": UNIT, "cores": nthreads, "kind": "port",
+                "sample": f"{cn} full {args.config} steps in {cel:.1f} s (oracle port: OpenMP int64 density, "
+                          f"scipy.fft fp32 DCT chain, OpenMP gather), CPU {cpu_model()}"}
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

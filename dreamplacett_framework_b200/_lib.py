@@ -26,7 +26,11 @@ EXPORTS = (
     "epb_version", "epb_status_string", "epb_create", "epb_destroy", "epb_last_error",
     "epb_geometry", "epb_set_initial_density", "epb_forward", "epb_backward",
     "epb_scatter_fixed", "epb_dct_solve", "epb_gather", "epb_error_flags",
+    "epb_profile_start", "epb_profile_stop",
 )
+
+# Stage indices of epb_profile_stop (EPB_STAGE_* in include/epb.h).
+STAGES = ("scatter", "row_fwd", "column", "row_inv", "gather")
 
 
 class EpbConfig(ctypes.Structure):
@@ -87,6 +91,8 @@ def load():
     L.epb_dct_solve.argtypes = [vp, vp, vp, vp, vp, vp, vp]
     L.epb_gather.argtypes = [vp, cp, vp, vp, vp, vp, vp, vp]
     L.epb_error_flags.argtypes = [vp, vp, ctypes.POINTER(ctypes.c_uint32)]
+    L.epb_profile_start.argtypes = [vp, i32]
+    L.epb_profile_stop.argtypes = [vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(i32)]
     for name in EXPORTS:
         if name not in ("epb_version", "epb_status_string", "epb_last_error"):
             getattr(L, name).restype = ctypes.c_int

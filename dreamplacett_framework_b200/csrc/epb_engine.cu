@@ -41,6 +41,13 @@ struct epb_handle {
     unsigned* counter = nullptr;
     double* energy_d = nullptr;
     unsigned* flags = nullptr;
+    // stage timing (epb_profile_start/stop)
+    struct Span { int stage, a, b; };
+    bool prof_on = false;
+    int prof_calls_left = 0;
+    std::vector<cudaEvent_t> prof_events;
+    int prof_used = 0;
+    std::vector<Span> prof_spans;
     std::string err;
 };
 
@@ -135,6 +142,8 @@ void free_all(epb_handle* h) {
                     h->twN, h->qwN, h->wu, h->wv, h->partials, h->counter, h->energy_d, h->flags};
     for (void* p : ptrs)
         if (p) cudaFree(p);
+    for (cudaEvent_t e : h->prof_events) cudaEventDestroy(e);
+    h->prof_events.clear();
 }
 
 // ----- kernel dispatch on the transform length -----
@@ -235,9 +244,33 @@ int col_blocks(int M, int N) {
     return (N + W - 1) / W;
 }
 
+// Profiling: a mark is an event recorded on the stream between two kernels.
+struct ProfCall {
+    epb_handle* h;
+    cudaStream_t st;
+    bool on;
+    int last = -1;
+    ProfCall(epb_handle* h_, cudaStream_t s) : h(h_), st(s) {
+        on = h->prof_on && h->prof_calls_left > 0;
+        if (on) h->prof_calls_left--;
+    }
+    int mark() {
+        if (!on || h->prof_used >= (int)h->prof_events.size()) return -1;
+        const int i = h->prof_used++;
+        if (cudaEventRecord(h->prof_events[i], st) != cudaSuccess) return -1;
+        return i;
+    }
+    void begin() { last = mark(); }
+    void end_stage(int stage) {
+        const int m = mark();
+        if (last >= 0 && m >= 0) h->prof_spans.push_back({stage, last, m});
+        last = m;
+    }
+};
+
 // DCT solve from the state in t1 (after the row-forward pass).
 int solve_from_t1(epb_handle* h, cudaStream_t st, float* potential, float* field_x, float* field_y,
-                  float* energy) {
+                  float* energy, ProfCall& pc) {
     ColArgs ca;
     ca.t1 = h->t1; ca.gx = h->gx; ca.gy = h->gy; ca.gp = h->gp;
     ca.wu = h->wu; ca.wv = h->wv; ca.tw = h->twM; ca.qw = h->qwM;
@@ -245,11 +278,13 @@ int solve_from_t1(epb_handle* h, cudaStream_t st, float* potential, float* field
     ca.energy_out = energy; ca.N = h->N; ca.want_phi = potential != nullptr;
     ca.energy_scale = (double)h->M * (double)h->N / 4.0;
     if (int rc = launch_col(h, ca, st)) return rc;
+    pc.end_stage(EPB_STAGE_COLUMN);
     RowInvArgs ra;
     ra.gx = h->gx; ra.gy = h->gy; ra.gp = h->gp;
     ra.fx = field_x; ra.fy = field_y; ra.phi = potential; ra.fxy = h->fxy;
     ra.tw = h->twN; ra.qw = h->qwN; ra.M = h->M; ra.want_phi = potential != nullptr;
     if (int rc = launch_row_inv(h, ra, st)) return rc;
+    pc.end_stage(EPB_STAGE_ROW_INV);
     h->have_fields = true;
     return EPB_OK;
 }
@@ -401,10 +436,14 @@ int epb_forward(epb_handle* h, const epb_cells* cells, epb_stream stream, float*
         h->grid_dirty = false;
     }
     h->grid_dirty = true;  // until the row pass has consumed and re-zeroed it
+    ProfCall pc(h, st);
+    pc.begin();
     if (int rc = scatter_into(h, v, st, h->grid)) return rc;
+    pc.end_stage(EPB_STAGE_SCATTER);
     if (int rc = launch_row_fwd(h, true, nullptr, density, st)) return rc;
+    pc.end_stage(EPB_STAGE_ROW_FWD);
     h->grid_dirty = false;
-    return solve_from_t1(h, st, potential, field_x, field_y, energy);
+    return solve_from_t1(h, st, potential, field_x, field_y, energy, pc);
 }
 
 int epb_backward(epb_handle* h, const epb_cells* cells, const float* grad_out, epb_stream stream,
@@ -416,9 +455,12 @@ int epb_backward(epb_handle* h, const epb_cells* cells, const float* grad_out, e
     if (v.n > 0 && (!grad_x || !grad_y)) return fail(h, EPB_EINVAL, "grad_x/grad_y must be non-NULL");
     if (v.n == 0) return EPB_OK;
     DeviceGuard guard(h->dev);
+    ProfCall pc(h, (cudaStream_t)stream);
+    pc.begin();
     k_gather<<<cell_blocks(v.n), 256, 0, (cudaStream_t)stream>>>(v, geom(h), h->fxy, nullptr, nullptr, grad_out,
                                                                grad_x, grad_y, h->flags);
     EPB_LAUNCHED(h, "k_gather launch");
+    pc.end_stage(EPB_STAGE_GATHER);
     return EPB_OK;
 }
 
@@ -430,7 +472,11 @@ int epb_scatter_fixed(epb_handle* h, const epb_cells* cells, epb_stream stream, 
     DeviceGuard guard(h->dev);
     cudaStream_t st = (cudaStream_t)stream;
     EPB_CUDA(h, cudaMemsetAsync(grid, 0, (size_t)h->M * h->N * sizeof(int64_t), st));
-    return scatter_into(h, v, st, (long long*)grid);
+    ProfCall pc(h, st);
+    pc.begin();
+    if (int rc = scatter_into(h, v, st, (long long*)grid)) return rc;
+    pc.end_stage(EPB_STAGE_SCATTER);
+    return EPB_OK;
 }
 
 int epb_dct_solve(epb_handle* h, const float* density, epb_stream stream, float* potential, float* field_x,
@@ -439,8 +485,11 @@ int epb_dct_solve(epb_handle* h, const float* density, epb_stream stream, float*
     if (!density) return fail(h, EPB_EINVAL, "density is NULL");
     DeviceGuard guard(h->dev);
     cudaStream_t st = (cudaStream_t)stream;
+    ProfCall pc(h, st);
+    pc.begin();
     if (int rc = launch_row_fwd(h, false, density, nullptr, st)) return rc;
-    return solve_from_t1(h, st, potential, field_x, field_y, energy);
+    pc.end_stage(EPB_STAGE_ROW_FWD);
+    return solve_from_t1(h, st, potential, field_x, field_y, energy, pc);
 }
 
 int epb_gather(epb_handle* h, const epb_cells* cells, const float* field_x, const float* field_y,
@@ -470,6 +519,60 @@ int epb_error_flags(epb_handle* h, epb_stream stream, uint32_t* flags) {
     if (flags) *flags = f;
     if (f & EPB_FLAG_SATURATED) return fail(h, EPB_EOVERFLOW, "fixed-point density saturated");
     return EPB_OK;
+}
+
+int epb_profile_start(epb_handle* h, int32_t max_calls) {
+    if (!h) return EPB_EINVAL;
+    if (max_calls < 1 || max_calls > 200000) return fail(h, EPB_EINVAL, "max_calls must be in [1, 200000]");
+    DeviceGuard guard(h->dev);
+    for (cudaEvent_t e : h->prof_events) cudaEventDestroy(e);
+    h->prof_events.clear();
+    h->prof_spans.clear();
+    h->prof_used = 0;
+    const size_t n = (size_t)max_calls * 5;
+    h->prof_events.resize(n);
+    for (size_t i = 0; i < n; ++i) {
+        cudaError_t e = cudaEventCreate(&h->prof_events[i]);
+        if (e != cudaSuccess) {
+            for (size_t j = 0; j < i; ++j) cudaEventDestroy(h->prof_events[j]);
+            h->prof_events.clear();
+            return cuda_fail(h, e, "cudaEventCreate");
+        }
+    }
+    h->prof_calls_left = max_calls;
+    h->prof_on = true;
+    return EPB_OK;
+}
+
+int epb_profile_stop(epb_handle* h, double* stage_ms, int32_t* stage_launches) {
+    if (!h) return EPB_EINVAL;
+    DeviceGuard guard(h->dev);
+    double ms[EPB_NUM_STAGES] = {0};
+    int32_t cnt[EPB_NUM_STAGES] = {0};
+    int rc = EPB_OK;
+    if (h->prof_used > 0) {
+        cudaError_t e = cudaEventSynchronize(h->prof_events[h->prof_used - 1]);
+        if (e != cudaSuccess) rc = cuda_fail(h, e, "cudaEventSynchronize");
+    }
+    for (const auto& sp : h->prof_spans) {
+        if (rc) break;
+        float t = 0.f;
+        cudaError_t e = cudaEventElapsedTime(&t, h->prof_events[sp.a], h->prof_events[sp.b]);
+        if (e != cudaSuccess) { rc = cuda_fail(h, e, "cudaEventElapsedTime"); break; }
+        ms[sp.stage] += t;
+        cnt[sp.stage] += 1;
+    }
+    for (cudaEvent_t e : h->prof_events) cudaEventDestroy(e);
+    h->prof_events.clear();
+    h->prof_spans.clear();
+    h->prof_used = 0;
+    h->prof_on = false;
+    h->prof_calls_left = 0;
+    for (int i = 0; i < EPB_NUM_STAGES; ++i) {
+        if (stage_ms) stage_ms[i] = ms[i];
+        if (stage_launches) stage_launches[i] = cnt[i];
+    }
+    return rc;
 }
 
 }  // extern "C"

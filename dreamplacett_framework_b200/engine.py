@@ -226,6 +226,18 @@ class ElectricPotentialEngine:
         _lib.check(self._h, st)
         return grad_x, grad_y
 
+    def profile_start(self, max_calls: int):
+        """Record CUDA events between this engine's kernels for the next
+        max_calls forward/backward calls (no host synchronisation)."""
+        _lib.check(self._h, self.lib.epb_profile_start(self._h, int(max_calls)))
+
+    def profile_stop(self) -> dict:
+        """{stage: (total_ms, launches)} for the calls timed since profile_start."""
+        ms = (ctypes.c_double * len(_lib.STAGES))()
+        cnt = (ctypes.c_int32 * len(_lib.STAGES))()
+        _lib.check(self._h, self.lib.epb_profile_stop(self._h, ms, cnt))
+        return {name: (float(ms[i]), int(cnt[i])) for i, name in enumerate(_lib.STAGES)}
+
     def error_flags(self, stream=None) -> int:
         """Synchronises; returns and clears EPB_FLAG_* bits.  Raises EpbError
         with EPB_EOVERFLOW when the fixed-point grid saturated."""

@@ -41,6 +41,10 @@
  *   epb_gather        the gather half of DREAMPlace's backward on given field maps.
  *   epb_error_flags   the drop counter read-back (host:1633-1659); here it reports
  *                     skipped non-finite cells and fixed-point saturation instead.
+ *   epb_profile_start / epb_profile_stop
+ *                     the server's per-stage hrclock spans written to the shm header
+ *                     (host:1343-1812, timing keys at integration/scatter_ttnn_client.py:492-507),
+ *                     here as CUDA events on the caller's stream around each kernel.
  */
 #ifndef EPB_H
 #define EPB_H
@@ -147,6 +151,21 @@ int epb_gather(epb_handle* h, const epb_cells* cells, const float* field_x, cons
 /* Synchronise the stream, return the accumulated EPB_FLAG_* word and clear
  * it.  Returns EPB_EOVERFLOW when EPB_FLAG_SATURATED is set. */
 int epb_error_flags(epb_handle* h, epb_stream stream, uint32_t* flags);
+
+/* Stage timing.  Stages, in launch order: */
+#define EPB_STAGE_SCATTER   0  /* cells -> fixed-point grid                          */
+#define EPB_STAGE_ROW_FWD   1  /* grid -> density (+ initial density) -> row DCT-II  */
+#define EPB_STAGE_COLUMN    2  /* column DCT-II, spectral weights, column inverses   */
+#define EPB_STAGE_ROW_INV   3  /* row inverses -> potential, fields                  */
+#define EPB_STAGE_GATHER    4  /* fields -> per-cell gradient                        */
+#define EPB_NUM_STAGES      5
+/* After epb_profile_start, the next max_calls forward/backward calls record a
+ * CUDA event between consecutive kernels on the caller's stream (no host
+ * synchronisation).  epb_profile_stop synchronises on those events and
+ * returns, per stage, the summed milliseconds and the number of launches
+ * timed; it releases the events.  Calls beyond max_calls are not timed. */
+int epb_profile_start(epb_handle* h, int32_t max_calls);
+int epb_profile_stop(epb_handle* h, double* stage_ms, int32_t* stage_launches);
 
 #ifdef __cplusplus
 }
