@@ -36,7 +36,6 @@ struct epb_handle {
     float2* fxy = nullptr;      // interleaved fields of the last forward
     bool have_fields = false;
     float2 *twM = nullptr, *qwM = nullptr, *twN = nullptr, *qwN = nullptr;
-    float *wu = nullptr, *wv = nullptr;
     double* partials = nullptr;
     unsigned* counter = nullptr;
     double* energy_d = nullptr;
@@ -139,7 +138,7 @@ int dev_alloc(epb_handle* h, T** p, size_t count) {
 
 void free_all(epb_handle* h) {
     void* ptrs[] = {h->grid, h->init, h->t1, h->gx, h->gy, h->gp, h->fxy, h->twM, h->qwM,
-                    h->twN, h->qwN, h->wu, h->wv, h->partials, h->counter, h->energy_d, h->flags};
+                    h->twN, h->qwN, h->partials, h->counter, h->energy_d, h->flags};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     for (cudaEvent_t e : h->prof_events) cudaEventDestroy(e);
@@ -162,12 +161,12 @@ int launch_row_fwd_t(epb_handle* h, bool from_fixed, const float* rho_in, float*
     if (from_fixed) {
         auto fn = k_row_fwd<L, true>;
         if (int rc = set_smem<L>(h, (const void*)fn, C::SMEM)) return rc;
-        fn<<<blocks, kFftThreads, C::SMEM, st>>>(h->grid, nullptr, init, h->dscale, h->M, rho_out, h->t1,
+        fn<<<blocks, C::T, C::SMEM, st>>>(h->grid, nullptr, init, h->dscale, h->M, rho_out, h->t1,
                                                 h->twN, h->qwN, h->flags);
     } else {
         auto fn = k_row_fwd<L, false>;
         if (int rc = set_smem<L>(h, (const void*)fn, C::SMEM)) return rc;
-        fn<<<blocks, kFftThreads, C::SMEM, st>>>(nullptr, rho_in, nullptr, h->dscale, h->M, rho_out, h->t1,
+        fn<<<blocks, C::T, C::SMEM, st>>>(nullptr, rho_in, nullptr, h->dscale, h->M, rho_out, h->t1,
                                                 h->twN, h->qwN, h->flags);
     }
     EPB_LAUNCHED(h, "k_row_fwd launch");
@@ -180,7 +179,7 @@ int launch_col_t(epb_handle* h, const ColArgs& a, cudaStream_t st) {
     const unsigned blocks = (unsigned)((h->N + C::W - 1) / C::W);
     auto fn = k_col<L>;
     if (int rc = set_smem<L>(h, (const void*)fn, C::SMEM)) return rc;
-    fn<<<blocks, kFftThreads, C::SMEM, st>>>(a);
+    fn<<<blocks, C::T, C::SMEM, st>>>(a);
     EPB_LAUNCHED(h, "k_col launch");
     return EPB_OK;
 }
@@ -191,7 +190,7 @@ int launch_row_inv_t(epb_handle* h, const RowInvArgs& a, cudaStream_t st) {
     const unsigned blocks = (unsigned)((h->M + C::ROWS - 1) / C::ROWS);
     auto fn = k_row_inv<L>;
     if (int rc = set_smem<L>(h, (const void*)fn, C::SMEM)) return rc;
-    fn<<<blocks, kFftThreads, C::SMEM, st>>>(a);
+    fn<<<blocks, C::T, C::SMEM, st>>>(a);
     EPB_LAUNCHED(h, "k_row_inv launch");
     return EPB_OK;
 }
@@ -273,7 +272,9 @@ int solve_from_t1(epb_handle* h, cudaStream_t st, float* potential, float* field
                   float* energy, ProfCall& pc) {
     ColArgs ca;
     ca.t1 = h->t1; ca.gx = h->gx; ca.gy = h->gy; ca.gp = h->gp;
-    ca.wu = h->wu; ca.wv = h->wv; ca.tw = h->twM; ca.qw = h->qwM;
+    ca.ku = (float)(2.0 * M_PI / h->M);
+    ca.kv = (float)(2.0 * M_PI / h->N * (double)(h->bsx / h->bsy));
+    ca.tw = h->twM; ca.qw = h->qwM;
     ca.partials = h->partials; ca.counter = h->counter; ca.energy_d = h->energy_d;
     ca.energy_out = energy; ca.N = h->N; ca.want_phi = potential != nullptr;
     ca.energy_scale = (double)h->M * (double)h->N / 4.0;
@@ -358,8 +359,6 @@ int epb_create(const epb_config* cfg, epb_handle** out) {
     if (!rc) rc = dev_alloc(h, &h->qwM, (size_t)h->M);
     if (!rc) rc = dev_alloc(h, &h->twN, (size_t)h->N);
     if (!rc) rc = dev_alloc(h, &h->qwN, (size_t)h->N);
-    if (!rc) rc = dev_alloc(h, &h->wu, (size_t)h->M);
-    if (!rc) rc = dev_alloc(h, &h->wv, (size_t)h->N);
     if (!rc) rc = dev_alloc(h, &h->partials, (size_t)ncolb);
     if (!rc) rc = dev_alloc(h, &h->counter, 1);
     if (!rc) rc = dev_alloc(h, &h->energy_d, 1);
@@ -367,7 +366,6 @@ int epb_create(const epb_config* cfg, epb_handle** out) {
     if (rc) { free_all(h); delete h; return rc; }
 
     std::vector<float2> tw, qw;
-    std::vector<float> w;
     cudaError_t e = cudaSuccess;
     host_tables(h->M, tw, qw);
     if (e == cudaSuccess) e = cudaMemcpy(h->twM, tw.data(), tw.size() * sizeof(float2), cudaMemcpyHostToDevice);
@@ -375,14 +373,6 @@ int epb_create(const epb_config* cfg, epb_handle** out) {
     host_tables(h->N, tw, qw);
     if (e == cudaSuccess) e = cudaMemcpy(h->twN, tw.data(), tw.size() * sizeof(float2), cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemcpy(h->qwN, qw.data(), qw.size() * sizeof(float2), cudaMemcpyHostToDevice);
-    // wu = 2 pi u / M ; wv = 2 pi v / N * (bsx / bsy)   (host:254-256)
-    w.resize(h->M);
-    for (int u = 0; u < h->M; ++u) w[u] = (float)(2.0 * M_PI * u / h->M);
-    if (e == cudaSuccess) e = cudaMemcpy(h->wu, w.data(), w.size() * sizeof(float), cudaMemcpyHostToDevice);
-    w.resize(h->N);
-    const double asp = (double)(h->bsx / h->bsy);
-    for (int v = 0; v < h->N; ++v) w[v] = (float)(2.0 * M_PI * v / h->N * asp);
-    if (e == cudaSuccess) e = cudaMemcpy(h->wv, w.data(), w.size() * sizeof(float), cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemset(h->grid, 0, MN * sizeof(long long));
     if (e == cudaSuccess) e = cudaMemset(h->counter, 0, sizeof(unsigned));
     if (e == cudaSuccess) e = cudaMemset(h->flags, 0, sizeof(unsigned));

@@ -29,7 +29,6 @@
 
 namespace epb {
 
-constexpr int kFftThreads = 256;
 constexpr unsigned kFlagNonFinite = 0x1u;
 constexpr unsigned kFlagSaturated = 0x2u;
 
@@ -60,17 +59,21 @@ k_scatter(CellView c, GridGeom g, float qscale, unsigned long long* __restrict__
 
 // ---------------------------------------------------------------------------
 // Pass 1: conversion + forward DCT along y (rows)
-// S sequences of length L = N per CTA -> 2S rows.
+// S sequences of length L = N per CTA (two rows packed per sequence), P = L/16
+// threads per sequence.
 // ---------------------------------------------------------------------------
 template <int L>
 struct RowFwdCfg {
+    static constexpr int P = L / 16;
     static constexpr int S = (4096 / L) > 0 ? 4096 / L : 1;
+    static constexpr int T = P * S;
     static constexpr int ROWS = 2 * S;
-    static constexpr size_t SMEM = (size_t)S * L * sizeof(float2);
+    static constexpr int LP = Padded<L>::value;
+    static constexpr size_t SMEM = (size_t)S * LP * sizeof(float2);
 };
 
 template <int L, bool FROM_FIXED>
-__global__ void __launch_bounds__(kFftThreads)
+__global__ void __launch_bounds__(RowFwdCfg<L>::T)
 k_row_fwd(long long* __restrict__ qgrid,            // FROM_FIXED: [M][L] int64 (zeroed after read)
           const float* __restrict__ rho_in,         // !FROM_FIXED: [M][L] fp32
           const float* __restrict__ init,           // nullable [M][L]
@@ -80,12 +83,13 @@ k_row_fwd(long long* __restrict__ qgrid,            // FROM_FIXED: [M][L] int64 
           const float2* __restrict__ tw, const float2* __restrict__ qw,
           unsigned* __restrict__ flags) {
     using C = RowFwdCfg<L>;
-    constexpr int S = C::S, T = kFftThreads;
+    constexpr int S = C::S, T = C::T, LP = C::LP;
     extern __shared__ float2 sm_rowfwd[];
     float2* buf = sm_rowfwd;
     const int row0 = blockIdx.x * C::ROWS;
     unsigned sat = 0;
-    // load: element m of row (row0 + 2s + p) goes to buf[s][makhoul_pos(m)], real (p=0) or imag (p=1)
+    // element m of row (row0 + 2s + p) goes to sequence s at makhoul_pos(m), real (p=0) or imag (p=1)
+#pragma unroll 4
     for (int e = threadIdx.x; e < S * L; e += T) {
         const int s = e / L, m = e % L;
         float vals[2];
@@ -96,8 +100,8 @@ k_row_fwd(long long* __restrict__ qgrid,            // FROM_FIXED: [M][L] int64 
             if (row < M) {
                 const int64_t off = (int64_t)row * L + m;
                 if (FROM_FIXED) {
-                    long long q = qgrid[off];
-                    qgrid[off] = 0;  // leave the grid zeroed for the next scatter
+                    const long long q = __ldcs(qgrid + off);
+                    __stcs(qgrid + off, 0ll);  // leave the grid zeroed for the next scatter
                     if (q < 0 || q >= (1ll << 62)) sat = 1;
                     v = __double2float_rn(__dmul_rn(__ll2double_rn(q), dscale));
                     if (init) v = __fadd_rn(v, __ldg(init + off));
@@ -108,16 +112,17 @@ k_row_fwd(long long* __restrict__ qgrid,            // FROM_FIXED: [M][L] int64 
             }
             vals[p] = v;
         }
-        buf[s * L + makhoul_pos(m, L)] = make_float2(vals[0], vals[1]);
+        buf[s * LP + pidx(makhoul_pos(m, L))] = make_float2(vals[0], vals[1]);
     }
     if (FROM_FIXED && sat) atomicOr(flags, kFlagSaturated);
     __syncthreads();
-    fft_smem<L, S, T, false>(buf, tw);
+    fft_seq<L, false>(buf + (threadIdx.x / C::P) * LP, threadIdx.x % C::P, tw);
     const float scale = 2.0f / (float)L;
+#pragma unroll 4
     for (int e = threadIdx.x; e < S * L; e += T) {
         const int s = e / L, k = e % L;
-        const float2 Z = buf[s * L + k];
-        const float2 Zr = buf[s * L + ((L - k) & (L - 1))];
+        const float2 Z = buf[s * LP + pidx(k)];
+        const float2 Zr = buf[s * LP + pidx((L - k) & (L - 1))];
         // Va = (Z + conj(Zr))/2 ; Vb = -i (Z - conj(Zr))/2
         const float2 Va = make_float2(0.5f * (Z.x + Zr.x), 0.5f * (Z.y - Zr.y));
         const float2 Vb = make_float2(0.5f * (Z.y + Zr.y), -0.5f * (Z.x - Zr.x));
@@ -133,9 +138,12 @@ k_row_fwd(long long* __restrict__ qgrid,            // FROM_FIXED: [M][L] int64 
 // ---------------------------------------------------------------------------
 template <int L>
 struct ColCfg {
+    static constexpr int P = L / 16;
     static constexpr int S = (4096 / L) > 2 ? 4096 / L : 2;
+    static constexpr int T = P * S;
     static constexpr int W = 2 * S;
-    static constexpr size_t SMEM = (size_t)S * L * sizeof(float2) + (size_t)W * L * sizeof(float);
+    static constexpr int LP = Padded<L>::value;
+    static constexpr size_t SMEM = (size_t)S * LP * sizeof(float2) + (size_t)W * L * sizeof(float);
 };
 
 struct ColArgs {
@@ -143,8 +151,8 @@ struct ColArgs {
     float* gx;              // [M][N] (2 IDXST_M)(auv*wu)
     float* gy;              // [M][N] (2 IDCT_M)(auv*wv)
     float* gp;              // [M][N] IDCT_M(auv*inv)   (only when want_phi)
-    const float* wu;        // [M] 2 pi u / M
-    const float* wv;        // [N] 2 pi v / N * bsx/bsy
+    float ku;               // wu = u * ku,  ku = 2 pi / M
+    float kv;               // wv = v * kv,  kv = 2 pi / N * bsx / bsy
     const float2* tw;       // FFT twiddles, length M
     const float2* qw;       // quarter-wave table, length M
     double* partials;       // [gridDim.x] energy partial sums
@@ -156,46 +164,68 @@ struct ColArgs {
     double energy_scale;    // M*N/4
 };
 
+// Eigenvalue weights (host/density_scatter_ttnn_server_host.cpp:252-263 and
+// DREAMPlace's inv_wu2_plus_wv2): inv = 1/(wu^2+wv^2), wuh = wu*inv/2,
+// wvh = wv*inv/2, all zero at (0, 0).
 __device__ __forceinline__ void spectral_weights(float wu, float wv, float& wuh, float& wvh, float& inv) {
     const float d = wu * wu + wv * wv;
-    if (d == 0.0f) { wuh = wvh = inv = 0.0f; return; }
-    inv = 1.0f / d;
+    inv = d == 0.0f ? 0.0f : __frcp_rn(d);
     wuh = wu * inv * 0.5f;
     wvh = wv * inv * 0.5f;
 }
 
+// Spectral input of the three column inverses for one column at row index u:
+// r = 0: b_u = a_{L-u} (IDXST via IDCT), a = auv * wu_half   (the caller mirrors)
+// r = 1: 2 * auv * wv_half
+// r = 2: auv * inv
+__device__ __forceinline__ float col_weight(int r, float wu, float wv) {
+    float wuh, wvh, inv;
+    spectral_weights(wu, wv, wuh, wvh, inv);
+    return r == 0 ? wuh : (r == 1 ? 2.0f * wvh : inv);
+}
+
+// V_n = (A_n - i A_{L-n}) e^{i pi n / 2L} of two packed real sequences (p=0 real, p=1 imaginary)
+__device__ __forceinline__ float2 idct_pre(float an0, float am0, float an1, float am1, float2 q) {
+    const float2 va = make_float2(an0 * q.x + am0 * q.y, an0 * q.y - am0 * q.x);
+    const float2 vb = make_float2(an1 * q.x + am1 * q.y, an1 * q.y - am1 * q.x);
+    return make_float2(va.x - vb.y, va.y + vb.x);
+}
+
 template <int L>
-__global__ void __launch_bounds__(kFftThreads)
+__global__ void __launch_bounds__(ColCfg<L>::T)
 k_col(ColArgs a) {
     using C = ColCfg<L>;
-    constexpr int S = C::S, W = C::W, T = kFftThreads;
+    constexpr int S = C::S, W = C::W, T = C::T, LP = C::LP;
     extern __shared__ float2 sm_col[];
-    float2* buf = sm_col;                                  // S x L complex
-    float* auv = reinterpret_cast<float*>(sm_col + S * L); // W x L real (column-major per column)
+    float2* buf = sm_col;                                   // S x LP complex
+    float* auv = reinterpret_cast<float*>(sm_col + S * LP); // W x L real (one column after another)
     const int N = a.N;
     const int c0 = blockIdx.x * W;
+    float2* myseq = buf + (threadIdx.x / C::P) * LP;
+    const int lane = threadIdx.x % C::P;
 
     // ---- load T1 strip [L rows][W cols], Makhoul reorder along rows ----
+#pragma unroll 4
     for (int e = threadIdx.x; e < L * (W / 4); e += T) {
         const int m = e / (W / 4), q4 = e % (W / 4);
         const int col = c0 + 4 * q4;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         if (col < N) v = __ldg(reinterpret_cast<const float4*>(a.t1 + (int64_t)m * N + col));
-        const int pos = makhoul_pos(m, L);
+        const int pos = pidx(makhoul_pos(m, L));
         const int s0 = 2 * q4;  // columns 4q4, 4q4+1 -> seq 2q4 ; 4q4+2, 4q4+3 -> seq 2q4+1
-        buf[s0 * L + pos] = make_float2(v.x, v.y);
-        buf[(s0 + 1) * L + pos] = make_float2(v.z, v.w);
+        buf[s0 * LP + pos] = make_float2(v.x, v.y);
+        buf[(s0 + 1) * LP + pos] = make_float2(v.z, v.w);
     }
     __syncthreads();
-    fft_smem<L, S, T, false>(buf, a.tw);
+    fft_seq<L, false>(myseq, lane, a.tw);
 
     // ---- auv + energy ----
     const float scale = 2.0f / (float)L;
     double esum = 0.0;
     for (int e = threadIdx.x; e < S * L; e += T) {
         const int s = e / L, u = e % L;
-        const float2 Z = buf[s * L + u];
-        const float2 Zr = buf[s * L + ((L - u) & (L - 1))];
+        const float2 Z = buf[s * LP + pidx(u)];
+        const float2 Zr = buf[s * LP + pidx((L - u) & (L - 1))];
         const float2 Va = make_float2(0.5f * (Z.x + Zr.x), 0.5f * (Z.y - Zr.y));
         const float2 Vb = make_float2(0.5f * (Z.y + Zr.y), -0.5f * (Z.x - Zr.x));
         const float2 q = __ldg(a.qw + u);
@@ -203,13 +233,13 @@ k_col(ColArgs a) {
         const float xb = scale * (Vb.x * q.x + Vb.y * q.y);
         auv[(2 * s) * L + u] = xa;
         auv[(2 * s + 1) * L + u] = xb;
-        const float wu = __ldg(a.wu + u);
+        const float wu = (float)u * a.ku;
         const double cu = u == 0 ? 1.0 : 2.0;
 #pragma unroll
         for (int p = 0; p < 2; ++p) {
             const int col = c0 + 2 * s + p;
             if (col < N) {
-                const float wv = __ldg(a.wv + col);
+                const float wv = (float)col * a.kv;
                 float wuh, wvh, inv;
                 spectral_weights(wu, wv, wuh, wvh, inv);
                 const double x = p ? xb : xa;
@@ -222,55 +252,51 @@ k_col(ColArgs a) {
     // ---- three inverse transforms along x: 0 -> gx (IDXST form), 1 -> gy, 2 -> gp ----
     const int rounds = a.want_phi ? 3 : 2;
     for (int r = 0; r < rounds; ++r) {
-        // build V for seq s = columns (2s, 2s+1)
-        for (int e = threadIdx.x; e < S * L; e += T) {
-            const int s = e / L, n = e % L;
-            float An[2], Am[2];  // A_n and A_{L-n} for the two packed columns
+        // build V for seq s = columns (2s, 2s+1); one thread makes V_n and V_{L-n}
+        for (int e = threadIdx.x; e < S * (L / 2); e += T) {
+            const int s = e / (L / 2), n = e % (L / 2);
+            const int nm = L - n;  // partner index (L when n == 0)
+            float An[2], Am[2];    // A_n, A_{L-n} of the two packed columns (A_L = 0)
 #pragma unroll
             for (int p = 0; p < 2; ++p) {
                 const int cl = 2 * s + p;
-                const int col = c0 + cl;
-                const float wv = col < N ? __ldg(a.wv + col) : 0.0f;
+                const float wv = (float)(c0 + cl) * a.kv;
                 const float* au = auv + cl * L;
                 if (r == 0) {
-                    // b_n = a_{L-n} (b_0 = 0), a_u = auv_u * wu_half
-                    float wuh, wvh, inv;
-                    if (n == 0) {
-                        An[p] = 0.0f;
-                        Am[p] = 0.0f;  // b_L = 0 by definition
-                    } else {
-                        spectral_weights(__ldg(a.wu + (L - n)), wv, wuh, wvh, inv);
-                        An[p] = au[L - n] * wuh;
-                        spectral_weights(__ldg(a.wu + n), wv, wuh, wvh, inv);
-                        Am[p] = au[n] * wuh;
-                    }
+                    // b_n = a_{L-n}, b_0 = b_L = 0, a_u = auv_u * wu_half(u)
+                    An[p] = n == 0 ? 0.0f : au[nm] * col_weight(0, (float)nm * a.ku, wv);
+                    Am[p] = n == 0 ? 0.0f : au[n] * col_weight(0, (float)n * a.ku, wv);
                 } else {
-                    float wuh, wvh, inv;
-                    spectral_weights(__ldg(a.wu + n), wv, wuh, wvh, inv);
-                    An[p] = au[n] * (r == 1 ? 2.0f * wvh : inv);
-                    if (n == 0) {
-                        Am[p] = 0.0f;
-                    } else {
-                        spectral_weights(__ldg(a.wu + (L - n)), wv, wuh, wvh, inv);
-                        Am[p] = au[L - n] * (r == 1 ? 2.0f * wvh : inv);
-                    }
+                    An[p] = au[n] * col_weight(r, (float)n * a.ku, wv);
+                    Am[p] = n == 0 ? 0.0f : au[nm] * col_weight(r, (float)nm * a.ku, wv);
                 }
             }
-            // V = (A_n - i A_{L-n}) e^{i pi n / 2L} for each column; pack col p=1 as imaginary
-            const float2 q = __ldg(a.qw + n);
-            const float2 va = make_float2(An[0] * q.x + Am[0] * q.y, An[0] * q.y - Am[0] * q.x);
-            const float2 vb = make_float2(An[1] * q.x + Am[1] * q.y, An[1] * q.y - Am[1] * q.x);
-            buf[s * L + n] = make_float2(va.x - vb.y, va.y + vb.x);
+            float2* sq = buf + s * LP;
+            sq[pidx(n)] = idct_pre(An[0], Am[0], An[1], Am[1], __ldg(a.qw + n));
+            if (n != 0) {
+                sq[pidx(nm)] = idct_pre(Am[0], An[0], Am[1], An[1], __ldg(a.qw + nm));
+            } else {
+                // V_{L/2} = (A_{L/2} - i A_{L/2}) e^{i pi / 4}
+                float h[2];
+#pragma unroll
+                for (int p = 0; p < 2; ++p) {
+                    const int cl = 2 * s + p;
+                    const float wv = (float)(c0 + cl) * a.kv;
+                    h[p] = auv[cl * L + L / 2] * col_weight(r, (float)(L / 2) * a.ku, wv);
+                }
+                sq[pidx(L / 2)] = idct_pre(h[0], h[0], h[1], h[1], __ldg(a.qw + L / 2));
+            }
         }
         __syncthreads();
-        fft_smem<L, S, T, true>(buf, a.tw);
+        fft_seq<L, true>(myseq, lane, a.tw);
         float* out = r == 0 ? a.gx : (r == 1 ? a.gy : a.gp);
+#pragma unroll 4
         for (int e = threadIdx.x; e < L * (W / 4); e += T) {
             const int k = e / (W / 4), q4 = e % (W / 4);
             const int col = c0 + 4 * q4;
-            const int src = makhoul_pos(k, L);
-            float2 v0 = buf[(2 * q4) * L + src];
-            float2 v1 = buf[(2 * q4 + 1) * L + src];
+            const int src = pidx(makhoul_pos(k, L));
+            float2 v0 = buf[(2 * q4) * LP + src];
+            float2 v1 = buf[(2 * q4 + 1) * LP + src];
             if (r == 0 && (k & 1)) { v0.x = -v0.x; v0.y = -v0.y; v1.x = -v1.x; v1.y = -v1.y; }
             if (col < N)
                 *reinterpret_cast<float4*>(out + (int64_t)k * N + col) = make_float4(v0.x, v0.y, v1.x, v1.y);
@@ -314,14 +340,17 @@ k_col(ColArgs a) {
 
 // ---------------------------------------------------------------------------
 // Pass 3: inverse along y (rows).  ROWS rows per CTA; sequences:
-//   2j   : fx row (IDCT of Gx) + i * fy row (IDXST of Gy) for row j (j < ROWS)
-//   ...  : potential rows packed in pairs (IDCT of Gp)
+//   j < ROWS : fx row j (IDCT of Gx) + i * fy row j (IDXST of Gy)
+//   then     : potential rows packed in pairs (IDCT of Gp)
 // ---------------------------------------------------------------------------
 template <int L>
 struct RowInvCfg {
+    static constexpr int P = L / 16;
     static constexpr int ROWS = (2048 / L) > 1 ? 2 * (2048 / L) : 2;
     static constexpr int S = ROWS + ROWS / 2;
-    static constexpr size_t SMEM = (size_t)S * L * sizeof(float2);
+    static constexpr int T = P * S;
+    static constexpr int LP = Padded<L>::value;
+    static constexpr size_t SMEM = (size_t)S * LP * sizeof(float2);
 };
 
 struct RowInvArgs {
@@ -334,53 +363,56 @@ struct RowInvArgs {
 };
 
 template <int L>
-__global__ void __launch_bounds__(kFftThreads)
+__global__ void __launch_bounds__(RowInvCfg<L>::T)
 k_row_inv(RowInvArgs a) {
     using C = RowInvCfg<L>;
-    constexpr int S = C::S, ROWS = C::ROWS, T = kFftThreads;
+    constexpr int S = C::S, ROWS = C::ROWS, T = C::T, LP = C::LP;
     extern __shared__ float2 sm_rowinv[];
     float2* buf = sm_rowinv;
     const int row0 = blockIdx.x * ROWS;
-    for (int e = threadIdx.x; e < S * L; e += T) {
-        const int s = e / L, n = e % L;
-        float An[2], Am[2];
-        bool valid = true;
+    // one thread builds V_n and V_{L-n} from the same four loads
+#pragma unroll 2
+    for (int e = threadIdx.x; e < S * (L / 2); e += T) {
+        const int s = e / (L / 2), n = e % (L / 2);
+        const int nm = L - n;
+        const int h = L / 2;
+        float An[2] = {0.f, 0.f}, Am[2] = {0.f, 0.f}, Ah[2] = {0.f, 0.f};  // A_n, A_{L-n}, A_{L/2}
         if (s < ROWS) {
             const int row = row0 + s;
-            valid = row < a.M;
-            if (valid) {
+            if (row < a.M) {
                 const float* gxr = a.gx + (int64_t)row * L;
                 const float* gyr = a.gy + (int64_t)row * L;
+                // fx: IDCT of the Gx row; fy: IDXST of the Gy row = IDCT of b (b_0 = 0,
+                // b_m = a_{L-m}) with the 1/2 folded in
                 An[0] = __ldg(gxr + n);
-                Am[0] = n == 0 ? 0.0f : __ldg(gxr + (L - n));
-                // IDXST: b_0 = 0, b_m = a_{L-m}; the 1/2 factor folded in
-                An[1] = n == 0 ? 0.0f : 0.5f * __ldg(gyr + (L - n));
+                Am[0] = n == 0 ? 0.0f : __ldg(gxr + nm);
+                An[1] = n == 0 ? 0.0f : 0.5f * __ldg(gyr + nm);
                 Am[1] = n == 0 ? 0.0f : 0.5f * __ldg(gyr + n);
+                if (n == 0) { Ah[0] = __ldg(gxr + h); Ah[1] = 0.5f * __ldg(gyr + h); }
             }
-        } else {
+        } else if (a.want_phi) {
             const int row = row0 + 2 * (s - ROWS);
-            valid = a.want_phi && row < a.M;
-            if (valid) {
 #pragma unroll
-                for (int p = 0; p < 2; ++p) {
+            for (int p = 0; p < 2; ++p) {
+                if (row + p < a.M) {
                     const float* gpr = a.gp + (int64_t)(row + p) * L;
-                    const bool ok = row + p < a.M;
-                    An[p] = ok ? __ldg(gpr + n) : 0.0f;
-                    Am[p] = (ok && n != 0) ? __ldg(gpr + (L - n)) : 0.0f;
+                    An[p] = __ldg(gpr + n);
+                    Am[p] = n == 0 ? 0.0f : __ldg(gpr + nm);
+                    if (n == 0) Ah[p] = __ldg(gpr + h);
                 }
             }
         }
-        if (!valid) { An[0] = An[1] = Am[0] = Am[1] = 0.0f; }
-        const float2 q = __ldg(a.qw + n);
-        const float2 va = make_float2(An[0] * q.x + Am[0] * q.y, An[0] * q.y - Am[0] * q.x);
-        const float2 vb = make_float2(An[1] * q.x + Am[1] * q.y, An[1] * q.y - Am[1] * q.x);
-        buf[s * L + n] = make_float2(va.x - vb.y, va.y + vb.x);
+        float2* sq = buf + s * LP;
+        sq[pidx(n)] = idct_pre(An[0], Am[0], An[1], Am[1], __ldg(a.qw + n));
+        if (n != 0) sq[pidx(nm)] = idct_pre(Am[0], An[0], Am[1], An[1], __ldg(a.qw + nm));
+        else sq[pidx(h)] = idct_pre(Ah[0], Ah[0], Ah[1], Ah[1], __ldg(a.qw + h));
     }
     __syncthreads();
-    fft_smem<L, S, T, true>(buf, a.tw);
+    fft_seq<L, true>(buf + (threadIdx.x / C::P) * LP, threadIdx.x % C::P, a.tw);
+#pragma unroll 2
     for (int e = threadIdx.x; e < S * L; e += T) {
         const int s = e / L, l = e % L;
-        const float2 v = buf[s * L + makhoul_pos(l, L)];
+        const float2 v = buf[s * LP + pidx(makhoul_pos(l, L))];
         if (s < ROWS) {
             const int row = row0 + s;
             if (row < a.M) {

@@ -1,17 +1,26 @@
 // fft.cuh -- shared-memory complex FFT used by the DCT-family kernels.
 //
-// A CTA of T threads transforms S contiguous length-L sequences held in
-// shared memory (sequence s at buf + s*L), in place, natural order in and
-// out.  The schedule is Stockham autosort with radix-4 stages and one closing
-// radix-2 stage when log2(L) is odd (formulation of E. Bainville, "OpenCL
-// Fast Fourier Transform", 2010: stage stride Ns, output index
-// expand(j, Ns, R) = (j / Ns) * Ns * R + j % Ns).  Each stage reads all of a
-// thread's butterfly inputs into registers, synchronises, then writes: the
-// permutation is a bijection, so the in-place update is race free.
+// One length-L sequence (L = 2^p, 16 <= L <= 4096) is transformed by
+// P = L/16 threads of a CTA; a CTA holds several sequences, one per group of P
+// consecutive threads, and all of them run the passes in lock step (each
+// pass ends in __syncthreads, so every thread of the CTA must call).
 //
-// Twiddles come from a table tw[t] = exp(-2*pi*i*t/L), t < L, computed in
-// float64 on the host and rounded once to fp32 (no device sincosf).
-// INV selects exp(+...) (unnormalised inverse DFT).
+// Schedule: Stockham autosort (natural order in and out) with radix-16
+// passes and one closing radix-2/4/8 pass when p is not a multiple of 4.
+// In a pass of radix R with stride Ns, butterfly b reads in[b + r*L/R],
+// multiplies element r by w_{Ns*R}^{r*(b mod Ns)}, takes an R-point DFT in
+// registers and writes out[(b / Ns)*Ns*R + b mod Ns + r*Ns] (E. Bainville,
+// "OpenCL Fast Fourier Transform", 2010).  Every thread owns 16 values per
+// pass (16/R butterflies), reads all of them, synchronises, then writes: the
+// pass is a bijection, so it runs in place.
+//
+// Shared-memory layout: logical element p of a sequence lives at
+// p + p/16 (one float2 of padding per 16), so the stride-16 writes of the
+// first pass and the stride-R reads of later passes spread over all banks.
+//
+// Twiddles come from a table tw[t] = exp(-2 pi i t / L), t < L, computed in
+// float64 on the host and rounded once to fp32 (no device sincosf).  INV
+// selects exp(+...) (unnormalised inverse DFT).
 #pragma once
 #include <cstdint>
 
@@ -25,105 +34,152 @@ __device__ __forceinline__ float2 cmulc(float2 a, float2 b) {  // a * conj(b)
 }
 __device__ __forceinline__ float2 cadd(float2 a, float2 b) { return make_float2(a.x + b.x, a.y + b.y); }
 __device__ __forceinline__ float2 csub(float2 a, float2 b) { return make_float2(a.x - b.x, a.y - b.y); }
+// multiply by -i (forward) or +i (inverse)
+template <bool INV>
+__device__ __forceinline__ float2 mul_mi(float2 a) {
+    return INV ? make_float2(-a.y, a.x) : make_float2(a.y, -a.x);
+}
 
 template <int L>
 struct Log2 { static constexpr int value = 1 + Log2<L / 2>::value; };
 template <>
 struct Log2<1> { static constexpr int value = 0; };
 
-template <int L, int S, int T, bool INV>
-__device__ __forceinline__ void fft_smem(float2* buf, const float2* __restrict__ tw) {
-    constexpr int LOG = Log2<L>::value;
-    constexpr int NR4 = LOG / 2;
-    constexpr int J4 = L / 4;                      // butterflies per sequence, radix-4
-    constexpr int TOT4 = S * J4;
-    constexpr int BPT4 = (TOT4 + T - 1) / T;
-    const int tid = threadIdx.x;
+// padded shared-memory index and sequence stride
+__device__ __forceinline__ int pidx(int p) { return p + (p >> 4); }
+template <int L>
+struct Padded { static constexpr int value = L + L / 16; };
 
-    int Ns = 1;
-#pragma unroll 1
-    for (int st = 0; st < NR4; ++st) {
-        float2 v[BPT4][4];
+// ---- small DFTs in registers, natural order in and out ----
+template <bool INV>
+__device__ __forceinline__ void dft2(float2* v) {
+    const float2 a = v[0];
+    v[0] = cadd(a, v[1]);
+    v[1] = csub(a, v[1]);
+}
+
+template <bool INV>
+__device__ __forceinline__ void dft4(float2& a0, float2& a1, float2& a2, float2& a3) {
+    const float2 b0 = cadd(a0, a2), b1 = csub(a0, a2);
+    const float2 b2 = cadd(a1, a3), b3 = mul_mi<INV>(csub(a1, a3));
+    a0 = cadd(b0, b2);
+    a2 = csub(b0, b2);
+    a1 = cadd(b1, b3);
+    a3 = csub(b1, b3);
+}
+
+template <bool INV>
+__device__ __forceinline__ void dft4(float2* v) { dft4<INV>(v[0], v[1], v[2], v[3]); }
+
+template <bool INV>
+__device__ __forceinline__ void dft8(float2* v) {
+    // even/odd split: X_k = E_k + w8^k O_k, X_{k+4} = E_k - w8^k O_k
+    float2 e0 = v[0], e1 = v[2], e2 = v[4], e3 = v[6];
+    float2 o0 = v[1], o1 = v[3], o2 = v[5], o3 = v[7];
+    dft4<INV>(e0, e1, e2, e3);
+    dft4<INV>(o0, o1, o2, o3);
+    const float h = 0.70710678118654752440f;
+    o1 = cmul(o1, make_float2(h, INV ? h : -h));
+    o2 = mul_mi<INV>(o2);
+    o3 = cmul(o3, make_float2(-h, INV ? h : -h));
+    v[0] = cadd(e0, o0); v[4] = csub(e0, o0);
+    v[1] = cadd(e1, o1); v[5] = csub(e1, o1);
+    v[2] = cadd(e2, o2); v[6] = csub(e2, o2);
+    v[3] = cadd(e3, o3); v[7] = csub(e3, o3);
+}
+
+template <bool INV>
+__device__ __forceinline__ void dft16(float2* x) {
+    // n = 4 n1 + n2, k = k1 + 4 k2:
+    // Y[n2][k1] = DFT4_n1(x[4 n1 + n2]) * w16^(n2 k1);  X[k1 + 4 k2] = DFT4_n2(Y[n2][k1])
 #pragma unroll
-        for (int b = 0; b < BPT4; ++b) {
-            const int idx = tid + b * T;
-            if (TOT4 % T == 0 || idx < TOT4) {
-                const int s = idx / J4, j = idx % J4;
-                const float2* in = buf + s * L;
+    for (int n2 = 0; n2 < 4; ++n2) dft4<INV>(x[n2], x[4 + n2], x[8 + n2], x[12 + n2]);
+    // after this, x[4 k1 + n2] holds Y[n2][k1]
+    const float c1 = 0.92387953251128675613f, s1 = 0.38268343236508977173f;
+    const float h = 0.70710678118654752440f;
+    const float sg = INV ? 1.0f : -1.0f;
+    // twiddles w16^j, j = n2*k1 in {1,2,3,2,4,6,3,6,9}
+    x[5] = cmul(x[5], make_float2(c1, sg * s1));     // n2=1,k1=1: j=1
+    x[9] = cmul(x[9], make_float2(h, sg * h));       // n2=1,k1=2: j=2
+    x[13] = cmul(x[13], make_float2(s1, sg * c1));   // n2=1,k1=3: j=3
+    x[6] = cmul(x[6], make_float2(h, sg * h));       // n2=2,k1=1: j=2
+    x[10] = mul_mi<INV>(x[10]);                      // n2=2,k1=2: j=4
+    x[14] = cmul(x[14], make_float2(-h, sg * h));    // n2=2,k1=3: j=6
+    x[7] = cmul(x[7], make_float2(s1, sg * c1));     // n2=3,k1=1: j=3
+    x[11] = cmul(x[11], make_float2(-h, sg * h));    // n2=3,k1=2: j=6
+    x[15] = cmul(x[15], make_float2(-c1, -sg * s1)); // n2=3,k1=3: j=9
 #pragma unroll
-                for (int r = 0; r < 4; ++r) v[b][r] = in[j + r * J4];
-            }
-        }
-        __syncthreads();
+    for (int k1 = 0; k1 < 4; ++k1) dft4<INV>(x[4 * k1], x[4 * k1 + 1], x[4 * k1 + 2], x[4 * k1 + 3]);
+    // now x[4 k1 + k2] holds X[k1 + 4 k2]; transpose to natural order
+    float2 t[16];
 #pragma unroll
-        for (int b = 0; b < BPT4; ++b) {
-            const int idx = tid + b * T;
-            if (TOT4 % T == 0 || idx < TOT4) {
-                const int s = idx / J4, j = idx % J4;
-                const int k = j & (Ns - 1);
-                const int ts = k * (L / (4 * Ns));
-                float2 a0 = v[b][0], a1, a2, a3;
-                if (INV) {
-                    a1 = cmulc(v[b][1], __ldg(tw + ts));
-                    a2 = cmulc(v[b][2], __ldg(tw + 2 * ts));
-                    a3 = cmulc(v[b][3], __ldg(tw + 3 * ts));
-                } else {
-                    a1 = cmul(v[b][1], __ldg(tw + ts));
-                    a2 = cmul(v[b][2], __ldg(tw + 2 * ts));
-                    a3 = cmul(v[b][3], __ldg(tw + 3 * ts));
-                }
-                const float2 b0 = cadd(a0, a2), b1 = csub(a0, a2);
-                const float2 b2 = cadd(a1, a3), b3 = csub(a1, a3);
-                // forward: X1 = b1 - i*b3, X3 = b1 + i*b3; inverse swaps the signs
-                const float2 ib3 = make_float2(-b3.y, b3.x);  // i * b3
-                float2* out = buf + s * L + (j / Ns) * Ns * 4 + k;
-                out[0] = cadd(b0, b2);
-                out[2 * Ns] = csub(b0, b2);
-                if (INV) {
-                    out[Ns] = cadd(b1, ib3);
-                    out[3 * Ns] = csub(b1, ib3);
-                } else {
-                    out[Ns] = csub(b1, ib3);
-                    out[3 * Ns] = cadd(b1, ib3);
-                }
-            }
-        }
-        __syncthreads();
-        Ns *= 4;
+    for (int i = 0; i < 16; ++i) t[i] = x[i];
+#pragma unroll
+    for (int k1 = 0; k1 < 4; ++k1)
+#pragma unroll
+        for (int k2 = 0; k2 < 4; ++k2) x[k1 + 4 * k2] = t[4 * k1 + k2];
+}
+
+template <int R, bool INV>
+__device__ __forceinline__ void dft(float2* v) {
+    if constexpr (R == 2) dft2<INV>(v);
+    else if constexpr (R == 4) dft4<INV>(v);
+    else if constexpr (R == 8) dft8<INV>(v);
+    else dft16<INV>(v);
+}
+
+template <int L, int R, int NS, bool INV>
+__device__ __forceinline__ void fft_pass(float2* seq, int lane, const float2* __restrict__ tw) {
+    constexpr int NB = L / R;      // butterflies per sequence
+    constexpr int P = L / 16;      // threads per sequence
+    constexpr int BPT = NB / P;    // butterflies per thread (16 / R)
+    float2 v[BPT][R];
+#pragma unroll
+    for (int bb = 0; bb < BPT; ++bb) {
+        const int b = lane + bb * P;
+#pragma unroll
+        for (int r = 0; r < R; ++r) v[bb][r] = seq[pidx(b + r * NB)];
     }
-    if (LOG & 1) {
-        constexpr int J2 = L / 2;
-        constexpr int TOT2 = S * J2;
-        constexpr int BPT2 = (TOT2 + T - 1) / T;
-        float2 v[BPT2][2];
+    __syncthreads();
 #pragma unroll
-        for (int b = 0; b < BPT2; ++b) {
-            const int idx = tid + b * T;
-            if (TOT2 % T == 0 || idx < TOT2) {
-                const int s = idx / J2, j = idx % J2;
-                v[b][0] = buf[s * L + j];
-                v[b][1] = buf[s * L + j + J2];
+    for (int bb = 0; bb < BPT; ++bb) {
+        const int b = lane + bb * P;
+        const int k = b & (NS - 1);
+        if (NS > 1) {
+            constexpr int STEP = L / (NS * R);
+#pragma unroll
+            for (int r = 1; r < R; ++r) {
+                const float2 w = __ldg(tw + r * k * STEP);
+                v[bb][r] = INV ? cmulc(v[bb][r], w) : cmul(v[bb][r], w);
             }
         }
-        __syncthreads();
+        dft<R, INV>(v[bb]);
+        const int base = (b / NS) * NS * R + k;
 #pragma unroll
-        for (int b = 0; b < BPT2; ++b) {
-            const int idx = tid + b * T;
-            if (TOT2 % T == 0 || idx < TOT2) {
-                const int s = idx / J2, j = idx % J2;
-                // last stage: Ns == L/2, so k == j and the twiddle index is j
-                const float2 w = __ldg(tw + j);
-                const float2 a1 = INV ? cmulc(v[b][1], w) : cmul(v[b][1], w);
-                buf[s * L + j] = cadd(v[b][0], a1);
-                buf[s * L + j + J2] = csub(v[b][0], a1);
-            }
-        }
-        __syncthreads();
+        for (int r = 0; r < R; ++r) seq[pidx(base + r * NS)] = v[bb][r];
+    }
+    __syncthreads();
+}
+
+template <int L, int NS, bool INV>
+__device__ __forceinline__ void fft_passes(float2* seq, int lane, const float2* __restrict__ tw) {
+    if constexpr (NS < L) {
+        constexpr int REM = L / NS;
+        constexpr int R = REM >= 16 ? 16 : REM;
+        fft_pass<L, R, NS, INV>(seq, lane, tw);
+        fft_passes<L, NS * R, INV>(seq, lane, tw);
     }
 }
 
+// Transform the padded sequence at `seq` in place; lane in [0, L/16).
+template <int L, bool INV>
+__device__ __forceinline__ void fft_seq(float2* seq, int lane, const float2* __restrict__ tw) {
+    static_assert(L >= 16 && (L & (L - 1)) == 0, "power-of-two length >= 16");
+    fft_passes<L, 1, INV>(seq, lane, tw);
+}
+
 // Makhoul (1980) even/odd reordering used by both directions:
-// v[n] = x[2n], v[L-1-n] = x[2n+1].  position_of(m) is where x[m] goes.
+// v[n] = x[2n], v[L-1-n] = x[2n+1].  makhoul_pos(m) is where x[m] goes.
 __device__ __forceinline__ int makhoul_pos(int m, int L) {
     return (m & 1) ? (L - 1 - (m >> 1)) : (m >> 1);
 }
