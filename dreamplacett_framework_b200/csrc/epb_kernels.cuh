@@ -100,8 +100,9 @@ k_row_fwd(long long* __restrict__ qgrid,            // FROM_FIXED: [M][L] int64 
             if (row < M) {
                 const int64_t off = (int64_t)row * L + m;
                 if (FROM_FIXED) {
-                    const long long q = __ldcs(qgrid + off);
-                    __stcs(qgrid + off, 0ll);  // leave the grid zeroed for the next scatter
+                    // the grid is re-zeroed after the FFT: a store right behind this
+                    // load to the same address would stall the load pipeline
+                    const long long q = qgrid[off];
                     if (q < 0 || q >= (1ll << 62)) sat = 1;
                     v = __double2float_rn(__dmul_rn(__ll2double_rn(q), dscale));
                     if (init) v = __fadd_rn(v, __ldg(init + off));
@@ -130,6 +131,12 @@ k_row_fwd(long long* __restrict__ qgrid,            // FROM_FIXED: [M][L] int64 
         const int ra = row0 + 2 * s;
         if (ra < M) t1[(int64_t)ra * L + k] = scale * (Va.x * q.x + Va.y * q.y);
         if (ra + 1 < M) t1[(int64_t)(ra + 1) * L + k] = scale * (Vb.x * q.x + Vb.y * q.y);
+    }
+    if (FROM_FIXED) {
+        // leave this CTA's rows of the grid zeroed for the next scatter
+        const int nrows = min(C::ROWS, M - row0);
+        longlong2* g2 = reinterpret_cast<longlong2*>(qgrid + (int64_t)row0 * L);
+        for (int e = threadIdx.x; e < nrows * L / 2; e += T) g2[e] = make_longlong2(0ll, 0ll);
     }
 }
 
