@@ -358,6 +358,7 @@ struct RowInvCfg {
     static constexpr int T = P * S;
     static constexpr int LP = Padded<L>::value;
     static constexpr size_t SMEM = (size_t)S * LP * sizeof(float2);
+    static constexpr int MINB = T <= 384 ? 3 : 1;
 };
 
 struct RowInvArgs {
@@ -370,7 +371,7 @@ struct RowInvArgs {
 };
 
 template <int L>
-__global__ void __launch_bounds__(RowInvCfg<L>::T)
+__global__ void __launch_bounds__(RowInvCfg<L>::T, RowInvCfg<L>::MINB)
 k_row_inv(RowInvArgs a) {
     using C = RowInvCfg<L>;
     constexpr int S = C::S, ROWS = C::ROWS, T = C::T, LP = C::LP;

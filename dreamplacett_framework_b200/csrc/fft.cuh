@@ -129,20 +129,23 @@ __device__ __forceinline__ void dft(float2* v) {
 }
 
 template <int L, int R, int NS, bool INV>
-__device__ __forceinline__ void fft_pass(float2* seq, int lane, const float2* __restrict__ tw) {
+__device__ __forceinline__ void fft_pass(float2* seq, int lane, const float2* __restrict__ tw, bool active) {
     constexpr int NB = L / R;      // butterflies per sequence
     constexpr int P = L / 16;      // threads per sequence
     constexpr int BPT = NB / P;    // butterflies per thread (16 / R)
     float2 v[BPT][R];
+    if (active) {
 #pragma unroll
-    for (int bb = 0; bb < BPT; ++bb) {
-        const int b = lane + bb * P;
+        for (int bb = 0; bb < BPT; ++bb) {
+            const int b = lane + bb * P;
 #pragma unroll
-        for (int r = 0; r < R; ++r) v[bb][r] = seq[pidx(b + r * NB)];
+            for (int r = 0; r < R; ++r) v[bb][r] = seq[pidx(b + r * NB)];
+        }
     }
     __syncthreads();
 #pragma unroll
     for (int bb = 0; bb < BPT; ++bb) {
+        if (!active) break;
         const int b = lane + bb * P;
         const int k = b & (NS - 1);
         if (NS > 1) {
@@ -162,20 +165,21 @@ __device__ __forceinline__ void fft_pass(float2* seq, int lane, const float2* __
 }
 
 template <int L, int NS, bool INV>
-__device__ __forceinline__ void fft_passes(float2* seq, int lane, const float2* __restrict__ tw) {
+__device__ __forceinline__ void fft_passes(float2* seq, int lane, const float2* __restrict__ tw, bool active) {
     if constexpr (NS < L) {
         constexpr int REM = L / NS;
         constexpr int R = REM >= 16 ? 16 : REM;
-        fft_pass<L, R, NS, INV>(seq, lane, tw);
-        fft_passes<L, NS * R, INV>(seq, lane, tw);
+        fft_pass<L, R, NS, INV>(seq, lane, tw, active);
+        fft_passes<L, NS * R, INV>(seq, lane, tw, active);
     }
 }
 
-// Transform the padded sequence at `seq` in place; lane in [0, L/16).
+// Transform the padded sequence at `seq` in place; lane in [0, L/16).  Threads
+// with active == false skip the arithmetic but still meet every barrier.
 template <int L, bool INV>
-__device__ __forceinline__ void fft_seq(float2* seq, int lane, const float2* __restrict__ tw) {
+__device__ __forceinline__ void fft_seq(float2* seq, int lane, const float2* __restrict__ tw, bool active = true) {
     static_assert(L >= 16 && (L & (L - 1)) == 0, "power-of-two length >= 16");
-    fft_passes<L, 1, INV>(seq, lane, tw);
+    fft_passes<L, 1, INV>(seq, lane, tw, active);
 }
 
 // Makhoul (1980) even/odd reordering used by both directions:
