@@ -26,8 +26,11 @@ EXPORTS = (
     "epb_version", "epb_status_string", "epb_create", "epb_destroy", "epb_last_error",
     "epb_geometry", "epb_set_initial_density", "epb_forward", "epb_backward",
     "epb_scatter_fixed", "epb_dct_solve", "epb_gather", "epb_error_flags",
-    "epb_profile_start", "epb_profile_stop",
+    "epb_profile_start", "epb_profile_stop", "epb_density_noalloc",
 )
+
+# Largest grid (M*N bins) epb_density_noalloc accepts (EPB_NOALLOC_MAX_BINS).
+NOALLOC_MAX_BINS = 1024 * 1024
 
 # Stage indices of epb_profile_stop (EPB_STAGE_* in include/epb.h).
 STAGES = ("scatter", "row_fwd", "column", "row_inv", "gather")
@@ -93,6 +96,7 @@ def load():
     L.epb_error_flags.argtypes = [vp, vp, ctypes.POINTER(ctypes.c_uint32)]
     L.epb_profile_start.argtypes = [vp, i32]
     L.epb_profile_stop.argtypes = [vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(i32)]
+    L.epb_density_noalloc.argtypes = [ctypes.POINTER(EpbConfig), cp, vp, vp, vp, ctypes.c_char_p, i32]
     for name in EXPORTS:
         if name not in ("epb_version", "epb_status_string", "epb_last_error"):
             getattr(L, name).restype = ctypes.c_int

@@ -10,6 +10,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -566,3 +567,107 @@ int epb_profile_stop(epb_handle* h, double* stage_ms, int32_t* stage_launches) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free density map (epb_density_noalloc).  For callers that may not
+// allocate device memory: their memory belongs to another allocator, or
+// cudaMalloc's device-wide synchronisation is not acceptable on their path.
+// The accumulation grid is this file-scope device array; its device address
+// is looked up once per device with cudaGetSymbolAddress (host code must not
+// use the symbol itself as a pointer).  The tail words after the grid hold the
+// kernel's flag word.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) long long g_noalloc_grid[EPB_NOALLOC_MAX_BINS + 32];
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {nullptr};
+
+// fp32 density = fp32(q * dscale) (+ init), the same operations as k_row_fwd's load phase
+__global__ void __launch_bounds__(256)
+k_fixed_to_density(const long long* __restrict__ q, const float* __restrict__ init, double dscale,
+                   int64_t nbins, float* __restrict__ out) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; b < nbins; b += stride) {
+        float v = __double2float_rn(__dmul_rn(__ll2double_rn(q[b]), dscale));
+        if (init) v = __fadd_rn(v, __ldg(init + b));
+        out[b] = v;
+    }
+}
+
+int noalloc_fail(char* err, int32_t len, int code, const std::string& msg) {
+    if (err && len > 0) {
+        std::strncpy(err, msg.c_str(), (size_t)len - 1);
+        err[len - 1] = '\0';
+    }
+    return code;
+}
+
+}  // namespace
+
+extern "C" int epb_density_noalloc(const epb_config* cfg, const epb_cells* cells, const float* init_norm,
+                                   epb_stream stream, float* density, char* err, int32_t err_len) {
+    if (!cfg || !cells || !density) return noalloc_fail(err, err_len, EPB_EINVAL, "cfg, cells and density must be non-NULL");
+    if (cfg->num_bins_x < 1 || cfg->num_bins_y < 1)
+        return noalloc_fail(err, err_len, EPB_EINVAL, "num_bins_x and num_bins_y must be positive");
+    const int64_t nbins = (int64_t)cfg->num_bins_x * cfg->num_bins_y;
+    if (nbins > EPB_NOALLOC_MAX_BINS)
+        return noalloc_fail(err, err_len, EPB_EINVAL,
+                            "grid of " + std::to_string(cfg->num_bins_x) + "x" + std::to_string(cfg->num_bins_y) +
+                                " bins exceeds the allocation-free limit of " + std::to_string(EPB_NOALLOC_MAX_BINS) +
+                                " bins; use epb_create/epb_forward");
+    if (!(cfg->xh > cfg->xl) || !(cfg->yh > cfg->yl) || cfg->fixed_point_bits > 60 || cfg->flags != 0)
+        return noalloc_fail(err, err_len, EPB_EINVAL, "invalid die box, fixed_point_bits or flags");
+    if (cfg->device < 0 || cfg->device >= kMaxDevices) return noalloc_fail(err, err_len, EPB_EINVAL, "bad device");
+    CellView v;
+    if (int rc = make_view(nullptr, cells, v)) return noalloc_fail(err, err_len, rc, "invalid cell ranges or NULL arrays");
+
+    DeviceGuard guard(cfg->device);
+    if (!guard.ok) return noalloc_fail(err, err_len, EPB_ECUDA, "cudaSetDevice failed");
+    void* base = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        if (!g_noalloc_ptr[cfg->device]) {
+            cudaError_t e = cudaGetSymbolAddress(&g_noalloc_ptr[cfg->device], g_noalloc_grid);
+            if (e != cudaSuccess) {
+                g_noalloc_ptr[cfg->device] = nullptr;
+                return noalloc_fail(err, err_len, EPB_ECUDA, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+            }
+        }
+        base = g_noalloc_ptr[cfg->device];
+    }
+    long long* grid = static_cast<long long*>(base);
+    unsigned* flags = reinterpret_cast<unsigned*>(grid + EPB_NOALLOC_MAX_BINS);
+
+    // geometry exactly as epb_create resolves it
+    epb_handle g;
+    g.M = cfg->num_bins_x; g.N = cfg->num_bins_y;
+    g.xl = cfg->xl; g.yl = cfg->yl; g.xh = cfg->xh; g.yh = cfg->yh;
+    g.bsx = ((float)cfg->xh - (float)cfg->xl) / (float)g.M;
+    g.bsy = ((float)cfg->yh - (float)cfg->yl) / (float)g.N;
+    if (cfg->fixed_point_bits > 0) {
+        g.S = cfg->fixed_point_bits;
+    } else {
+        const double area = (cfg->xh - cfg->xl) * (cfg->yh - cfg->yl);
+        int ib = (int)std::ceil(std::log2(area > 1.0 ? area : 1.0)) + 1;
+        if (ib < 32) ib = 32;
+        g.S = 63 - ib;
+    }
+    const double dscale = std::ldexp(1.0, -g.S) / ((double)g.bsx * (double)g.bsy);
+    cudaStream_t st = (cudaStream_t)stream;
+    cudaError_t e = cudaMemsetAsync(grid, 0, (size_t)(nbins + 32) * sizeof(long long), st);
+    if (e != cudaSuccess) return noalloc_fail(err, err_len, EPB_ECUDA, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
+    if (v.n > 0) {
+        k_scatter<<<cell_blocks(v.n), 256, 0, st>>>(v, geom(&g), ldexpf(1.0f, g.S), (unsigned long long*)grid, flags);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return noalloc_fail(err, err_len, EPB_ECUDA, std::string("k_scatter: ") + cudaGetErrorString(e));
+    }
+    int64_t blocks = (nbins + 255) / 256;
+    if (blocks > 4096) blocks = 4096;
+    k_fixed_to_density<<<(unsigned)blocks, 256, 0, st>>>(grid, init_norm, dscale, nbins, density);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return noalloc_fail(err, err_len, EPB_ECUDA, std::string("k_fixed_to_density: ") + cudaGetErrorString(e));
+    return EPB_OK;
+}

@@ -167,6 +167,31 @@ int epb_error_flags(epb_handle* h, epb_stream stream, uint32_t* flags);
 int epb_profile_start(epb_handle* h, int32_t max_calls);
 int epb_profile_stop(epb_handle* h, double* stage_ms, int32_t* stage_launches);
 
+/* Allocation-free density map.  This entry point has no counterpart in the
+ * reference; it exists for callers that cannot allocate device memory: code
+ * whose device memory is owned by another allocator (a framework's caching
+ * allocator or a fixed memory pool that must account for every byte), and
+ * code on a latency-critical path where cudaMalloc/cudaFree, which can
+ * synchronise the whole device, are not acceptable.
+ *
+ * It computes exactly the `density` output of epb_forward (fixed-point
+ * scatter, normalisation, plus the optional normalised initial density
+ * init_norm[M*N]) into the caller's density[M*N], without a handle.  The
+ * int64 accumulation grid lives in a fixed device array inside the library,
+ * EPB_NOALLOC_MAX_BINS bins (8 MiB), which every GPU that loads the library
+ * holds until the process exits.  Grids with M*N > EPB_NOALLOC_MAX_BINS are
+ * rejected with EPB_EINVAL and a message in err[err_len] (nullable).
+ * cfg->device selects the GPU; the first call on a device looks up the
+ * array's device address there, so make that first call before any stream
+ * capture.  All calls share the one array and clear it before use: calls that
+ * overlap on the GPU (different streams, or different host threads) race and
+ * corrupt each other's result; serialise them.  Non-finite cells are skipped;
+ * saturation is not reported by this entry point (use epb_error_flags on a
+ * handle for that). */
+#define EPB_NOALLOC_MAX_BINS (1024 * 1024)
+int epb_density_noalloc(const epb_config* cfg, const epb_cells* cells, const float* init_norm,
+                        epb_stream stream, float* density, char* err, int32_t err_len);
+
 #ifdef __cplusplus
 }
 #endif
