@@ -51,6 +51,19 @@ STAGE_BYTES = {
 }
 
 
+# DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of each
+# engine kernel on the c3 workload, from one ncu --set full capture of this
+# build (profiles/c3_step_kernels_full.md); ncu flushes caches per launch, so
+# these are cold-cache figures.
+NCU_TRAFFIC_C3 = {
+    "scatter": 72.8e6,
+    "row_fwd": 60.7e6,
+    "column": 19.4e6,
+    "row_inv": 90.2e6,
+    "gather": 80.1e6,
+}
+
+
 def algorithmic_bytes(stage, n_cells, bins):
     per_cell, per_bin = STAGE_BYTES[stage]
     return per_cell * n_cells + per_bin * bins
@@ -357,7 +370,8 @@ def main():
                           "gbs": b / avg_s / 1e9, "frac": b / avg_s / 1e9 / peak}
         dom = max(kern, key=lambda k: kern[k]["avg_us"])
         roof = {"bound": "hbm", "kernel": dom, "achieved": kern[dom]["gbs"], "peak": peak, "unit": "GB/s",
-                "frac": kern[dom]["frac"], "traffic": None, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"}
+                "frac": kern[dom]["frac"],
+                "traffic": NCU_TRAFFIC_C3.get(dom) if args.config == "c3" else None, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"}
         step_bytes = sum(algorithmic_bytes(k, p.num_cells, bins) for k in STAGE_BYTES)
         value = world * K / (total_ms / 1000.0)
         line = {

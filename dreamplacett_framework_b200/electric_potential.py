@@ -1,0 +1,238 @@
+"""DREAMPlace-compatible electric-potential operator on the B200 engine.
+
+`ElectricPotentialFunction` keeps DREAMPlace's argument list (the 35
+arguments after ctx that the reference's patched forward receives,
+integration/scatter_ttnn_client.py:553-574) and its semantics:
+
+* forward: density of movable + filler cells, where terminals are already in
+  `initial_density_map`; the DCT Poisson solve; fields saved in ctx; returns
+  the energy.  The reference returns 0 (client:860); this operator returns the
+  real energy sum(rho * phi), computed spectrally.
+* backward: per-node gradient -grad * ratio * sum(overlap * field) (DREAMPlace's
+  electric_force form), on the GPU, in `pos`'s [x | y] layout with zeros for
+  terminals.
+
+`ElectricPotential` is a module with DREAMPlace's constructor that prepares
+the stretched sizes, offsets, ratio and the initial density, for callers
+that do not have DREAMPlace.
+
+Inputs may live on the host or on a CUDA device; host tensors are copied to
+the engine's GPU and results are returned on the input's device.
+"""
+from __future__ import annotations
+
+import math
+import threading
+from typing import Dict, Optional, Tuple
+
+import torch
+
+from .engine import CellTensors, ElectricPotentialEngine
+
+_engines: Dict[tuple, ElectricPotentialEngine] = {}
+_engines_lock = threading.Lock()
+_static_cache: Dict[tuple, tuple] = {}
+
+
+def get_engine(num_bins_x, num_bins_y, xl, yl, xh, yh, device) -> ElectricPotentialEngine:
+    """One engine per grid geometry and device (the reference starts one
+    server per grid, integration/scatter_ttnn_client.py:780-784)."""
+    key = (int(num_bins_x), int(num_bins_y), float(xl), float(yl), float(xh), float(yh), device.index)
+    with _engines_lock:
+        eng = _engines.get(key)
+        if eng is None:
+            eng = ElectricPotentialEngine(num_bins_x, num_bins_y, xl, yl, xh, yh, device=device)
+            eng._init_key = None
+            _engines[key] = eng
+        return eng
+
+
+def release_engines():
+    with _engines_lock:
+        for e in _engines.values():
+            e.close()
+        _engines.clear()
+        _static_cache.clear()
+
+
+def engine_device(t: torch.Tensor) -> torch.device:
+    if t.is_cuda:
+        return t.device
+    if not torch.cuda.is_available():
+        raise RuntimeError("the B200 electric-potential operator needs a CUDA device (no CPU path)")
+    return torch.device("cuda", torch.cuda.current_device())
+
+
+def _on(t, dev):
+    """fp32 contiguous copy of t on dev (no copy when already there)."""
+    if t is None:
+        return None
+    return t.detach().to(device=dev, dtype=torch.float32).contiguous()
+
+
+def _static(t, dev):
+    """Device copy of a per-design buffer, re-uploaded only when the tensor changes."""
+    if t is None:
+        return None
+    if t.is_cuda and t.device == dev and t.dtype == torch.float32 and t.is_contiguous():
+        return t.detach()
+    key = (id(t), t.data_ptr(), t._version, tuple(t.shape), str(dev))
+    hit = _static_cache.get(id(t))
+    if hit is not None and hit[0] == key:
+        return hit[1]
+    d = _on(t, dev)
+    _static_cache[id(t)] = (key, d)
+    return d
+
+
+def node_cells(pos_dev, num_nodes, size_x, size_y, offset_x, offset_y, ratio, num_movable, num_filler):
+    """CellTensors over DREAMPlace's node layout [movable | terminals | fillers]."""
+    n = num_nodes
+    return CellTensors(pos_dev[:n], pos_dev[n:2 * n], size_x, size_y, offset_x, offset_y, ratio,
+                       ranges=((0, int(num_movable)), (n - int(num_filler), n)))
+
+
+class ElectricPotentialFunction(torch.autograd.Function):
+    """DREAMPlace ElectricPotentialFunction on the B200 engine."""
+
+    @staticmethod
+    def forward(ctx, pos,
+                node_size_x_clamped, node_size_y_clamped,
+                offset_x, offset_y, ratio,
+                bin_center_x, bin_center_y,
+                initial_density_map, target_density,
+                xl, yl, xh, yh,
+                bin_size_x, bin_size_y,
+                num_movable_nodes, num_filler_nodes,
+                padding, padding_mask,
+                num_bins_x, num_bins_y,
+                num_movable_impacted_bins_x, num_movable_impacted_bins_y,
+                num_filler_impacted_bins_x, num_filler_impacted_bins_y,
+                deterministic_flag, sorted_node_map,
+                exact_expkM=None, exact_expkN=None,
+                inv_wu2_plus_wv2=None,
+                wu_by_wu2_plus_wv2_half=None,
+                wv_by_wu2_plus_wv2_half=None,
+                dct2=None, idct2=None, idct_idxst=None, idxst_idct=None,
+                fast_mode=True):
+        dev = engine_device(pos)
+        eng = get_engine(num_bins_x, num_bins_y, xl, yl, xh, yh, dev)
+        num_nodes = pos.numel() // 2
+        pos_dev = _on(pos, dev)
+        sx = _static(node_size_x_clamped, dev)
+        sy = _static(node_size_y_clamped, dev)
+        ox = _static(offset_x, dev)
+        oy = _static(offset_y, dev)
+        r = _static(ratio, dev)
+        # initial (fixed-cell) density: normalised by bin area once, as the
+        # reference client uploads it (integration/scatter_ttnn_client.py:791-795)
+        if initial_density_map is not None:
+            ikey = (id(initial_density_map), initial_density_map._version, float(bin_size_x), float(bin_size_y))
+            if eng._init_key != ikey:
+                bin_area = float(bin_size_x) * float(bin_size_y)
+                eng.set_initial_density(_on(initial_density_map / bin_area, dev).reshape(-1))
+                eng._init_key = ikey
+        cells = node_cells(pos_dev, num_nodes, sx, sy, ox, oy, r, num_movable_nodes, num_filler_nodes)
+        out = eng.forward(cells, want_density=False, want_potential=False, want_fields=True, want_energy=True)
+        ctx.engine = eng
+        ctx.num_nodes = num_nodes
+        ctx.cells = (sx, sy, ox, oy, r, int(num_movable_nodes), int(num_filler_nodes))
+        ctx.pos_dev = pos_dev
+        ctx.pos_device = pos.device
+        ctx.pos_dtype = pos.dtype
+        # DREAMPlace's own backward reads these (scatter_ttnn_client.py:831-832)
+        ctx.field_map_x = out["field_x"] if pos.is_cuda else out["field_x"].to(pos.device)
+        ctx.field_map_y = out["field_y"] if pos.is_cuda else out["field_y"].to(pos.device)
+        ctx._fx_dev, ctx._fy_dev = out["field_x"], out["field_y"]
+        energy = out["energy"]
+        return energy.to(device=pos.device, dtype=pos.dtype)
+
+    @staticmethod
+    def backward(ctx, grad_energy):
+        eng = ctx.engine
+        n = ctx.num_nodes
+        sx, sy, ox, oy, r, nm, nf = ctx.cells
+        cells = node_cells(ctx.pos_dev, n, sx, sy, ox, oy, r, nm, nf)
+        dev = ctx.pos_dev.device
+        g = _on(grad_energy.reshape(1), dev)
+        grad = torch.zeros(2 * n, dtype=torch.float32, device=dev)
+        eng.gather(cells, ctx._fx_dev, ctx._fy_dev, grad_out=g, grad_x=grad[:n], grad_y=grad[n:])
+        grad = grad.to(device=ctx.pos_device, dtype=ctx.pos_dtype)
+        return (grad,) + (None,) * 37
+
+
+def stretch_nodes(node_size_x, node_size_y, bin_size_x, bin_size_y):
+    """DREAMPlace's clamp to sqrt(2) bins and area ratio
+    (tools/v13_offset_ratio_stats.py:54-67 of the reference restates it)."""
+    sqrt2 = math.sqrt(2.0)
+    sx_c = node_size_x.clamp(min=bin_size_x * sqrt2)
+    sy_c = node_size_y.clamp(min=bin_size_y * sqrt2)
+    offset_x = (node_size_x - sx_c).mul(0.5)
+    offset_y = (node_size_y - sy_c).mul(0.5)
+    ratio = (node_size_x * node_size_y) / (sx_c * sy_c)
+    return sx_c, sy_c, offset_x, offset_y, ratio
+
+
+class ElectricPotential(torch.nn.Module):
+    """DREAMPlace's ElectricPotential module interface on the B200 engine.
+
+    Nodes are ordered [movable | terminals | fillers].  Terminal (fixed)
+    cells are rasterised once into the initial density with their original
+    sizes and scaled by target_density; movable and filler cells are
+    stretched to sqrt(2) bins with their area kept through `ratio`."""
+
+    def __init__(self, node_size_x, node_size_y, bin_center_x, bin_center_y, target_density,
+                 xl, yl, xh, yh, bin_size_x, bin_size_y, num_movable_nodes, num_terminals,
+                 num_filler_nodes, padding=0, deterministic_flag=True, sorted_node_map=None,
+                 movable_macro_mask=None, fast_mode=False):
+        super().__init__()
+        self.node_size_x = node_size_x
+        self.node_size_y = node_size_y
+        self.bin_center_x, self.bin_center_y = bin_center_x, bin_center_y
+        self.target_density = float(target_density)
+        self.xl, self.yl, self.xh, self.yh = float(xl), float(yl), float(xh), float(yh)
+        self.bin_size_x, self.bin_size_y = float(bin_size_x), float(bin_size_y)
+        self.num_bins_x = int(round((self.xh - self.xl) / self.bin_size_x))
+        self.num_bins_y = int(round((self.yh - self.yl) / self.bin_size_y))
+        self.num_movable_nodes = int(num_movable_nodes)
+        self.num_terminals = int(num_terminals)
+        self.num_filler_nodes = int(num_filler_nodes)
+        self.padding = padding
+        self.deterministic_flag = deterministic_flag
+        self.sorted_node_map = sorted_node_map
+        self.fast_mode = fast_mode
+        (self.node_size_x_clamped, self.node_size_y_clamped, self.offset_x, self.offset_y,
+         self.ratio) = stretch_nodes(node_size_x, node_size_y, self.bin_size_x, self.bin_size_y)
+        if movable_macro_mask is not None and self.target_density < 1:
+            # movable macros keep target_density as their density scale
+            r = self.ratio.clone()
+            r[:self.num_movable_nodes][movable_macro_mask] = self.target_density
+            self.ratio = r
+        self.initial_density_map = None
+
+    def _initial_density(self, pos):
+        """Fixed-terminal overlap area per bin (area units), times target_density."""
+        n = pos.numel() // 2
+        dev = engine_device(pos)
+        M, N = self.num_bins_x, self.num_bins_y
+        if self.num_terminals == 0:
+            return torch.zeros(M, N, dtype=pos.dtype, device=pos.device)
+        eng = get_engine(M, N, self.xl, self.yl, self.xh, self.yh, dev)
+        t0, t1 = self.num_movable_nodes, self.num_movable_nodes + self.num_terminals
+        pos_dev = _on(pos, dev)
+        cells = CellTensors(pos_dev[:n], pos_dev[n:], _on(self.node_size_x, dev), _on(self.node_size_y, dev),
+                            ranges=((t0, t1), (0, 0)))
+        grid = eng.scatter_fixed(cells)
+        scale = math.ldexp(1.0, -eng.fixed_point_bits) * self.target_density
+        return (grid.to(torch.float64) * scale).to(dtype=pos.dtype, device=pos.device)
+
+    def forward(self, pos):
+        if self.initial_density_map is None:
+            self.initial_density_map = self._initial_density(pos)
+        return ElectricPotentialFunction.apply(
+            pos, self.node_size_x_clamped, self.node_size_y_clamped, self.offset_x, self.offset_y, self.ratio,
+            self.bin_center_x, self.bin_center_y, self.initial_density_map, self.target_density,
+            self.xl, self.yl, self.xh, self.yh, self.bin_size_x, self.bin_size_y,
+            self.num_movable_nodes, self.num_filler_nodes, self.padding, None,
+            self.num_bins_x, self.num_bins_y, 0, 0, 0, 0, self.deterministic_flag, self.sorted_node_map,
+            None, None, None, None, None, None, None, None, None, self.fast_mode)

@@ -1,0 +1,220 @@
+"""Drop-in replacement for the reference's integration/scatter_ttnn_client.py.
+
+Same public surface, no server process and no shared memory:
+
+* `ScatterTTNNClient(container, ipc_dir, num_bins_x, num_bins_y, nc_max, xl, yl, xh, yh, direct)`
+  with `start(M, N, nc_actual, xl, yl, xh, yh)`, `call(px, py, sx, sy) -> (field_x, field_y, timing)`,
+  `stop()` and `timing_summary(n_warmup)` (reference client:185-531).  `container`,
+  `ipc_dir` and `direct` are accepted and ignored: the engine runs in process.
+* `patch_dreamplace(container, ipc_dir, num_cells=0, direct=False)` replaces
+  DREAMPlace's `ElectricPotentialFunction.forward` (and its backward) with the
+  B200 operator (reference client:534-870).
+* `get_timing_summary()` and `teardown()` (reference client:873-881).
+
+`call` keeps the reference semantics (scatter_ttnn_client.py:411-509):
+px, py are lower-left corners, sx, sy the sizes used for binning, with no
+ratio.  The initial density set by `set_initial_density` (the reference's shm
+slot, client:263-266 and 786-795) is folded in before the solve.  field_x and
+field_y come back as torch tensors on the inputs' device, host for numpy
+inputs.  The timing dict has the reference's keys.  The shared-memory keys are
+0, and the TT stages are mapped to this engine's kernels:
+  scatter_ms      <- density scatter
+  gather_ms       <- density map + row DCT (the reference's accumulate / density write)
+  ttnn_compute_ms <- column pass + row inverses (the DCT solve)
+"""
+from __future__ import annotations
+
+import os
+import time
+from typing import Optional
+
+import numpy as np
+import torch
+
+from . import electric_potential as _ep
+from .engine import CellTensors, ElectricPotentialEngine
+
+_client: Optional["ScatterTTNNClient"] = None
+
+
+def _as_f32(a, dev):
+    if isinstance(a, torch.Tensor):
+        return a.detach().to(device=dev, dtype=torch.float32).contiguous()
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(dev)
+
+
+class ScatterTTNNClient:
+    def __init__(self, container: str = "", ipc_dir: str = "",
+                 num_bins_x: int = 0, num_bins_y: int = 0,
+                 nc_max: int = 0,
+                 xl: float = 0.0, yl: float = 0.0,
+                 xh: float = 1e6, yh: float = 1e6,
+                 direct: bool = False, device=None):
+        self.container = container
+        self.ipc_dir = ipc_dir
+        self.direct = direct
+        self.M = num_bins_x
+        self.N = num_bins_y
+        self.nc_max = nc_max
+        self.xl, self.yl, self.xh, self.yh = xl, yl, xh, yh
+        self.device = device
+        self._engine: Optional[ElectricPotentialEngine] = None
+        self._ready = False
+        self._timings: list = []
+        self._init_norm = None
+
+    # -- lifecycle (reference client:293-407) ------------------------------
+    def start(self, M: int = 0, N: int = 0, nc_actual: int = 0,
+              xl: float = 0.0, yl: float = 0.0, xh: float = 1e6, yh: float = 1e6) -> None:
+        if self._ready:
+            return
+        if M:
+            self.M = M
+        if N:
+            self.N = N
+        if xl or yl or xh != 1e6 or yh != 1e6:
+            self.xl, self.yl, self.xh, self.yh = xl, yl, xh, yh
+        if self.nc_max == 0:
+            if nc_actual == 0:
+                raise ValueError("nc_max=0 and no nc_actual supplied")
+            self.nc_max = nc_actual
+        dev = self.device
+        if dev is None:
+            if not torch.cuda.is_available():
+                raise RuntimeError("ScatterTTNNClient needs a CUDA device (no CPU path)")
+            dev = torch.device("cuda", torch.cuda.current_device())
+        self.device = torch.device(dev)
+        self._engine = ElectricPotentialEngine(self.M, self.N, self.xl, self.yl, self.xh, self.yh,
+                                               device=self.device)
+        if self._init_norm is not None:
+            self._engine.set_initial_density(self._init_norm)
+        self._ready = True
+
+    def stop(self) -> None:
+        if not self._ready:
+            return
+        self._engine.close()
+        self._engine = None
+        self._ready = False
+
+    def set_initial_density(self, init_norm) -> None:
+        """initial_density_map / bin_area, [M, N] (the reference's shm slot)."""
+        dev = self.device if self.device is not None else torch.device("cuda", torch.cuda.current_device())
+        self._init_norm = _as_f32(init_norm, dev).reshape(-1)
+        if self._engine is not None:
+            self._engine.set_initial_density(self._init_norm)
+
+    # -- per-iteration call (reference client:411-509) ----------------------
+    def call(self, px, py, sx, sy) -> tuple:
+        if not self._ready:
+            raise RuntimeError("ScatterTTNNClient.call before start()")
+        eng = self._engine
+        dev = self.device
+        host = not (isinstance(px, torch.Tensor) and px.is_cuda)
+        t0 = time.perf_counter()
+        x, y, w, h = (_as_f32(a, dev) for a in (px, py, sx, sy))
+        torch.cuda.synchronize(dev)
+        pos_write_ms = (time.perf_counter() - t0) * 1000
+        t0 = time.perf_counter()
+        eng.profile_start(1)
+        out = eng.forward(CellTensors(x, y, w, h), want_density=False, want_potential=False,
+                          want_fields=True, want_energy=False)
+        stages = eng.profile_stop()  # synchronises
+        kernel_wait_ms = (time.perf_counter() - t0) * 1000
+        t0 = time.perf_counter()
+        field_x, field_y = out["field_x"], out["field_y"]
+        if host:
+            field_x, field_y = field_x.cpu(), field_y.cpu()
+        field_read_ms = (time.perf_counter() - t0) * 1000
+        scatter = stages["scatter"][0]
+        dens = stages["row_fwd"][0]
+        dct = stages["column"][0] + stages["row_inv"][0]
+        timing = {
+            "pos_write_ms": pos_write_ms,
+            "kernel_wait_ms": kernel_wait_ms,
+            "field_read_ms": field_read_ms,
+            "h2d_ms": pos_write_ms,
+            "scatter_ms": scatter,
+            "gather_ms": dens,
+            "d2h_density_ms": 0.0,
+            "ttnn_upload_ms": 0.0,
+            "ttnn_compute_ms": dct,
+            "ttnn_download_ms": 0.0,
+            "fw_ms": 0.0,
+            "total_server_ms": scatter + dens + dct,
+            "total_client_ms": pos_write_ms + kernel_wait_ms + field_read_ms,
+            "gather_mode": "epb200",
+        }
+        self._timings.append(timing)
+        return field_x, field_y, timing
+
+    def timing_summary(self, n_warmup: int = 4) -> dict:
+        timings = self._timings[n_warmup:] if len(self._timings) > n_warmup else self._timings
+        if not timings:
+            timings = self._timings
+        if not timings:
+            return {}
+        result = {}
+        for k in timings[0].keys():
+            vals = [t[k] for t in timings if k in t]
+            if not vals:
+                continue
+            if isinstance(vals[0], (int, float)):
+                result[f"{k}_mean"] = float(np.mean(vals))
+                result[f"{k}_median"] = float(np.median(vals))
+            else:
+                result[k] = max(set(vals), key=vals.count)
+        result["n_iters"] = len(self._timings)
+        result["n_timed"] = len(timings)
+        return result
+
+
+def patch_dreamplace(container: str = "", ipc_dir: str = "", num_cells: int = 0,
+                     direct: bool = False) -> None:
+    """Replace DREAMPlace's ElectricPotentialFunction forward/backward with the
+    B200 operator (reference client:534-870).  V13_USE_CPU_AFTER_ITER keeps the
+    reference's cut-over back to DREAMPlace's own forward after N iterations."""
+    global _client
+    _client = ScatterTTNNClient(container=container, ipc_dir=ipc_dir, nc_max=num_cells, direct=direct)
+    import dreamplace.ops.electric_potential.electric_potential as ep_mod
+
+    fn_cls = ep_mod.ElectricPotentialFunction
+    orig_forward = fn_cls.forward.__func__ if hasattr(fn_cls.forward, "__func__") else fn_cls.forward
+    orig_backward = fn_cls.backward.__func__ if hasattr(fn_cls.backward, "__func__") else fn_cls.backward
+    counter = [0]
+
+    def _forward(ctx, pos, *args):
+        counter[0] += 1
+        try:
+            cpu_after = int(os.environ.get("V13_USE_CPU_AFTER_ITER", "0"))
+        except ValueError:
+            cpu_after = 0
+        if cpu_after > 0 and counter[0] > cpu_after:
+            ctx._epb = False
+            return orig_forward(ctx, pos, *args)
+        t0 = time.perf_counter()
+        energy = _ep.ElectricPotentialFunction.forward(ctx, pos, *args)
+        ctx._epb = True
+        _client._timings.append({"ep_total_ms": (time.perf_counter() - t0) * 1000, "gather_mode": "epb200"})
+        return energy
+
+    def _backward(ctx, grad_pos):
+        if getattr(ctx, "_epb", False):
+            return _ep.ElectricPotentialFunction.backward(ctx, grad_pos)
+        return orig_backward(ctx, grad_pos)
+
+    fn_cls.forward = staticmethod(_forward)
+    fn_cls.backward = staticmethod(_backward)
+    print("[epb200] Patched ElectricPotentialFunction.forward/backward -> B200 engine", flush=True)
+
+
+def get_timing_summary() -> dict:
+    if _client is None:
+        return {}
+    return _client.timing_summary()
+
+
+def teardown() -> None:
+    if _client is not None:
+        _client.stop()
+    _ep.release_engines()
