@@ -223,8 +223,141 @@ def workload_config(args, p):
         "cells": p.num_cells, "bins": [p.num_bins_x, p.num_bins_y],
         "density": "int64 fixed point (bit-exact), fp32 DCT/fields",
         "l2": "flushed between timed steps (write of 2x L2 size)",
-        "parallelism": "single" if args.gpus == 1 else f"replicas{args.gpus}",
+        "parallelism": "single" if args.gpus == 1 else
+        f"row-band shards x{args.gpus} (NCCL all-to-all transposes, fp64 energy all-reduce, field halo)",
     }
+
+
+def sharded_bytes(stage, n_cells, bins, P):
+    """Algorithmic bytes one rank moves per launch when the grid is split in P
+    row bands: every rank reads all cells for its band filter (scatter, gather),
+    grids are 1/P per rank."""
+    per_cell, per_bin = STAGE_BYTES[stage]
+    if stage == "gather":
+        return 28 * n_cells + 8 * n_cells // P + per_bin * bins // P
+    return per_cell * n_cells + per_bin * bins // P
+
+
+def run_sharded(args, p, dev, world, rank):
+    """One grid over `world` GPUs (strong scaling of the same workload)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from dreamplacett_framework_b200.engine import CellTensors
+    from dreamplacett_framework_b200.sharded import ShardedElectricPotential
+
+    to = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dev)
+    n = p.num_nodes
+    pos = torch.empty(2 * n, dtype=torch.float32, device=dev)
+    pos[:n].copy_(to(p.x))
+    pos[n:].copy_(to(p.y))
+    sx, sy, ox, oy, ratio = (to(a) for a in (p.size_x_clamped, p.size_y_clamped, p.offset_x, p.offset_y, p.ratio))
+    cells = CellTensors(pos[:n], pos[n:], sx, sy, ox, oy, ratio, ranges=p.ranges)
+    sh = ShardedElectricPotential(p.num_bins_x, p.num_bins_y, p.xl, p.yl, p.xh, p.yh,
+                                  float(p.size_x_clamped.max()), device=dev)
+    sh.set_initial_density(to(p.initial_density_norm()))
+    RB, N = sh.RB, p.num_bins_y
+    outs = {k: torch.empty((RB, N), dtype=torch.float32, device=dev)
+            for k in ("density", "potential", "field_x", "field_y")}
+    grad = torch.zeros(2 * n, dtype=torch.float32, device=dev)
+
+    def step():
+        sh.forward(cells, out=outs)
+        sh.backward(cells, grad_x=grad[:n], grad_y=grad[n:])
+
+    l2 = getattr(torch.cuda.get_device_properties(dev), "L2_cache_size", 126 * 2 ** 20)
+    flush = torch.empty(max(2 * l2, 256 * 2 ** 20) // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sampler = ClockSampler(gpu_smi_id(dev))
+    sampler.start()
+    time.sleep(0.5)
+    t_warm0 = time.perf_counter()
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    K = args.steps
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    sh.be.profile_start(4 * K)
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    for i in range(K):
+        flush.zero_()
+        ev[i][0].record(stream)
+        step()
+        ev[i][1].record(stream)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    t1 = time.perf_counter()
+    stages = sh.be.profile_stop()
+    total_ms = sum(a.elapsed_time(b) for a, b in ev)
+    clocks = sampler.summary(t0, t1)
+    if clocks["samples"] < 3:
+        clocks = sampler.summary(t_warm0, t1)
+        clocks["window"] = "warm-up and timed region"
+    # e2e: pinned host pos in, this rank's gradient array and the energy out
+    pos_host = torch.empty(2 * n, dtype=torch.float32).pin_memory()
+    pos_host.copy_(pos.cpu())
+    grad_host = torch.empty(2 * n, dtype=torch.float32).pin_memory()
+    energy_host = torch.empty(1, dtype=torch.float64).pin_memory()
+
+    def e2e_step():
+        pos.copy_(pos_host, non_blocking=True)
+        step()
+        grad_host.copy_(grad, non_blocking=True)
+        energy_host.copy_(sh.energy, non_blocking=True)
+
+    K_e2e = max(10, min(K, 200))
+    for _ in range(args.warmup):
+        e2e_step()
+    ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K_e2e)]
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    for i in range(K_e2e):
+        ev2[i][0].record(stream)
+        e2e_step()
+        ev2[i][1].record(stream)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    e2e_ms = sum(a.elapsed_time(b) for a, b in ev2)
+    sampler.stop()
+    flags = sh.be.error_flags()
+    vals = torch.tensor([total_ms, e2e_ms, float(flags)], dtype=torch.float64, device=dev)
+    dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    total_ms, e2e_ms, flags = float(vals[0]), float(vals[1]), int(vals[2])
+    if rank == 0:
+        peak, peak_kind = load_peaks()
+        bins = p.num_bins_x * p.num_bins_y
+        kern = {}
+        for name, (ms, cnt) in stages.items():
+            if cnt == 0:
+                continue
+            avg_s = ms / cnt / 1000.0
+            b = sharded_bytes(name, p.num_cells, bins, world)
+            kern[name] = {"avg_us": avg_s * 1e6, "launches": cnt, "bytes": b,
+                          "gbs": b / avg_s / 1e9, "frac": b / avg_s / 1e9 / peak}
+        dom = max(kern, key=lambda k: kern[k]["avg_us"])
+        kernel_us = sum(v["avg_us"] for v in kern.values())
+        line = {
+            "metric": METRIC, "value": K / (total_ms / 1000.0), "unit": UNIT, "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded stand-in for ISPD-2005 shapes)",
+            "config": workload_config(args, p),
+            "roofline": {"bound": "hbm", "kernel": dom, "achieved": kern[dom]["gbs"], "peak": peak, "unit": "GB/s",
+                         "frac": kern[dom]["frac"], "traffic": None,
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"},
+            "kernels": kern,
+            "exchange_us_per_step": 1000.0 * total_ms / K - kernel_us,
+            "e2e": {"value": K_e2e / (e2e_ms / 1000.0), "unit": UNIT, "steps": K_e2e,
+                    "h2d_bytes_per_step": world * 2 * n * 4, "d2h_bytes_per_step": world * (2 * n * 4 + 8),
+                    "path": "each rank: pinned pos[2n] H2D, sharded forward+backward, grad[2n] + energy D2H"},
+            "gpu_launches": 5 * K * world,
+            "clocks": clocks,
+            "error_flags": flags,
+            "wall_s_timed_region": t1 - t0,
+        }
+        print(json.dumps(line), flush=True)
+    sh.close()
 
 
 def main():
@@ -262,6 +395,13 @@ def main():
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    if world > 1:
+        try:
+            run_sharded(args, p, dev, world, rank)
+        finally:
+            dist.destroy_process_group()
+        return
 
     def barrier():
         if world > 1:

@@ -20,6 +20,7 @@ EPB_EOVERFLOW = 5
 EPB_ENOSTATE = 6
 EPB_FLAG_NONFINITE_CELL = 0x1
 EPB_FLAG_SATURATED = 0x2
+EPB_FLAG_HALO = 0x4
 
 # Every symbol include/epb.h declares (the CPU tests check the exports).
 EXPORTS = (
@@ -27,6 +28,8 @@ EXPORTS = (
     "epb_geometry", "epb_set_initial_density", "epb_forward", "epb_backward",
     "epb_scatter_fixed", "epb_dct_solve", "epb_gather", "epb_error_flags",
     "epb_profile_start", "epb_profile_stop", "epb_density_noalloc",
+    "epb_create_shard", "epb_shard_geometry", "epb_shard_rows_forward", "epb_shard_columns",
+    "epb_shard_rows_inverse", "epb_shard_gather",
 )
 
 # Largest grid (M*N bins) epb_density_noalloc accepts (EPB_NOALLOC_MAX_BINS).
@@ -97,6 +100,12 @@ def load():
     L.epb_profile_start.argtypes = [vp, i32]
     L.epb_profile_stop.argtypes = [vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(i32)]
     L.epb_density_noalloc.argtypes = [ctypes.POINTER(EpbConfig), cp, vp, vp, vp, ctypes.c_char_p, i32]
+    L.epb_create_shard.argtypes = [ctypes.POINTER(EpbConfig), i32, i32, ctypes.POINTER(vp)]
+    L.epb_shard_geometry.argtypes = [vp] + [ctypes.POINTER(i32)] * 4
+    L.epb_shard_rows_forward.argtypes = [vp, cp, vp, vp, vp]
+    L.epb_shard_columns.argtypes = [vp, vp, vp, vp, i32, vp]
+    L.epb_shard_rows_inverse.argtypes = [vp, vp, vp, vp, vp, vp, vp]
+    L.epb_shard_gather.argtypes = [vp, cp, vp, i32, vp, vp, vp, vp]
     for name in EXPORTS:
         if name not in ("epb_version", "epb_status_string", "epb_last_error"):
             getattr(L, name).restype = ctypes.c_int

@@ -22,19 +22,20 @@ using namespace epb;
 struct epb_handle {
     int dev = 0;
     int M = 0, N = 0;
+    // sharding: this handle is shard p of P; it owns rows [row0, row0+RB) and,
+    // in the column pass, columns [col0, col0+NB).  P = 1 for a whole grid.
+    int P = 1, p = 0, RB = 0, NB = 0, row0 = 0, col0 = 0;
     double xl = 0, yl = 0, xh = 0, yh = 0;
     float bsx = 0, bsy = 0;
     int S = 0;
     double dscale = 0;          // 2^-S / bin_area
-    long long* grid = nullptr;  // int64 [M*N], kept zeroed between forwards
+    long long* grid = nullptr;  // int64 [RB*N] (this band), kept zeroed between forwards
     bool grid_dirty = false;
-    float* init = nullptr;      // normalised initial density [M*N]
+    float* init = nullptr;      // normalised initial density of this band [RB*N]
     bool has_init = false;
-    float* t1 = nullptr;        // [M*N]
-    float* gx = nullptr;        // [M*N]
-    float* gy = nullptr;
-    float* gp = nullptr;
-    float2* fxy = nullptr;      // interleaved fields of the last forward
+    float* t1 = nullptr;        // [M*N] row-DCT output (P == 1 only; shards use the caller's buffers)
+    float* g = nullptr;         // [3*M*N] column-pass outputs (P == 1 only)
+    float2* fxy = nullptr;      // interleaved fields of the last forward (P == 1 only)
     bool have_fields = false;
     float2 *twM = nullptr, *qwM = nullptr, *twN = nullptr, *qwN = nullptr;
     double* partials = nullptr;
@@ -138,7 +139,7 @@ int dev_alloc(epb_handle* h, T** p, size_t count) {
 }
 
 void free_all(epb_handle* h) {
-    void* ptrs[] = {h->grid, h->init, h->t1, h->gx, h->gy, h->gp, h->fxy, h->twM, h->qwM,
+    void* ptrs[] = {h->grid, h->init, h->t1, h->g, h->fxy, h->twM, h->qwM,
                     h->twN, h->qwN, h->partials, h->counter, h->energy_d, h->flags};
     for (void* p : ptrs)
         if (p) cudaFree(p);
@@ -154,21 +155,32 @@ int set_smem(epb_handle* h, const void* fn, size_t bytes) {
     return EPB_OK;
 }
 
+int ilog2(int v) {
+    int l = 0;
+    while ((1 << l) < v) ++l;
+    return l;
+}
+
+// Row pass over this handle's RB rows: t1 receives the blocked layout (block
+// width NB, RB*NB elements per block); for P == 1 that is plain [M][N].
 template <int L>
-int launch_row_fwd_t(epb_handle* h, bool from_fixed, const float* rho_in, float* rho_out, cudaStream_t st) {
+int launch_row_fwd_t(epb_handle* h, bool from_fixed, const float* rho_in, float* rho_out, float* t1,
+                     cudaStream_t st) {
     using C = RowFwdCfg<L>;
-    const unsigned blocks = (unsigned)((h->M + C::ROWS - 1) / C::ROWS);
+    const unsigned blocks = (unsigned)((h->RB + C::ROWS - 1) / C::ROWS);
     const float* init = h->has_init && from_fixed ? h->init : nullptr;
+    const int lnb = ilog2(h->NB);
+    const int64_t tblock = (int64_t)h->RB * h->NB;
     if (from_fixed) {
         auto fn = k_row_fwd<L, true>;
         if (int rc = set_smem<L>(h, (const void*)fn, C::SMEM)) return rc;
-        fn<<<blocks, C::T, C::SMEM, st>>>(h->grid, nullptr, init, h->dscale, h->M, rho_out, h->t1,
-                                                h->twN, h->qwN, h->flags);
+        fn<<<blocks, C::T, C::SMEM, st>>>(h->grid, nullptr, init, h->dscale, h->RB, rho_out, t1, lnb, tblock,
+                                          h->twN, h->qwN, h->flags);
     } else {
         auto fn = k_row_fwd<L, false>;
         if (int rc = set_smem<L>(h, (const void*)fn, C::SMEM)) return rc;
-        fn<<<blocks, C::T, C::SMEM, st>>>(nullptr, rho_in, nullptr, h->dscale, h->M, rho_out, h->t1,
-                                                h->twN, h->qwN, h->flags);
+        fn<<<blocks, C::T, C::SMEM, st>>>(nullptr, rho_in, nullptr, h->dscale, h->RB, rho_out, t1, lnb, tblock,
+                                          h->twN, h->qwN, h->flags);
     }
     EPB_LAUNCHED(h, "k_row_fwd launch");
     return EPB_OK;
@@ -177,7 +189,7 @@ int launch_row_fwd_t(epb_handle* h, bool from_fixed, const float* rho_in, float*
 template <int L>
 int launch_col_t(epb_handle* h, const ColArgs& a, cudaStream_t st) {
     using C = ColCfg<L>;
-    const unsigned blocks = (unsigned)((h->N + C::W - 1) / C::W);
+    const unsigned blocks = (unsigned)((a.N + C::W - 1) / C::W);
     auto fn = k_col<L>;
     if (int rc = set_smem<L>(h, (const void*)fn, C::SMEM)) return rc;
     fn<<<blocks, C::T, C::SMEM, st>>>(a);
@@ -188,7 +200,7 @@ int launch_col_t(epb_handle* h, const ColArgs& a, cudaStream_t st) {
 template <int L>
 int launch_row_inv_t(epb_handle* h, const RowInvArgs& a, cudaStream_t st) {
     using C = RowInvCfg<L>;
-    const unsigned blocks = (unsigned)((h->M + C::ROWS - 1) / C::ROWS);
+    const unsigned blocks = (unsigned)((a.M + C::ROWS - 1) / C::ROWS);
     auto fn = k_row_inv<L>;
     if (int rc = set_smem<L>(h, (const void*)fn, C::SMEM)) return rc;
     fn<<<blocks, C::T, C::SMEM, st>>>(a);
@@ -210,8 +222,9 @@ int launch_row_inv_t(epb_handle* h, const RowInvArgs& a, cudaStream_t st) {
         default: return fail(h, EPB_EINVAL, "unsupported transform length"); \
     }
 
-int launch_row_fwd(epb_handle* h, bool from_fixed, const float* rho_in, float* rho_out, cudaStream_t st) {
-#define CALL_RF(L) launch_row_fwd_t<L>(h, from_fixed, rho_in, rho_out, st)
+int launch_row_fwd(epb_handle* h, bool from_fixed, const float* rho_in, float* rho_out, float* t1,
+                   cudaStream_t st) {
+#define CALL_RF(L) launch_row_fwd_t<L>(h, from_fixed, rho_in, rho_out, t1, st)
     EPB_DISPATCH_L(h->N, CALL_RF)
 #undef CALL_RF
 }
@@ -268,24 +281,46 @@ struct ProfCall {
     }
 };
 
-// DCT solve from the state in t1 (after the row-forward pass).
-int solve_from_t1(epb_handle* h, cudaStream_t st, float* potential, float* field_x, float* field_y,
-                  float* energy, ProfCall& pc) {
+// Column pass: t1 = column strip [M][NB] of this handle's column band; g =
+// outputs laid out g[d][o][r][c] (d destination row band).  The energy of the
+// strip (times MN/4) lands in h->energy_d and, when given, energy_out.
+int launch_columns(epb_handle* h, const float* t1, float* g, bool want_phi, float* energy_out, cudaStream_t st) {
     ColArgs ca;
-    ca.t1 = h->t1; ca.gx = h->gx; ca.gy = h->gy; ca.gp = h->gp;
+    ca.t1 = t1;
+    ca.g = g;
+    ca.ostride = (int64_t)h->RB * h->NB;
+    ca.dstride = 3 * (int64_t)h->RB * h->NB;
+    ca.lrb = ilog2(h->RB);
+    ca.col_base = h->col0;
     ca.ku = (float)(2.0 * M_PI / h->M);
     ca.kv = (float)(2.0 * M_PI / h->N * (double)(h->bsx / h->bsy));
     ca.tw = h->twM; ca.qw = h->qwM;
     ca.partials = h->partials; ca.counter = h->counter; ca.energy_d = h->energy_d;
-    ca.energy_out = energy; ca.N = h->N; ca.want_phi = potential != nullptr;
+    ca.energy_out = energy_out; ca.N = h->NB; ca.want_phi = want_phi;
     ca.energy_scale = (double)h->M * (double)h->N / 4.0;
-    if (int rc = launch_col(h, ca, st)) return rc;
-    pc.end_stage(EPB_STAGE_COLUMN);
+    return launch_col(h, ca, st);
+}
+
+// Row inverses of this handle's RB rows from g[q][o][r][c] (q source column band).
+int launch_rows_inverse(epb_handle* h, const float* g, float* potential, float* field_x, float* field_y,
+                        float2* fxy, bool want_phi, cudaStream_t st) {
     RowInvArgs ra;
-    ra.gx = h->gx; ra.gy = h->gy; ra.gp = h->gp;
-    ra.fx = field_x; ra.fy = field_y; ra.phi = potential; ra.fxy = h->fxy;
-    ra.tw = h->twN; ra.qw = h->qwN; ra.M = h->M; ra.want_phi = potential != nullptr;
-    if (int rc = launch_row_inv(h, ra, st)) return rc;
+    ra.g = g;
+    ra.ostride = (int64_t)h->RB * h->NB;
+    ra.qstride = 3 * (int64_t)h->RB * h->NB;
+    ra.lnb = ilog2(h->NB);
+    ra.fx = field_x; ra.fy = field_y; ra.phi = want_phi ? potential : nullptr; ra.fxy = fxy;
+    ra.tw = h->twN; ra.qw = h->qwN; ra.M = h->RB; ra.want_phi = want_phi;
+    return launch_row_inv(h, ra, st);
+}
+
+// DCT solve from the state in t1 (after the row-forward pass), single-grid handles.
+int solve_from_t1(epb_handle* h, cudaStream_t st, float* potential, float* field_x, float* field_y,
+                  float* energy, ProfCall& pc) {
+    const bool want_phi = potential != nullptr;
+    if (int rc = launch_columns(h, h->t1, h->g, want_phi, energy, st)) return rc;
+    pc.end_stage(EPB_STAGE_COLUMN);
+    if (int rc = launch_rows_inverse(h, h->g, potential, field_x, field_y, h->fxy, want_phi, st)) return rc;
     pc.end_stage(EPB_STAGE_ROW_INV);
     h->have_fields = true;
     return EPB_OK;
@@ -294,7 +329,8 @@ int solve_from_t1(epb_handle* h, cudaStream_t st, float* potential, float* field
 int scatter_into(epb_handle* h, const CellView& v, cudaStream_t st, long long* grid) {
     if (v.n == 0) return EPB_OK;
     const float qscale = ldexpf(1.0f, h->S);
-    k_scatter<<<cell_blocks(v.n), 256, 0, st>>>(v, geom(h), qscale, (unsigned long long*)grid, h->flags);
+    k_scatter<<<cell_blocks(v.n), 256, 0, st>>>(v, geom(h), qscale, (unsigned long long*)grid, h->row0,
+                                                h->row0 + h->RB, h->flags);
     EPB_LAUNCHED(h, "k_scatter launch");
     return EPB_OK;
 }
@@ -318,7 +354,12 @@ const char* epb_status_string(int s) {
     }
 }
 
-int epb_create(const epb_config* cfg, epb_handle** out) {
+}  // extern "C"
+
+namespace {
+
+// Shared by epb_create and epb_create_shard.
+int create_handle(const epb_config* cfg, int P, int p, epb_handle** out) {
     if (!out) return EPB_EINVAL;
     *out = nullptr;
     if (!cfg) return EPB_EINVAL;
@@ -327,9 +368,15 @@ int epb_create(const epb_config* cfg, epb_handle** out) {
         !std::isfinite(cfg->yl) || !std::isfinite(cfg->yh))
         return EPB_EINVAL;
     if (cfg->flags != 0 || cfg->fixed_point_bits > 60) return EPB_EINVAL;
+    // shards: P a power of two, each band at least 16 rows / columns
+    if (P < 1 || p < 0 || p >= P || (P & (P - 1)) != 0) return EPB_EINVAL;
+    if (cfg->num_bins_x / P < 16 || cfg->num_bins_y / P < 16) return EPB_EINVAL;
     epb_handle* h = new epb_handle();
     h->dev = cfg->device;
     h->M = cfg->num_bins_x; h->N = cfg->num_bins_y;
+    h->P = P; h->p = p;
+    h->RB = h->M / P; h->NB = h->N / P;
+    h->row0 = p * h->RB; h->col0 = p * h->NB;
     h->xl = cfg->xl; h->yl = cfg->yl; h->xh = cfg->xh; h->yh = cfg->yh;
     // fp32 bin sizes as the reference server computes them (host:411)
     h->bsx = ((float)cfg->xh - (float)cfg->xl) / (float)h->M;
@@ -347,15 +394,16 @@ int epb_create(const epb_config* cfg, epb_handle** out) {
     DeviceGuard guard(h->dev);
     if (!guard.ok) { delete h; return EPB_ECUDA; }
     const size_t MN = (size_t)h->M * h->N;
+    const size_t band = (size_t)h->RB * h->N;
     int rc = EPB_OK;
     const int ncolb = col_blocks(h->M, h->N);
-    if (!rc) rc = dev_alloc(h, &h->grid, MN);
-    if (!rc) rc = dev_alloc(h, &h->init, MN);
-    if (!rc) rc = dev_alloc(h, &h->t1, MN);
-    if (!rc) rc = dev_alloc(h, &h->gx, MN);
-    if (!rc) rc = dev_alloc(h, &h->gy, MN);
-    if (!rc) rc = dev_alloc(h, &h->gp, MN);
-    if (!rc) rc = dev_alloc(h, &h->fxy, MN);
+    if (!rc) rc = dev_alloc(h, &h->grid, band);
+    if (!rc) rc = dev_alloc(h, &h->init, band);
+    if (P == 1) {
+        if (!rc) rc = dev_alloc(h, &h->t1, MN);
+        if (!rc) rc = dev_alloc(h, &h->g, 3 * MN);
+        if (!rc) rc = dev_alloc(h, &h->fxy, MN);
+    }
     if (!rc) rc = dev_alloc(h, &h->twM, (size_t)h->M);
     if (!rc) rc = dev_alloc(h, &h->qwM, (size_t)h->M);
     if (!rc) rc = dev_alloc(h, &h->twN, (size_t)h->N);
@@ -374,7 +422,7 @@ int epb_create(const epb_config* cfg, epb_handle** out) {
     host_tables(h->N, tw, qw);
     if (e == cudaSuccess) e = cudaMemcpy(h->twN, tw.data(), tw.size() * sizeof(float2), cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemcpy(h->qwN, qw.data(), qw.size() * sizeof(float2), cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = cudaMemset(h->grid, 0, MN * sizeof(long long));
+    if (e == cudaSuccess) e = cudaMemset(h->grid, 0, band * sizeof(long long));
     if (e == cudaSuccess) e = cudaMemset(h->counter, 0, sizeof(unsigned));
     if (e == cudaSuccess) e = cudaMemset(h->flags, 0, sizeof(unsigned));
     if (e == cudaSuccess) e = cudaMemset(h->energy_d, 0, sizeof(double));
@@ -382,6 +430,22 @@ int epb_create(const epb_config* cfg, epb_handle** out) {
     if (e != cudaSuccess) { free_all(h); delete h; return EPB_ECUDA; }
     *out = h;
     return EPB_OK;
+}
+
+int whole_grid_only(epb_handle* h) {
+    if (h->P != 1) return fail(h, EPB_EINVAL, "this entry point needs a whole-grid handle (epb_create); "
+                                              "use the epb_shard_* stages on a shard handle");
+    return EPB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int epb_create(const epb_config* cfg, epb_handle** out) { return create_handle(cfg, 1, 0, out); }
+
+int epb_create_shard(const epb_config* cfg, int32_t num_shards, int32_t shard, epb_handle** out) {
+    return create_handle(cfg, num_shards, shard, out);
 }
 
 int epb_destroy(epb_handle* h) {
@@ -409,7 +473,8 @@ int epb_set_initial_density(epb_handle* h, const float* init_norm, epb_stream st
     if (!h) return EPB_EINVAL;
     DeviceGuard guard(h->dev);
     if (!init_norm) { h->has_init = false; return EPB_OK; }
-    EPB_CUDA(h, cudaMemcpyAsync(h->init, init_norm, (size_t)h->M * h->N * sizeof(float),
+    // a shard keeps only its own rows of the [M][N] map
+    EPB_CUDA(h, cudaMemcpyAsync(h->init, init_norm + (size_t)h->row0 * h->N, (size_t)h->RB * h->N * sizeof(float),
                                 cudaMemcpyDeviceToDevice, (cudaStream_t)stream));
     h->has_init = true;
     return EPB_OK;
@@ -418,6 +483,7 @@ int epb_set_initial_density(epb_handle* h, const float* init_norm, epb_stream st
 int epb_forward(epb_handle* h, const epb_cells* cells, epb_stream stream, float* density, float* potential,
                 float* field_x, float* field_y, float* energy) {
     if (!h) return EPB_EINVAL;
+    if (int rc = whole_grid_only(h)) return rc;
     CellView v;
     if (int rc = make_view(h, cells, v)) return rc;
     DeviceGuard guard(h->dev);
@@ -431,7 +497,7 @@ int epb_forward(epb_handle* h, const epb_cells* cells, epb_stream stream, float*
     pc.begin();
     if (int rc = scatter_into(h, v, st, h->grid)) return rc;
     pc.end_stage(EPB_STAGE_SCATTER);
-    if (int rc = launch_row_fwd(h, true, nullptr, density, st)) return rc;
+    if (int rc = launch_row_fwd(h, true, nullptr, density, h->t1, st)) return rc;
     pc.end_stage(EPB_STAGE_ROW_FWD);
     h->grid_dirty = false;
     return solve_from_t1(h, st, potential, field_x, field_y, energy, pc);
@@ -440,6 +506,7 @@ int epb_forward(epb_handle* h, const epb_cells* cells, epb_stream stream, float*
 int epb_backward(epb_handle* h, const epb_cells* cells, const float* grad_out, epb_stream stream,
                  float* grad_x, float* grad_y) {
     if (!h) return EPB_EINVAL;
+    if (int rc = whole_grid_only(h)) return rc;
     if (!h->have_fields) return fail(h, EPB_ENOSTATE, "epb_backward before epb_forward");
     CellView v;
     if (int rc = make_view(h, cells, v)) return rc;
@@ -448,8 +515,8 @@ int epb_backward(epb_handle* h, const epb_cells* cells, const float* grad_out, e
     DeviceGuard guard(h->dev);
     ProfCall pc(h, (cudaStream_t)stream);
     pc.begin();
-    k_gather<<<cell_blocks(v.n), 256, 0, (cudaStream_t)stream>>>(v, geom(h), h->fxy, nullptr, nullptr, grad_out,
-                                                               grad_x, grad_y, h->flags);
+    k_gather<<<cell_blocks(v.n), 256, 0, (cudaStream_t)stream>>>(v, geom(h), h->fxy, nullptr, nullptr, 0, h->M, 0, 0,
+                                                               grad_out, grad_x, grad_y, h->flags);
     EPB_LAUNCHED(h, "k_gather launch");
     pc.end_stage(EPB_STAGE_GATHER);
     return EPB_OK;
@@ -457,6 +524,7 @@ int epb_backward(epb_handle* h, const epb_cells* cells, const float* grad_out, e
 
 int epb_scatter_fixed(epb_handle* h, const epb_cells* cells, epb_stream stream, int64_t* grid) {
     if (!h) return EPB_EINVAL;
+    if (int rc = whole_grid_only(h)) return rc;
     if (!grid) return fail(h, EPB_EINVAL, "grid is NULL");
     CellView v;
     if (int rc = make_view(h, cells, v)) return rc;
@@ -473,12 +541,13 @@ int epb_scatter_fixed(epb_handle* h, const epb_cells* cells, epb_stream stream, 
 int epb_dct_solve(epb_handle* h, const float* density, epb_stream stream, float* potential, float* field_x,
                   float* field_y, float* energy) {
     if (!h) return EPB_EINVAL;
+    if (int rc = whole_grid_only(h)) return rc;
     if (!density) return fail(h, EPB_EINVAL, "density is NULL");
     DeviceGuard guard(h->dev);
     cudaStream_t st = (cudaStream_t)stream;
     ProfCall pc(h, st);
     pc.begin();
-    if (int rc = launch_row_fwd(h, false, density, nullptr, st)) return rc;
+    if (int rc = launch_row_fwd(h, false, density, nullptr, h->t1, st)) return rc;
     pc.end_stage(EPB_STAGE_ROW_FWD);
     return solve_from_t1(h, st, potential, field_x, field_y, energy, pc);
 }
@@ -486,14 +555,15 @@ int epb_dct_solve(epb_handle* h, const float* density, epb_stream stream, float*
 int epb_gather(epb_handle* h, const epb_cells* cells, const float* field_x, const float* field_y,
                const float* grad_out, epb_stream stream, float* grad_x, float* grad_y) {
     if (!h) return EPB_EINVAL;
+    if (int rc = whole_grid_only(h)) return rc;
     if (!field_x || !field_y) return fail(h, EPB_EINVAL, "field maps must be non-NULL");
     CellView v;
     if (int rc = make_view(h, cells, v)) return rc;
     if (v.n > 0 && (!grad_x || !grad_y)) return fail(h, EPB_EINVAL, "grad_x/grad_y must be non-NULL");
     if (v.n == 0) return EPB_OK;
     DeviceGuard guard(h->dev);
-    k_gather<<<cell_blocks(v.n), 256, 0, (cudaStream_t)stream>>>(v, geom(h), nullptr, field_x, field_y, grad_out,
-                                                               grad_x, grad_y, h->flags);
+    k_gather<<<cell_blocks(v.n), 256, 0, (cudaStream_t)stream>>>(v, geom(h), nullptr, field_x, field_y, 0, h->M, 0, 0,
+                                                               grad_out, grad_x, grad_y, h->flags);
     EPB_LAUNCHED(h, "k_gather launch");
     return EPB_OK;
 }
@@ -509,6 +579,91 @@ int epb_error_flags(epb_handle* h, epb_stream stream, uint32_t* flags) {
     EPB_CUDA(h, cudaStreamSynchronize(st));
     if (flags) *flags = f;
     if (f & EPB_FLAG_SATURATED) return fail(h, EPB_EOVERFLOW, "fixed-point density saturated");
+    return EPB_OK;
+}
+
+int epb_shard_geometry(const epb_handle* h, int32_t* num_shards, int32_t* shard, int32_t* rows_per_band,
+                       int32_t* cols_per_band) {
+    if (!h) return EPB_EINVAL;
+    if (num_shards) *num_shards = h->P;
+    if (shard) *shard = h->p;
+    if (rows_per_band) *rows_per_band = h->RB;
+    if (cols_per_band) *cols_per_band = h->NB;
+    return EPB_OK;
+}
+
+int epb_shard_rows_forward(epb_handle* h, const epb_cells* cells, epb_stream stream, float* density_band,
+                           float* t1_send) {
+    if (!h) return EPB_EINVAL;
+    if (!t1_send) return fail(h, EPB_EINVAL, "t1_send is NULL");
+    CellView v;
+    if (int rc = make_view(h, cells, v)) return rc;
+    DeviceGuard guard(h->dev);
+    cudaStream_t st = (cudaStream_t)stream;
+    if (h->grid_dirty) {
+        EPB_CUDA(h, cudaMemsetAsync(h->grid, 0, (size_t)h->RB * h->N * sizeof(long long), st));
+        h->grid_dirty = false;
+    }
+    h->grid_dirty = true;
+    ProfCall pc(h, st);
+    pc.begin();
+    if (int rc = scatter_into(h, v, st, h->grid)) return rc;
+    pc.end_stage(EPB_STAGE_SCATTER);
+    if (int rc = launch_row_fwd(h, true, nullptr, density_band, t1_send, st)) return rc;
+    pc.end_stage(EPB_STAGE_ROW_FWD);
+    h->grid_dirty = false;
+    return EPB_OK;
+}
+
+int epb_shard_columns(epb_handle* h, const float* t1_recv, epb_stream stream, float* g_send, int32_t want_potential,
+                      double* energy_partial) {
+    if (!h) return EPB_EINVAL;
+    if (!t1_recv || !g_send) return fail(h, EPB_EINVAL, "t1_recv and g_send must be non-NULL");
+    DeviceGuard guard(h->dev);
+    cudaStream_t st = (cudaStream_t)stream;
+    ProfCall pc(h, st);
+    pc.begin();
+    if (int rc = launch_columns(h, t1_recv, g_send, want_potential != 0, nullptr, st)) return rc;
+    pc.end_stage(EPB_STAGE_COLUMN);
+    if (energy_partial)
+        EPB_CUDA(h, cudaMemcpyAsync(energy_partial, h->energy_d, sizeof(double), cudaMemcpyDeviceToDevice, st));
+    return EPB_OK;
+}
+
+int epb_shard_rows_inverse(epb_handle* h, const float* g_recv, epb_stream stream, float* potential_band,
+                           float* field_x_band, float* field_y_band, float* fxy_band) {
+    if (!h) return EPB_EINVAL;
+    if (!g_recv || !fxy_band) return fail(h, EPB_EINVAL, "g_recv and fxy_band must be non-NULL");
+    DeviceGuard guard(h->dev);
+    cudaStream_t st = (cudaStream_t)stream;
+    ProfCall pc(h, st);
+    pc.begin();
+    if (int rc = launch_rows_inverse(h, g_recv, potential_band, field_x_band, field_y_band,
+                                     reinterpret_cast<float2*>(fxy_band), potential_band != nullptr, st))
+        return rc;
+    pc.end_stage(EPB_STAGE_ROW_INV);
+    return EPB_OK;
+}
+
+int epb_shard_gather(epb_handle* h, const epb_cells* cells, const float* fxy_ext, int32_t halo_rows,
+                     const float* grad_out, epb_stream stream, float* grad_x, float* grad_y) {
+    if (!h) return EPB_EINVAL;
+    if (!fxy_ext) return fail(h, EPB_EINVAL, "fxy_ext is NULL");
+    if (halo_rows < 0 || h->row0 + h->RB + halo_rows > h->M)
+        return fail(h, EPB_EINVAL, "halo_rows must keep the extended band inside the grid");
+    CellView v;
+    if (int rc = make_view(h, cells, v)) return rc;
+    if (v.n > 0 && (!grad_x || !grad_y)) return fail(h, EPB_EINVAL, "grad_x/grad_y must be non-NULL");
+    if (v.n == 0) return EPB_OK;
+    DeviceGuard guard(h->dev);
+    cudaStream_t st = (cudaStream_t)stream;
+    ProfCall pc(h, st);
+    pc.begin();
+    k_gather<<<cell_blocks(v.n), 256, 0, st>>>(v, geom(h), reinterpret_cast<const float2*>(fxy_ext), nullptr, nullptr,
+                                                h->row0, h->row0 + h->RB, halo_rows, 1, grad_out, grad_x, grad_y,
+                                                h->flags);
+    EPB_LAUNCHED(h, "k_gather launch");
+    pc.end_stage(EPB_STAGE_GATHER);
     return EPB_OK;
 }
 
@@ -660,7 +815,8 @@ extern "C" int epb_density_noalloc(const epb_config* cfg, const epb_cells* cells
     cudaError_t e = cudaMemsetAsync(grid, 0, (size_t)(nbins + 32) * sizeof(long long), st);
     if (e != cudaSuccess) return noalloc_fail(err, err_len, EPB_ECUDA, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
     if (v.n > 0) {
-        k_scatter<<<cell_blocks(v.n), 256, 0, st>>>(v, geom(&g), ldexpf(1.0f, g.S), (unsigned long long*)grid, flags);
+        k_scatter<<<cell_blocks(v.n), 256, 0, st>>>(v, geom(&g), ldexpf(1.0f, g.S), (unsigned long long*)grid, 0, g.M,
+                                                    flags);
         e = cudaGetLastError();
         if (e != cudaSuccess) return noalloc_fail(err, err_len, EPB_ECUDA, std::string("k_scatter: ") + cudaGetErrorString(e));
     }

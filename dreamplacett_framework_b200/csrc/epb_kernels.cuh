@@ -12,6 +12,17 @@
 // Grid layout: [M rows = x bins][N columns = y bins], row-major, index bx*N+by
 // (the reference's density layout, host/density_scatter_ttnn_server_host.cpp:458-459).
 //
+// Sharding: with P GPUs, GPU p owns the row band [p*M/P, (p+1)*M/P) and, for the
+// column pass, the column band [p*N/P, (p+1)*N/P).  The kernels take the band
+// and the layouts of the exchanged buffers as arguments; P = 1 is the
+// single-GPU case of the same code.  Exchanged layouts (NB = N/P, RB = M/P):
+//   T1 (row pass -> column pass): block q (destination) = rows of my band, columns of
+//       band q: t1[q][r][c], r < RB, c < NB; after the all-to-all GPU q holds its
+//       column strip as [M][NB] (source bands stacked in row order).
+//   G (column pass -> row pass): g[d][o][r][c]: destination band d, output o
+//       (0 = field_x form, 1 = field_y form, 2 = potential form), band row r, local
+//       column c; after the all-to-all GPU d holds g[q][o][r][c] from each source q.
+//
 // Transform conventions follow the reference's matrices
 // (host/density_scatter_ttnn_server_host.cpp:124-181):
 //   DCT2[k,n]  = (2/L) cos(pi k (n+1/2)/L)
@@ -31,23 +42,26 @@ namespace epb {
 
 constexpr unsigned kFlagNonFinite = 0x1u;
 constexpr unsigned kFlagSaturated = 0x2u;
+constexpr unsigned kFlagHalo = 0x4u;       // a gathered footprint reached past the field halo
 
 // ---------------------------------------------------------------------------
 // Scatter
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256)
 k_scatter(CellView c, GridGeom g, float qscale, unsigned long long* __restrict__ grid,
-          unsigned* __restrict__ flags) {
+          int row0, int row1, unsigned* __restrict__ flags) {
+    // grid holds rows [row0, row1) of the density grid; footprints are clipped to them
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < c.n; i += stride) {
         Footprint f;
         const int st = cell_footprint(c, g, cell_node(c, i), f);
         if (st < 0) { atomicOr(flags, kFlagNonFinite); continue; }
         if (st == 0) continue;
-        for (int kx = f.kx0; kx <= f.kx1; ++kx) {
+        const int kxa = max(f.kx0, row0), kxb = min(f.kx1, row1 - 1);
+        for (int kx = kxa; kx <= kxb; ++kx) {
             const float oxr = __fmul_rn(bin_overlap(f.x, f.ex, g.xl, g.bsx, kx), f.r);
             if (oxr == 0.0f) continue;
-            unsigned long long* row = grid + (int64_t)kx * g.N;
+            unsigned long long* row = grid + (int64_t)(kx - row0) * g.N;
             for (int ky = f.ky0; ky <= f.ky1; ++ky) {
                 const float a = __fmul_rn(oxr, bin_overlap(f.y, f.ey, g.yl, g.bsy, ky));
                 const long long q = __float2ll_rn(__fmul_rn(a, qscale));
@@ -79,7 +93,8 @@ k_row_fwd(long long* __restrict__ qgrid,            // FROM_FIXED: [M][L] int64 
           const float* __restrict__ init,           // nullable [M][L]
           double dscale, int M,
           float* __restrict__ rho_out,              // nullable
-          float* __restrict__ t1,                   // [M][L]
+          float* __restrict__ t1,                   // blocked: t1[k >> lnb][row][k & (nb-1)]
+          int lnb, int64_t tblock,                  // log2 block width, elements per block
           const float2* __restrict__ tw, const float2* __restrict__ qw,
           unsigned* __restrict__ flags) {
     using C = RowFwdCfg<L>;
@@ -129,8 +144,10 @@ k_row_fwd(long long* __restrict__ qgrid,            // FROM_FIXED: [M][L] int64 
         const float2 Vb = make_float2(0.5f * (Z.y + Zr.y), -0.5f * (Z.x - Zr.x));
         const float2 q = __ldg(qw + k);  // (cos, sin)(pi k / 2L)
         const int ra = row0 + 2 * s;
-        if (ra < M) t1[(int64_t)ra * L + k] = scale * (Va.x * q.x + Va.y * q.y);
-        if (ra + 1 < M) t1[(int64_t)(ra + 1) * L + k] = scale * (Vb.x * q.x + Vb.y * q.y);
+        const int nb = 1 << lnb;
+        float* tb = t1 + (int64_t)(k >> lnb) * tblock + (k & (nb - 1));
+        if (ra < M) tb[(int64_t)ra * nb] = scale * (Va.x * q.x + Va.y * q.y);
+        if (ra + 1 < M) tb[(int64_t)(ra + 1) * nb] = scale * (Vb.x * q.x + Vb.y * q.y);
     }
     if (FROM_FIXED) {
         // leave this CTA's rows of the grid zeroed for the next scatter
@@ -154,10 +171,13 @@ struct ColCfg {
 };
 
 struct ColArgs {
-    const float* t1;        // [M][N]
-    float* gx;              // [M][N] (2 IDXST_M)(auv*wu)
-    float* gy;              // [M][N] (2 IDCT_M)(auv*wv)
-    float* gp;              // [M][N] IDCT_M(auv*inv)   (only when want_phi)
+    const float* t1;        // column strip [M][N] (N = local strip width, the row stride)
+    float* g;               // outputs g[d][o][r][c]: o = 0 (2 IDXST_M)(auv*wu), 1 (2 IDCT_M)(auv*wv),
+                            //   2 IDCT_M(auv*inv) (only when want_phi)
+    int64_t ostride;        // elements between outputs o
+    int64_t dstride;        // elements between destination bands d
+    int lrb;                // log2 rows per destination band
+    int col_base;           // global index of local column 0
     float ku;               // wu = u * ku,  ku = 2 pi / M
     float kv;               // wv = v * kv,  kv = 2 pi / N * bsx / bsy
     const float2* tw;       // FFT twiddles, length M
@@ -246,11 +266,12 @@ k_col(ColArgs a) {
         for (int p = 0; p < 2; ++p) {
             const int col = c0 + 2 * s + p;
             if (col < N) {
-                const float wv = (float)col * a.kv;
+                const int gcol = a.col_base + col;
+                const float wv = (float)gcol * a.kv;
                 float wuh, wvh, inv;
                 spectral_weights(wu, wv, wuh, wvh, inv);
                 const double x = p ? xb : xa;
-                esum += cu * (col == 0 ? 1.0 : 2.0) * (double)inv * x * x;
+                esum += cu * (gcol == 0 ? 1.0 : 2.0) * (double)inv * x * x;
             }
         }
     }
@@ -267,7 +288,7 @@ k_col(ColArgs a) {
 #pragma unroll
             for (int p = 0; p < 2; ++p) {
                 const int cl = 2 * s + p;
-                const float wv = (float)(c0 + cl) * a.kv;
+                const float wv = (float)(a.col_base + c0 + cl) * a.kv;
                 const float* au = auv + cl * L;
                 if (r == 0) {
                     // b_n = a_{L-n}, b_0 = b_L = 0, a_u = auv_u * wu_half(u)
@@ -288,7 +309,7 @@ k_col(ColArgs a) {
 #pragma unroll
                 for (int p = 0; p < 2; ++p) {
                     const int cl = 2 * s + p;
-                    const float wv = (float)(c0 + cl) * a.kv;
+                    const float wv = (float)(a.col_base + c0 + cl) * a.kv;
                     h[p] = auv[cl * L + L / 2] * col_weight(r, (float)(L / 2) * a.ku, wv);
                 }
                 sq[pidx(L / 2)] = idct_pre(h[0], h[0], h[1], h[1], __ldg(a.qw + L / 2));
@@ -296,7 +317,8 @@ k_col(ColArgs a) {
         }
         __syncthreads();
         fft_seq<L, true>(myseq, lane, a.tw);
-        float* out = r == 0 ? a.gx : (r == 1 ? a.gy : a.gp);
+        float* out = a.g + (int64_t)r * a.ostride;
+        const int rbm = (1 << a.lrb) - 1;
 #pragma unroll 4
         for (int e = threadIdx.x; e < L * (W / 4); e += T) {
             const int k = e / (W / 4), q4 = e % (W / 4);
@@ -306,7 +328,8 @@ k_col(ColArgs a) {
             float2 v1 = buf[(2 * q4 + 1) * LP + src];
             if (r == 0 && (k & 1)) { v0.x = -v0.x; v0.y = -v0.y; v1.x = -v1.x; v1.y = -v1.y; }
             if (col < N)
-                *reinterpret_cast<float4*>(out + (int64_t)k * N + col) = make_float4(v0.x, v0.y, v1.x, v1.y);
+                *reinterpret_cast<float4*>(out + (int64_t)(k >> a.lrb) * a.dstride + (int64_t)(k & rbm) * N + col) =
+                    make_float4(v0.x, v0.y, v1.x, v1.y);
         }
         __syncthreads();
     }
@@ -362,13 +385,22 @@ struct RowInvCfg {
 };
 
 struct RowInvArgs {
-    const float* gx; const float* gy; const float* gp;  // [M][N]
-    float* fx; float* fy; float* phi;                   // nullable outputs
-    float2* fxy;                                        // interleaved fields [M][N]
+    const float* g;          // g[q][o][r][c] from every source band q (see the layout note at the top)
+    int64_t ostride;         // elements between outputs o
+    int64_t qstride;         // elements between source bands q
+    int lnb;                 // log2 columns per band
+    float* fx; float* fy; float* phi;                   // nullable outputs, [M][N] of this band
+    float2* fxy;                                        // interleaved fields [M][N] of this band
     const float2* tw; const float2* qw;                 // length N
-    int M;
+    int M;                   // rows in this band
     int want_phi;
 };
+
+// element l of band row r of column-pass output o
+__device__ __forceinline__ float rowinv_load(const RowInvArgs& a, int o, int r, int l) {
+    const int nb = 1 << a.lnb;
+    return __ldg(a.g + (int64_t)(l >> a.lnb) * a.qstride + (int64_t)o * a.ostride + (int64_t)r * nb + (l & (nb - 1)));
+}
 
 template <int L>
 __global__ void __launch_bounds__(RowInvCfg<L>::T, RowInvCfg<L>::MINB)
@@ -388,25 +420,22 @@ k_row_inv(RowInvArgs a) {
         if (s < ROWS) {
             const int row = row0 + s;
             if (row < a.M) {
-                const float* gxr = a.gx + (int64_t)row * L;
-                const float* gyr = a.gy + (int64_t)row * L;
                 // fx: IDCT of the Gx row; fy: IDXST of the Gy row = IDCT of b (b_0 = 0,
                 // b_m = a_{L-m}) with the 1/2 folded in
-                An[0] = __ldg(gxr + n);
-                Am[0] = n == 0 ? 0.0f : __ldg(gxr + nm);
-                An[1] = n == 0 ? 0.0f : 0.5f * __ldg(gyr + nm);
-                Am[1] = n == 0 ? 0.0f : 0.5f * __ldg(gyr + n);
-                if (n == 0) { Ah[0] = __ldg(gxr + h); Ah[1] = 0.5f * __ldg(gyr + h); }
+                An[0] = rowinv_load(a, 0, row, n);
+                Am[0] = n == 0 ? 0.0f : rowinv_load(a, 0, row, nm);
+                An[1] = n == 0 ? 0.0f : 0.5f * rowinv_load(a, 1, row, nm);
+                Am[1] = n == 0 ? 0.0f : 0.5f * rowinv_load(a, 1, row, n);
+                if (n == 0) { Ah[0] = rowinv_load(a, 0, row, h); Ah[1] = 0.5f * rowinv_load(a, 1, row, h); }
             }
         } else if (a.want_phi) {
             const int row = row0 + 2 * (s - ROWS);
 #pragma unroll
             for (int p = 0; p < 2; ++p) {
                 if (row + p < a.M) {
-                    const float* gpr = a.gp + (int64_t)(row + p) * L;
-                    An[p] = __ldg(gpr + n);
-                    Am[p] = n == 0 ? 0.0f : __ldg(gpr + nm);
-                    if (n == 0) Ah[p] = __ldg(gpr + h);
+                    An[p] = rowinv_load(a, 2, row + p, n);
+                    Am[p] = n == 0 ? 0.0f : rowinv_load(a, 2, row + p, nm);
+                    if (n == 0) Ah[p] = rowinv_load(a, 2, row + p, h);
                 }
             }
         }
@@ -445,8 +474,12 @@ k_row_inv(RowInvArgs a) {
 __global__ void __launch_bounds__(256)
 k_gather(CellView c, GridGeom g, const float2* __restrict__ fxy,
          const float* __restrict__ fx, const float* __restrict__ fy,  // planar alternative when fxy == nullptr
+         int row0, int row1, int halo, int owned_only,
          const float* __restrict__ grad_out, float* __restrict__ grad_x, float* __restrict__ grad_y,
          unsigned* __restrict__ flags) {
+    // The field maps hold rows [row0, row1 + halo).  With owned_only, only cells
+    // whose first bin row lies in [row0, row1) are computed and written; other
+    // entries of grad_x / grad_y are left as they are.
     const float gscale = grad_out ? -__ldg(grad_out) : -1.0f;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < c.n; i += stride) {
@@ -455,11 +488,17 @@ k_gather(CellView c, GridGeom g, const float2* __restrict__ fxy,
         const int st = cell_footprint(c, g, node, f);
         float ax = 0.0f, ay = 0.0f, r = 0.0f;
         if (st < 0) atomicOr(flags, kFlagNonFinite);
+        if (owned_only && (st <= 0 || f.kx0 < row0 || f.kx0 >= row1)) continue;
         if (st > 0) {
             r = f.r;
-            for (int kx = f.kx0; kx <= f.kx1; ++kx) {
+            int kxb = f.kx1;
+            if (kxb >= row1 + halo) {
+                atomicOr(flags, kFlagHalo);
+                kxb = row1 + halo - 1;
+            }
+            for (int kx = f.kx0; kx <= kxb; ++kx) {
                 const float ox = bin_overlap(f.x, f.ex, g.xl, g.bsx, kx);
-                const int64_t rowoff = (int64_t)kx * g.N;
+                const int64_t rowoff = (int64_t)(kx - row0) * g.N;
                 for (int ky = f.ky0; ky <= f.ky1; ++ky) {
                     const float w = ox * bin_overlap(f.y, f.ey, g.yl, g.bsy, ky);
                     float2 fv;

@@ -152,6 +152,45 @@ int epb_gather(epb_handle* h, const epb_cells* cells, const float* field_x, cons
  * it.  Returns EPB_EOVERFLOW when EPB_FLAG_SATURATED is set. */
 int epb_error_flags(epb_handle* h, epb_stream stream, uint32_t* flags);
 
+/* ---- One grid over P GPUs -------------------------------------------------
+ * The reference runs on one device (a unit mesh, host/density_scatter_ttnn_server_host.cpp:399)
+ * and has no multi-device counterpart; these entry points split epb_forward /
+ * epb_backward into the stages between which the caller moves data between GPUs
+ * (NCCL all-to-all, all-reduce, point-to-point).  P is a power of two; shard p
+ * owns grid rows [p*RB, (p+1)*RB) and, in the column pass, columns
+ * [p*NB, (p+1)*NB), RB = M/P, NB = N/P.  Buffers are caller-owned device arrays:
+ *   t1_send  RB*N floats  block q = [RB][NB] rows of this band, columns of band q
+ *   t1_recv  M*NB floats  after all-to-all(t1_send): block q = rows of band q (= [M][NB])
+ *   g_send   3*M*NB       block d = [3][RB][NB]: outputs (field_x form, field_y form,
+ *                          potential form) for band d's rows, columns of this band
+ *   g_recv   3*M*NB       after all-to-all(g_send): block q = [3][RB][NB] from band q
+ *   fxy_ext  (RB+halo)*N*2 floats: interleaved (field_x, field_y) of this band,
+ *                          then `halo` rows of the next band (point-to-point)
+ * Every cell that overlaps the band is scattered (clipped to it), so the
+ * fixed-point density of every bin is the same integer as on one GPU.  The
+ * gather computes the cells whose first bin row is in the band and leaves
+ * other gradient entries untouched; a footprint reaching past the halo sets
+ * EPB_FLAG_HALO and is clipped. */
+#define EPB_FLAG_HALO 0x4u
+int epb_create_shard(const epb_config* cfg, int32_t num_shards, int32_t shard, epb_handle** out);
+int epb_shard_geometry(const epb_handle* h, int32_t* num_shards, int32_t* shard, int32_t* rows_per_band,
+                       int32_t* cols_per_band);
+/* scatter into this band + density band (nullable, [RB][N]) + row DCT-II -> t1_send */
+int epb_shard_rows_forward(epb_handle* h, const epb_cells* cells, epb_stream stream, float* density_band,
+                           float* t1_send);
+/* column DCT-II, weights, column inverses -> g_send; this strip's share of the
+ * energy (double, device scalar, nullable) to be summed over shards */
+int epb_shard_columns(epb_handle* h, const float* t1_recv, epb_stream stream, float* g_send, int32_t want_potential,
+                      double* energy_partial);
+/* row inverses of this band from g_recv -> potential / field_x / field_y bands
+ * (nullable, [RB][N]) and the first RB rows of fxy_band; want_potential must
+ * match the epb_shard_columns call (non-NULL potential_band) */
+int epb_shard_rows_inverse(epb_handle* h, const float* g_recv, epb_stream stream, float* potential_band,
+                           float* field_x_band, float* field_y_band, float* fxy_band);
+/* gradient of the cells whose first bin row lies in this band */
+int epb_shard_gather(epb_handle* h, const epb_cells* cells, const float* fxy_ext, int32_t halo_rows,
+                     const float* grad_out, epb_stream stream, float* grad_x, float* grad_y);
+
 /* Stage timing.  Stages, in launch order: */
 #define EPB_STAGE_SCATTER   0  /* cells -> fixed-point grid                          */
 #define EPB_STAGE_ROW_FWD   1  /* grid -> density (+ initial density) -> row DCT-II  */
