@@ -224,7 +224,8 @@ def workload_config(args, p):
         "density": "int64 fixed point (bit-exact), fp32 DCT/fields",
         "l2": "flushed between timed steps (write of 2x L2 size)",
         "parallelism": "single" if args.gpus == 1 else
-        f"row-band shards x{args.gpus} (NCCL all-to-all transposes, fp64 energy all-reduce, field halo)",
+        f"row-band shards x{args.gpus}, transport {args.transport} "
+        f"({'kernel stores into peer memory over NVLink' if args.transport == 'peer' else 'NCCL all-to-all, all-reduce, p2p'})",
     }
 
 
@@ -254,7 +255,7 @@ def run_sharded(args, p, dev, world, rank):
     sx, sy, ox, oy, ratio = (to(a) for a in (p.size_x_clamped, p.size_y_clamped, p.offset_x, p.offset_y, p.ratio))
     cells = CellTensors(pos[:n], pos[n:], sx, sy, ox, oy, ratio, ranges=p.ranges)
     sh = ShardedElectricPotential(p.num_bins_x, p.num_bins_y, p.xl, p.yl, p.xh, p.yh,
-                                  float(p.size_x_clamped.max()), device=dev)
+                                  float(p.size_x_clamped.max()), device=dev, transport=args.transport)
     sh.set_initial_density(to(p.initial_density_norm()))
     RB, N = sh.RB, p.num_bins_y
     outs = {k: torch.empty((RB, N), dtype=torch.float32, device=dev)
@@ -277,7 +278,7 @@ def run_sharded(args, p, dev, world, rank):
     torch.cuda.synchronize(dev)
     K = args.steps
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
-    sh.be.profile_start(4 * K)
+    sh.be.profile_start(2 * K)
     dist.barrier()
     torch.cuda.synchronize(dev)
     t0 = time.perf_counter()
@@ -370,6 +371,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
     ap.add_argument("--ref-seconds", type=float, default=120.0, help="reference arm time cap")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--transport", default="peer", choices=["peer", "nccl"],
+                    help="multi-GPU exchange: stores into peer memory fused into the kernels, or NCCL collectives")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

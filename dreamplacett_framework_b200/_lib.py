@@ -21,6 +21,8 @@ EPB_ENOSTATE = 6
 EPB_FLAG_NONFINITE_CELL = 0x1
 EPB_FLAG_SATURATED = 0x2
 EPB_FLAG_HALO = 0x4
+EPB_FLAG_TIMEOUT = 0x8
+IPC_HANDLE_BYTES = 64
 
 # Every symbol include/epb.h declares (the CPU tests check the exports).
 EXPORTS = (
@@ -30,6 +32,8 @@ EXPORTS = (
     "epb_profile_start", "epb_profile_stop", "epb_density_noalloc",
     "epb_create_shard", "epb_shard_geometry", "epb_shard_rows_forward", "epb_shard_columns",
     "epb_shard_rows_inverse", "epb_shard_gather",
+    "epb_shard_peer_buffers", "epb_shard_connect", "epb_shard_set_timeout", "epb_shard_forward_peer",
+    "epb_shard_backward_peer", "epb_shard_wait_test",
 )
 
 # Largest grid (M*N bins) epb_density_noalloc accepts (EPB_NOALLOC_MAX_BINS).
@@ -106,6 +110,12 @@ def load():
     L.epb_shard_columns.argtypes = [vp, vp, vp, vp, i32, vp]
     L.epb_shard_rows_inverse.argtypes = [vp, vp, vp, vp, vp, vp, vp]
     L.epb_shard_gather.argtypes = [vp, cp, vp, i32, vp, vp, vp, vp]
+    L.epb_shard_peer_buffers.argtypes = [vp, i32, ctypes.c_char_p]
+    L.epb_shard_connect.argtypes = [vp, ctypes.c_char_p]
+    L.epb_shard_set_timeout.argtypes = [vp, i64]
+    L.epb_shard_forward_peer.argtypes = [vp, cp, vp, vp, vp, vp, vp, vp]
+    L.epb_shard_backward_peer.argtypes = [vp, cp, vp, vp, vp, vp]
+    L.epb_shard_wait_test.argtypes = [vp, vp, i64]
     for name in EXPORTS:
         if name not in ("epb_version", "epb_status_string", "epb_last_error"):
             getattr(L, name).restype = ctypes.c_int

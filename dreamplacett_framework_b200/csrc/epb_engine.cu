@@ -42,6 +42,22 @@ struct epb_handle {
     unsigned* counter = nullptr;
     double* energy_d = nullptr;
     unsigned* flags = nullptr;
+    // peer transport (epb_shard_peer_buffers / epb_shard_connect)
+    float* p_t1 = nullptr;      // t1_recv [M*NB]
+    float* p_g = nullptr;       // g_recv [3*M*NB]
+    float* p_gsend = nullptr;   // column-pass blocks bound for other shards [3*M*NB]
+    float2* p_fxy = nullptr;    // fxy_ext [(RB+Hmax)*N]
+    unsigned char* p_sig = nullptr;  // signal slots [3][kMaxShards] uint32, then energies [kMaxShards] double
+    int p_halo = 0;             // halo rows this band receives (0 for the last band)
+    int p_halo_max = 0;
+    bool connected = false;
+    unsigned epoch = 0;
+    float* peer_t1[kMaxShards] = {nullptr};
+    float* peer_g[kMaxShards] = {nullptr};
+    float2* peer_fxy[kMaxShards] = {nullptr};
+    unsigned char* peer_sig[kMaxShards] = {nullptr};
+    double* energy_total = nullptr;
+    long long max_polls = 40000000;  // bounded waits: ~5 s of 128 ns polls
     // stage timing (epb_profile_start/stop)
     struct Span { int stage, a, b; };
     bool prof_on = false;
@@ -143,6 +159,16 @@ void free_all(epb_handle* h) {
                     h->twN, h->qwN, h->partials, h->counter, h->energy_d, h->flags};
     for (void* p : ptrs)
         if (p) cudaFree(p);
+    for (int q = 0; q < kMaxShards; ++q) {
+        if (q == h->p) continue;
+        if (h->peer_t1[q]) cudaIpcCloseMemHandle(h->peer_t1[q]);
+        if (h->peer_g[q]) cudaIpcCloseMemHandle(h->peer_g[q]);
+        if (h->peer_fxy[q]) cudaIpcCloseMemHandle(h->peer_fxy[q]);
+        if (h->peer_sig[q]) cudaIpcCloseMemHandle(h->peer_sig[q]);
+    }
+    void* own[] = {h->p_t1, h->p_g, h->p_gsend, h->p_fxy, h->p_sig, h->energy_total};
+    for (void* p : own)
+        if (p) cudaFree(p);
     for (cudaEvent_t e : h->prof_events) cudaEventDestroy(e);
     h->prof_events.clear();
 }
@@ -164,22 +190,21 @@ int ilog2(int v) {
 // Row pass over this handle's RB rows: t1 receives the blocked layout (block
 // width NB, RB*NB elements per block); for P == 1 that is plain [M][N].
 template <int L>
-int launch_row_fwd_t(epb_handle* h, bool from_fixed, const float* rho_in, float* rho_out, float* t1,
-                     cudaStream_t st) {
+int launch_row_fwd_t(epb_handle* h, bool from_fixed, const float* rho_in, float* rho_out, const DstTable& t1,
+                     int drow0, cudaStream_t st) {
     using C = RowFwdCfg<L>;
     const unsigned blocks = (unsigned)((h->RB + C::ROWS - 1) / C::ROWS);
     const float* init = h->has_init && from_fixed ? h->init : nullptr;
     const int lnb = ilog2(h->NB);
-    const int64_t tblock = (int64_t)h->RB * h->NB;
     if (from_fixed) {
         auto fn = k_row_fwd<L, true>;
         if (int rc = set_smem<L>(h, (const void*)fn, C::SMEM)) return rc;
-        fn<<<blocks, C::T, C::SMEM, st>>>(h->grid, nullptr, init, h->dscale, h->RB, rho_out, t1, lnb, tblock,
+        fn<<<blocks, C::T, C::SMEM, st>>>(h->grid, nullptr, init, h->dscale, h->RB, rho_out, t1, lnb, drow0,
                                           h->twN, h->qwN, h->flags);
     } else {
         auto fn = k_row_fwd<L, false>;
         if (int rc = set_smem<L>(h, (const void*)fn, C::SMEM)) return rc;
-        fn<<<blocks, C::T, C::SMEM, st>>>(nullptr, rho_in, nullptr, h->dscale, h->RB, rho_out, t1, lnb, tblock,
+        fn<<<blocks, C::T, C::SMEM, st>>>(nullptr, rho_in, nullptr, h->dscale, h->RB, rho_out, t1, lnb, drow0,
                                           h->twN, h->qwN, h->flags);
     }
     EPB_LAUNCHED(h, "k_row_fwd launch");
@@ -222,9 +247,9 @@ int launch_row_inv_t(epb_handle* h, const RowInvArgs& a, cudaStream_t st) {
         default: return fail(h, EPB_EINVAL, "unsupported transform length"); \
     }
 
-int launch_row_fwd(epb_handle* h, bool from_fixed, const float* rho_in, float* rho_out, float* t1,
-                   cudaStream_t st) {
-#define CALL_RF(L) launch_row_fwd_t<L>(h, from_fixed, rho_in, rho_out, t1, st)
+int launch_row_fwd(epb_handle* h, bool from_fixed, const float* rho_in, float* rho_out, const DstTable& t1,
+                   int drow0, cudaStream_t st) {
+#define CALL_RF(L) launch_row_fwd_t<L>(h, from_fixed, rho_in, rho_out, t1, drow0, st)
     EPB_DISPATCH_L(h->N, CALL_RF)
 #undef CALL_RF
 }
@@ -281,15 +306,22 @@ struct ProfCall {
     }
 };
 
+// Destination table of a local send buffer laid out in P blocks of `block` elements.
+DstTable blocked(float* base, int64_t block, int P) {
+    DstTable t;
+    for (int q = 0; q < kMaxShards; ++q) t.p[q] = q < P ? base + q * block : nullptr;
+    return t;
+}
+
 // Column pass: t1 = column strip [M][NB] of this handle's column band; g =
 // outputs laid out g[d][o][r][c] (d destination row band).  The energy of the
 // strip (times MN/4) lands in h->energy_d and, when given, energy_out.
-int launch_columns(epb_handle* h, const float* t1, float* g, bool want_phi, float* energy_out, cudaStream_t st) {
+int launch_columns(epb_handle* h, const float* t1, const DstTable& g, bool want_phi, float* energy_out,
+                   cudaStream_t st) {
     ColArgs ca;
     ca.t1 = t1;
     ca.g = g;
     ca.ostride = (int64_t)h->RB * h->NB;
-    ca.dstride = 3 * (int64_t)h->RB * h->NB;
     ca.lrb = ilog2(h->RB);
     ca.col_base = h->col0;
     ca.ku = (float)(2.0 * M_PI / h->M);
@@ -303,13 +335,14 @@ int launch_columns(epb_handle* h, const float* t1, float* g, bool want_phi, floa
 
 // Row inverses of this handle's RB rows from g[q][o][r][c] (q source column band).
 int launch_rows_inverse(epb_handle* h, const float* g, float* potential, float* field_x, float* field_y,
-                        float2* fxy, bool want_phi, cudaStream_t st) {
+                        float2* fxy, bool want_phi, cudaStream_t st, float2* halo_dst = nullptr, int halo_rows = 0) {
     RowInvArgs ra;
     ra.g = g;
     ra.ostride = (int64_t)h->RB * h->NB;
     ra.qstride = 3 * (int64_t)h->RB * h->NB;
     ra.lnb = ilog2(h->NB);
     ra.fx = field_x; ra.fy = field_y; ra.phi = want_phi ? potential : nullptr; ra.fxy = fxy;
+    ra.halo_dst = halo_dst; ra.halo_rows = halo_dst ? halo_rows : 0;
     ra.tw = h->twN; ra.qw = h->qwN; ra.M = h->RB; ra.want_phi = want_phi;
     return launch_row_inv(h, ra, st);
 }
@@ -318,7 +351,7 @@ int launch_rows_inverse(epb_handle* h, const float* g, float* potential, float* 
 int solve_from_t1(epb_handle* h, cudaStream_t st, float* potential, float* field_x, float* field_y,
                   float* energy, ProfCall& pc) {
     const bool want_phi = potential != nullptr;
-    if (int rc = launch_columns(h, h->t1, h->g, want_phi, energy, st)) return rc;
+    if (int rc = launch_columns(h, h->t1, blocked(h->g, 0, 1), want_phi, energy, st)) return rc;
     pc.end_stage(EPB_STAGE_COLUMN);
     if (int rc = launch_rows_inverse(h, h->g, potential, field_x, field_y, h->fxy, want_phi, st)) return rc;
     pc.end_stage(EPB_STAGE_ROW_INV);
@@ -497,7 +530,7 @@ int epb_forward(epb_handle* h, const epb_cells* cells, epb_stream stream, float*
     pc.begin();
     if (int rc = scatter_into(h, v, st, h->grid)) return rc;
     pc.end_stage(EPB_STAGE_SCATTER);
-    if (int rc = launch_row_fwd(h, true, nullptr, density, h->t1, st)) return rc;
+    if (int rc = launch_row_fwd(h, true, nullptr, density, blocked(h->t1, 0, 1), 0, st)) return rc;
     pc.end_stage(EPB_STAGE_ROW_FWD);
     h->grid_dirty = false;
     return solve_from_t1(h, st, potential, field_x, field_y, energy, pc);
@@ -547,7 +580,7 @@ int epb_dct_solve(epb_handle* h, const float* density, epb_stream stream, float*
     cudaStream_t st = (cudaStream_t)stream;
     ProfCall pc(h, st);
     pc.begin();
-    if (int rc = launch_row_fwd(h, false, density, nullptr, h->t1, st)) return rc;
+    if (int rc = launch_row_fwd(h, false, density, nullptr, blocked(h->t1, 0, 1), 0, st)) return rc;
     pc.end_stage(EPB_STAGE_ROW_FWD);
     return solve_from_t1(h, st, potential, field_x, field_y, energy, pc);
 }
@@ -578,6 +611,7 @@ int epb_error_flags(epb_handle* h, epb_stream stream, uint32_t* flags) {
     EPB_CUDA(h, cudaMemsetAsync(h->flags, 0, sizeof(unsigned), st));
     EPB_CUDA(h, cudaStreamSynchronize(st));
     if (flags) *flags = f;
+    if (f & EPB_FLAG_TIMEOUT) return fail(h, EPB_ETIMEOUT, "a wait for another GPU's signal gave up");
     if (f & EPB_FLAG_SATURATED) return fail(h, EPB_EOVERFLOW, "fixed-point density saturated");
     return EPB_OK;
 }
@@ -609,7 +643,9 @@ int epb_shard_rows_forward(epb_handle* h, const epb_cells* cells, epb_stream str
     pc.begin();
     if (int rc = scatter_into(h, v, st, h->grid)) return rc;
     pc.end_stage(EPB_STAGE_SCATTER);
-    if (int rc = launch_row_fwd(h, true, nullptr, density_band, t1_send, st)) return rc;
+    if (int rc = launch_row_fwd(h, true, nullptr, density_band, blocked(t1_send, (int64_t)h->RB * h->NB, h->P), 0,
+                                st))
+        return rc;
     pc.end_stage(EPB_STAGE_ROW_FWD);
     h->grid_dirty = false;
     return EPB_OK;
@@ -623,7 +659,9 @@ int epb_shard_columns(epb_handle* h, const float* t1_recv, epb_stream stream, fl
     cudaStream_t st = (cudaStream_t)stream;
     ProfCall pc(h, st);
     pc.begin();
-    if (int rc = launch_columns(h, t1_recv, g_send, want_potential != 0, nullptr, st)) return rc;
+    if (int rc = launch_columns(h, t1_recv, blocked(g_send, 3 * (int64_t)h->RB * h->NB, h->P), want_potential != 0,
+                                nullptr, st))
+        return rc;
     pc.end_stage(EPB_STAGE_COLUMN);
     if (energy_partial)
         EPB_CUDA(h, cudaMemcpyAsync(energy_partial, h->energy_d, sizeof(double), cudaMemcpyDeviceToDevice, st));
@@ -667,6 +705,183 @@ int epb_shard_gather(epb_handle* h, const epb_cells* cells, const float* fxy_ext
     return EPB_OK;
 }
 
+// ---- peer transport -------------------------------------------------------
+
+int epb_shard_peer_buffers(epb_handle* h, int32_t halo_rows, void* handles_out) {
+    if (!h || !handles_out) return EPB_EINVAL;
+    if (h->P > kMaxShards) return fail(h, EPB_EINVAL, "at most 8 shards");
+    if (halo_rows < 0 || halo_rows > h->RB) return fail(h, EPB_EINVAL, "halo_rows must be in [0, rows per band]");
+    if (h->p_t1) return fail(h, EPB_EINVAL, "peer buffers already created");
+    DeviceGuard guard(h->dev);
+    const size_t strip = (size_t)h->M * h->NB;
+    h->p_halo_max = halo_rows;
+    h->p_halo = h->p == h->P - 1 ? 0 : halo_rows;
+    const size_t sig_bytes = 3 * kMaxShards * sizeof(unsigned) + kMaxShards * sizeof(double) + 64;
+    int rc = EPB_OK;
+    if (!rc) rc = dev_alloc(h, &h->p_t1, strip);
+    if (!rc) rc = dev_alloc(h, &h->p_g, 3 * strip);
+    if (!rc && h->P > 1) rc = dev_alloc(h, &h->p_gsend, 3 * strip);
+    if (!rc) rc = dev_alloc(h, &h->p_fxy, (size_t)(h->RB + halo_rows) * h->N);
+    if (!rc) rc = dev_alloc(h, &h->p_sig, sig_bytes);
+    if (!rc) rc = dev_alloc(h, &h->energy_total, 1);
+    if (rc) return rc;
+    EPB_CUDA(h, cudaMemset(h->p_sig, 0, sig_bytes));
+    EPB_CUDA(h, cudaMemset(h->p_fxy, 0, (size_t)(h->RB + halo_rows) * h->N * sizeof(float2)));
+    cudaIpcMemHandle_t* out = static_cast<cudaIpcMemHandle_t*>(handles_out);
+    EPB_CUDA(h, cudaIpcGetMemHandle(&out[0], h->p_t1));
+    EPB_CUDA(h, cudaIpcGetMemHandle(&out[1], h->p_g));
+    EPB_CUDA(h, cudaIpcGetMemHandle(&out[2], h->p_fxy));
+    EPB_CUDA(h, cudaIpcGetMemHandle(&out[3], h->p_sig));
+    EPB_CUDA(h, cudaDeviceSynchronize());
+    return EPB_OK;
+}
+
+int epb_shard_connect(epb_handle* h, const void* all_handles) {
+    if (!h || !all_handles) return EPB_EINVAL;
+    if (!h->p_t1) return fail(h, EPB_ENOSTATE, "epb_shard_peer_buffers first");
+    DeviceGuard guard(h->dev);
+    const cudaIpcMemHandle_t* hs = static_cast<const cudaIpcMemHandle_t*>(all_handles);
+    for (int q = 0; q < h->P; ++q) {
+        if (q == h->p) {
+            h->peer_t1[q] = h->p_t1; h->peer_g[q] = h->p_g; h->peer_fxy[q] = h->p_fxy; h->peer_sig[q] = h->p_sig;
+            continue;
+        }
+        void* ptr = nullptr;
+        EPB_CUDA(h, cudaIpcOpenMemHandle(&ptr, hs[4 * q + 0], cudaIpcMemLazyEnablePeerAccess));
+        h->peer_t1[q] = static_cast<float*>(ptr);
+        EPB_CUDA(h, cudaIpcOpenMemHandle(&ptr, hs[4 * q + 1], cudaIpcMemLazyEnablePeerAccess));
+        h->peer_g[q] = static_cast<float*>(ptr);
+        EPB_CUDA(h, cudaIpcOpenMemHandle(&ptr, hs[4 * q + 2], cudaIpcMemLazyEnablePeerAccess));
+        h->peer_fxy[q] = static_cast<float2*>(ptr);
+        EPB_CUDA(h, cudaIpcOpenMemHandle(&ptr, hs[4 * q + 3], cudaIpcMemLazyEnablePeerAccess));
+        h->peer_sig[q] = static_cast<unsigned char*>(ptr);
+    }
+    h->connected = true;
+    return EPB_OK;
+}
+
+int epb_shard_set_timeout(epb_handle* h, int64_t max_polls) {
+    if (!h || max_polls < 1) return EPB_EINVAL;
+    h->max_polls = max_polls;
+    return EPB_OK;
+}
+
+namespace {
+
+PeerSignals peer_signals(epb_handle* h) {
+    PeerSignals ps;
+    for (int q = 0; q < kMaxShards; ++q) {
+        ps.sig[q] = q < h->P ? reinterpret_cast<unsigned*>(h->peer_sig[q]) : nullptr;
+        ps.energy[q] = q < h->P ? reinterpret_cast<double*>(h->peer_sig[q] + 3 * kMaxShards * sizeof(unsigned))
+                                : nullptr;
+    }
+    return ps;
+}
+
+int signal_and_wait(epb_handle* h, int stage, cudaStream_t st, const double* energy = nullptr,
+                    float* energy_out = nullptr) {
+    k_signal<<<1, 32, 0, st>>>(peer_signals(h), h->P, h->p, stage, h->epoch, energy);
+    EPB_LAUNCHED(h, "k_signal launch");
+    const double* my_energy = reinterpret_cast<const double*>(h->p_sig + 3 * kMaxShards * sizeof(unsigned));
+    k_wait<<<1, 32, 0, st>>>(reinterpret_cast<const unsigned*>(h->p_sig), h->P, stage, h->epoch, h->max_polls,
+                             my_energy, energy ? h->energy_total : nullptr, energy_out, 1.0, h->flags);
+    EPB_LAUNCHED(h, "k_wait launch");
+    return EPB_OK;
+}
+
+}  // namespace
+
+int epb_shard_forward_peer(epb_handle* h, const epb_cells* cells, epb_stream stream, float* density_band,
+                           float* potential_band, float* field_x_band, float* field_y_band, float* energy) {
+    if (!h) return EPB_EINVAL;
+    if (!h->connected) return fail(h, EPB_ENOSTATE, "epb_shard_connect first");
+    CellView v;
+    if (int rc = make_view(h, cells, v)) return rc;
+    DeviceGuard guard(h->dev);
+    cudaStream_t st = (cudaStream_t)stream;
+    h->epoch += 1;
+    if (h->grid_dirty) {
+        EPB_CUDA(h, cudaMemsetAsync(h->grid, 0, (size_t)h->RB * h->N * sizeof(long long), st));
+        h->grid_dirty = false;
+    }
+    h->grid_dirty = true;
+    ProfCall pc(h, st);
+    pc.begin();
+    if (int rc = scatter_into(h, v, st, h->grid)) return rc;
+    pc.end_stage(EPB_STAGE_SCATTER);
+    // row DCT blocks go straight into every shard's column strip
+    DstTable t1;
+    for (int q = 0; q < kMaxShards; ++q) t1.p[q] = q < h->P ? h->peer_t1[q] : nullptr;
+    if (int rc = launch_row_fwd(h, true, nullptr, density_band, t1, h->row0, st)) return rc;
+    pc.end_stage(EPB_STAGE_ROW_FWD);
+    h->grid_dirty = false;
+    if (int rc = signal_and_wait(h, 0, st)) return rc;
+    pc.last = pc.mark();
+    // column outputs: this band's block in place, the other bands' blocks staged
+    // locally (each row of a strip is only 4 columns wide) and pushed as whole
+    // contiguous blocks into the peers' row-band buffers
+    const int64_t gblock = 3 * (int64_t)h->RB * h->NB;
+    DstTable g;
+    for (int q = 0; q < kMaxShards; ++q)
+        g.p[q] = q >= h->P ? nullptr : (q == h->p ? h->p_g + h->p * gblock : h->p_gsend + q * gblock);
+    const bool want_phi = potential_band != nullptr;
+    if (int rc = launch_columns(h, h->p_t1, g, want_phi, nullptr, st)) return rc;
+    if (h->P > 1) {
+        PushArgs pa;
+        pa.nblocks = 0;
+        pa.n4 = gblock / 4;
+        for (int q = 0; q < h->P; ++q) {
+            if (q == h->p) continue;
+            pa.src[pa.nblocks] = reinterpret_cast<const float4*>(h->p_gsend + q * gblock);
+            pa.dst[pa.nblocks] = reinterpret_cast<float4*>(h->peer_g[q] + h->p * gblock);
+            pa.nblocks++;
+        }
+        k_push<<<148 * 8, 256, 0, st>>>(pa);
+        EPB_LAUNCHED(h, "k_push launch");
+    }
+    pc.end_stage(EPB_STAGE_COLUMN);
+    if (int rc = signal_and_wait(h, 1, st, h->energy_d, energy)) return rc;
+    pc.last = pc.mark();
+    // row inverses; the first halo rows also go to the previous band's halo
+    float2* halo_dst = h->p > 0 ? h->peer_fxy[h->p - 1] + (int64_t)h->RB * h->N : nullptr;
+    if (int rc = launch_rows_inverse(h, h->p_g, potential_band, field_x_band, field_y_band, h->p_fxy, want_phi, st,
+                                     halo_dst, h->p_halo_max))
+        return rc;
+    pc.end_stage(EPB_STAGE_ROW_INV);
+    return signal_and_wait(h, 2, st);
+}
+
+int epb_shard_backward_peer(epb_handle* h, const epb_cells* cells, const float* grad_out, epb_stream stream,
+                            float* grad_x, float* grad_y) {
+    if (!h) return EPB_EINVAL;
+    if (!h->connected) return fail(h, EPB_ENOSTATE, "epb_shard_connect first");
+    CellView v;
+    if (int rc = make_view(h, cells, v)) return rc;
+    if (v.n > 0 && (!grad_x || !grad_y)) return fail(h, EPB_EINVAL, "grad_x/grad_y must be non-NULL");
+    if (v.n == 0) return EPB_OK;
+    DeviceGuard guard(h->dev);
+    cudaStream_t st = (cudaStream_t)stream;
+    ProfCall pc(h, st);
+    pc.begin();
+    k_gather<<<cell_blocks(v.n), 256, 0, st>>>(v, geom(h), h->p_fxy, nullptr, nullptr, h->row0, h->row0 + h->RB,
+                                                h->p_halo, 1, grad_out, grad_x, grad_y, h->flags);
+    EPB_LAUNCHED(h, "k_gather launch");
+    pc.end_stage(EPB_STAGE_GATHER);
+    return EPB_OK;
+}
+
+int epb_shard_wait_test(epb_handle* h, epb_stream stream, int64_t max_polls) {
+    if (!h || max_polls < 1) return EPB_EINVAL;
+    if (!h->p_sig) return fail(h, EPB_ENOSTATE, "epb_shard_peer_buffers first");
+    DeviceGuard guard(h->dev);
+    // an epoch no shard has published: the wait must run out and flag a timeout
+    k_wait<<<1, 32, 0, (cudaStream_t)stream>>>(reinterpret_cast<const unsigned*>(h->p_sig), h->P, 0,
+                                                h->epoch + 0x40000000u, (long long)max_polls, nullptr, nullptr,
+                                                nullptr, 1.0, h->flags);
+    EPB_LAUNCHED(h, "k_wait launch");
+    return EPB_OK;
+}
+
 int epb_profile_start(epb_handle* h, int32_t max_calls) {
     if (!h) return EPB_EINVAL;
     if (max_calls < 1 || max_calls > 200000) return fail(h, EPB_EINVAL, "max_calls must be in [1, 200000]");
@@ -675,7 +890,7 @@ int epb_profile_start(epb_handle* h, int32_t max_calls) {
     h->prof_events.clear();
     h->prof_spans.clear();
     h->prof_used = 0;
-    const size_t n = (size_t)max_calls * 5;
+    const size_t n = (size_t)max_calls * 8;
     h->prof_events.resize(n);
     for (size_t i = 0; i < n; ++i) {
         cudaError_t e = cudaEventCreate(&h->prof_events[i]);

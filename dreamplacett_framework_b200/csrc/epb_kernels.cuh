@@ -43,6 +43,15 @@ namespace epb {
 constexpr unsigned kFlagNonFinite = 0x1u;
 constexpr unsigned kFlagSaturated = 0x2u;
 constexpr unsigned kFlagHalo = 0x4u;       // a gathered footprint reached past the field halo
+constexpr unsigned kFlagTimeout = 0x8u;    // a wait for another GPU's signal gave up
+constexpr int kMaxShards = 8;
+
+// Destination of each column block / row band of an exchanged buffer: this
+// GPU's send buffer (NCCL transport) or the peer's receive buffer mapped over
+// NVLink (peer transport).
+struct DstTable {
+    float* p[kMaxShards];
+};
 
 // ---------------------------------------------------------------------------
 // Scatter
@@ -54,9 +63,9 @@ k_scatter(CellView c, GridGeom g, float qscale, unsigned long long* __restrict__
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < c.n; i += stride) {
         Footprint f;
-        const int st = cell_footprint(c, g, cell_node(c, i), f);
+        const int st = cell_footprint(c, g, cell_node(c, i), f, row0, row1, false);
         if (st < 0) { atomicOr(flags, kFlagNonFinite); continue; }
-        if (st == 0) continue;
+        if (st != 1) continue;
         const int kxa = max(f.kx0, row0), kxb = min(f.kx1, row1 - 1);
         for (int kx = kxa; kx <= kxb; ++kx) {
             const float oxr = __fmul_rn(bin_overlap(f.x, f.ex, g.xl, g.bsx, kx), f.r);
@@ -93,8 +102,8 @@ k_row_fwd(long long* __restrict__ qgrid,            // FROM_FIXED: [M][L] int64 
           const float* __restrict__ init,           // nullable [M][L]
           double dscale, int M,
           float* __restrict__ rho_out,              // nullable
-          float* __restrict__ t1,                   // blocked: t1[k >> lnb][row][k & (nb-1)]
-          int lnb, int64_t tblock,                  // log2 block width, elements per block
+          DstTable t1dst,                           // column block q goes to t1dst.p[q][(drow0 + row) * nb + c]
+          int lnb, int drow0,                       // log2 block width nb; first row of this band there
           const float2* __restrict__ tw, const float2* __restrict__ qw,
           unsigned* __restrict__ flags) {
     using C = RowFwdCfg<L>;
@@ -145,7 +154,7 @@ k_row_fwd(long long* __restrict__ qgrid,            // FROM_FIXED: [M][L] int64 
         const float2 q = __ldg(qw + k);  // (cos, sin)(pi k / 2L)
         const int ra = row0 + 2 * s;
         const int nb = 1 << lnb;
-        float* tb = t1 + (int64_t)(k >> lnb) * tblock + (k & (nb - 1));
+        float* tb = t1dst.p[k >> lnb] + (int64_t)drow0 * nb + (k & (nb - 1));
         if (ra < M) tb[(int64_t)ra * nb] = scale * (Va.x * q.x + Va.y * q.y);
         if (ra + 1 < M) tb[(int64_t)(ra + 1) * nb] = scale * (Vb.x * q.x + Vb.y * q.y);
     }
@@ -172,10 +181,9 @@ struct ColCfg {
 
 struct ColArgs {
     const float* t1;        // column strip [M][N] (N = local strip width, the row stride)
-    float* g;               // outputs g[d][o][r][c]: o = 0 (2 IDXST_M)(auv*wu), 1 (2 IDCT_M)(auv*wv),
-                            //   2 IDCT_M(auv*inv) (only when want_phi)
+    DstTable g;             // outputs for destination band d at g.p[d][o*ostride + r*N + c]:
+                            //   o = 0 (2 IDXST_M)(auv*wu), 1 (2 IDCT_M)(auv*wv), 2 IDCT_M(auv*inv) (want_phi)
     int64_t ostride;        // elements between outputs o
-    int64_t dstride;        // elements between destination bands d
     int lrb;                // log2 rows per destination band
     int col_base;           // global index of local column 0
     float ku;               // wu = u * ku,  ku = 2 pi / M
@@ -317,7 +325,7 @@ k_col(ColArgs a) {
         }
         __syncthreads();
         fft_seq<L, true>(myseq, lane, a.tw);
-        float* out = a.g + (int64_t)r * a.ostride;
+        const int64_t oo = (int64_t)r * a.ostride;
         const int rbm = (1 << a.lrb) - 1;
 #pragma unroll 4
         for (int e = threadIdx.x; e < L * (W / 4); e += T) {
@@ -328,7 +336,7 @@ k_col(ColArgs a) {
             float2 v1 = buf[(2 * q4 + 1) * LP + src];
             if (r == 0 && (k & 1)) { v0.x = -v0.x; v0.y = -v0.y; v1.x = -v1.x; v1.y = -v1.y; }
             if (col < N)
-                *reinterpret_cast<float4*>(out + (int64_t)(k >> a.lrb) * a.dstride + (int64_t)(k & rbm) * N + col) =
+                *reinterpret_cast<float4*>(a.g.p[k >> a.lrb] + oo + (int64_t)(k & rbm) * N + col) =
                     make_float4(v0.x, v0.y, v1.x, v1.y);
         }
         __syncthreads();
@@ -391,6 +399,8 @@ struct RowInvArgs {
     int lnb;                 // log2 columns per band
     float* fx; float* fy; float* phi;                   // nullable outputs, [M][N] of this band
     float2* fxy;                                        // interleaved fields [M][N] of this band
+    float2* halo_dst;        // nullable: the previous band's field halo (its rows RB..), peer memory
+    int halo_rows;           // rows of this band that also go to halo_dst
     const float2* tw; const float2* qw;                 // length N
     int M;                   // rows in this band
     int want_phi;
@@ -457,6 +467,7 @@ k_row_inv(RowInvArgs a) {
                 const float fx = v.x;
                 const float fy = (l & 1) ? -v.y : v.y;
                 a.fxy[off] = make_float2(fx, fy);
+                if (row < a.halo_rows) a.halo_dst[off] = make_float2(fx, fy);
                 if (a.fx) a.fx[off] = fx;
                 if (a.fy) a.fy[off] = fy;
             }
@@ -485,11 +496,11 @@ k_gather(CellView c, GridGeom g, const float2* __restrict__ fxy,
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < c.n; i += stride) {
         const int64_t node = cell_node(c, i);
         Footprint f;
-        const int st = cell_footprint(c, g, node, f);
+        const int st = cell_footprint(c, g, node, f, row0, row1, owned_only != 0);
         float ax = 0.0f, ay = 0.0f, r = 0.0f;
         if (st < 0) atomicOr(flags, kFlagNonFinite);
-        if (owned_only && (st <= 0 || f.kx0 < row0 || f.kx0 >= row1)) continue;
-        if (st > 0) {
+        if (owned_only && st != 1) continue;
+        if (st == 1) {
             r = f.r;
             int kxb = f.kx1;
             if (kxb >= row1 + halo) {
@@ -512,6 +523,79 @@ k_gather(CellView c, GridGeom g, const float2* __restrict__ fxy,
         const float s = gscale * r;
         grad_x[node] = s * ax;
         grad_y[node] = s * ay;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Cross-GPU ordering for the peer transport.  After a producer kernel has
+// stored its blocks into the peers' buffers, k_signal publishes `epoch` in
+// every peer's signal slot for (stage, this shard), optionally with this
+// shard's energy partial.  k_wait (one thread) then waits until every shard
+// has published `epoch` for the stage, with a bounded number of polls: when
+// the limit is reached it sets kFlagTimeout and returns, so a missing peer
+// turns into an error status instead of a hang.
+// ---------------------------------------------------------------------------
+// Coalesced copy of whole blocks into peer memory: block d of `src` goes to
+// `dst[d]` (16-byte loads and stores, consecutive threads on consecutive
+// addresses, so every NVLink write carries full lines).
+struct PushArgs {
+    const float4* src[kMaxShards];
+    float4* dst[kMaxShards];
+    int nblocks;
+    int64_t n4;   // float4 per block
+};
+
+__global__ void __launch_bounds__(256) k_push(PushArgs a) {
+    const int64_t total = (int64_t)a.nblocks * a.n4;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+        const int d = (int)(i / a.n4);
+        const int64_t j = i - (int64_t)d * a.n4;
+        a.dst[d][j] = __ldg(a.src[d] + j);
+    }
+}
+
+struct PeerSignals {
+    unsigned* sig[kMaxShards];     // peer q's signal array: [stage][shard]
+    double* energy[kMaxShards];    // peer q's energy partials: [shard]
+};
+
+__global__ void k_signal(PeerSignals peers, int P, int p, int stage, unsigned epoch, const double* energy) {
+    if (threadIdx.x != 0) return;
+    __threadfence_system();
+    for (int q = 0; q < P; ++q) {
+        if (energy) peers.energy[q][p] = *energy;
+    }
+    __threadfence_system();
+    for (int q = 0; q < P; ++q) {
+        volatile unsigned* slot = peers.sig[q] + stage * kMaxShards + p;
+        *slot = epoch;
+    }
+    __threadfence_system();
+}
+
+__global__ void k_wait(const unsigned* sig, int P, int stage, unsigned epoch, long long max_polls,
+                       const double* energy_in, double* energy_sum, float* energy_out, double energy_scale,
+                       unsigned* flags) {
+    if (threadIdx.x != 0) return;
+    const volatile unsigned* row = sig + stage * kMaxShards;
+    for (int q = 0; q < P; ++q) {
+        long long polls = 0;
+        while ((int)(row[q] - epoch) < 0) {
+            if (++polls > max_polls) {
+                atomicOr(flags, kFlagTimeout);
+                return;
+            }
+            __nanosleep(128);
+        }
+    }
+    __threadfence_system();
+    if (energy_sum) {
+        // fixed summation order: every shard gets the same bits
+        double e = 0.0;
+        for (int q = 0; q < P; ++q) e += ((const volatile double*)energy_in)[q];
+        *energy_sum = e;
+        if (energy_out) *energy_out = (float)(e * energy_scale);
     }
 }
 

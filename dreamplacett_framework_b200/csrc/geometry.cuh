@@ -66,23 +66,37 @@ struct Footprint {
 };
 
 // Returns -1 for a non-finite cell (skipped and flagged), 0 when the cell
-// contributes nothing (non-positive size or off the die), 1 otherwise.
+// contributes nothing (non-positive size or off the die), 2 when it is outside
+// the row band [row_lo, row_hi) (owner == false: its rows do not meet the band;
+// owner == true: its first row is not in the band), 1 otherwise.  The x data is
+// read first so cells of other bands cost three loads, not seven.
 __device__ __forceinline__ int cell_footprint(const CellView& c, const GridGeom& g, int64_t node,
-                                              Footprint& f) {
-    float x = __ldg(c.x + node), y = __ldg(c.y + node);
+                                              Footprint& f, int row_lo, int row_hi, bool owner) {
+    float x = __ldg(c.x + node);
     if (c.ox) x = __fadd_rn(x, __ldg(c.ox + node));
+    const float sx = __ldg(c.sx + node);
+    if (!isfinite(x) || !isfinite(sx)) return -1;
+    bool empty = !(sx > 0.0f);
+    if (!empty) {
+        f.ex = __fadd_rn(x, sx);
+        f.kx0 = bin_floor(x, g.xl, g.bsx, g.ibsx, g.M);
+        f.kx1 = min(bin_floor(f.ex, g.xl, g.bsx, g.ibsx, g.M), g.M - 1);
+        empty = f.kx0 > f.kx1;
+        if (!empty && (owner ? (f.kx0 < row_lo || f.kx0 >= row_hi) : (f.kx1 < row_lo || f.kx0 >= row_hi)))
+            return 2;
+    }
+    // the rest is read for cells of this band, and for empty cells so every
+    // non-finite input is reported as on one GPU
+    float y = __ldg(c.y + node);
     if (c.oy) y = __fadd_rn(y, __ldg(c.oy + node));
-    float sx = __ldg(c.sx + node), sy = __ldg(c.sy + node);
-    float r = c.ratio ? __ldg(c.ratio + node) : 1.0f;
-    if (!isfinite(x) || !isfinite(y) || !isfinite(sx) || !isfinite(sy) || !isfinite(r)) return -1;
-    if (!(sx > 0.0f) || !(sy > 0.0f)) return 0;
-    f.ex = __fadd_rn(x, sx);
+    const float sy = __ldg(c.sy + node);
+    const float r = c.ratio ? __ldg(c.ratio + node) : 1.0f;
+    if (!isfinite(y) || !isfinite(sy) || !isfinite(r)) return -1;
+    if (empty || !(sy > 0.0f)) return 0;
     f.ey = __fadd_rn(y, sy);
-    f.kx0 = bin_floor(x, g.xl, g.bsx, g.ibsx, g.M);
-    f.kx1 = min(bin_floor(f.ex, g.xl, g.bsx, g.ibsx, g.M), g.M - 1);
     f.ky0 = bin_floor(y, g.yl, g.bsy, g.ibsy, g.N);
     f.ky1 = min(bin_floor(f.ey, g.yl, g.bsy, g.ibsy, g.N), g.N - 1);
-    if (f.kx0 > f.kx1 || f.ky0 > f.ky1) return 0;
+    if (f.ky0 > f.ky1) return 0;
     f.x = x; f.y = y; f.r = r;
     return 1;
 }

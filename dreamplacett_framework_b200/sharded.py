@@ -21,6 +21,11 @@ The exchange is split from the arithmetic by a small backend interface so the
 same orchestration runs on the CUDA engine (`EngineShard`, NCCL) and, in the
 CPU tests, on a restatement with gloo.
 
+transport="peer" fuses steps 2, 4 and 6 into the kernels instead: they store
+their blocks straight into the other GPUs' buffers over NVLink (CUDA IPC
+mappings), and bounded one-thread waits on epoch signals order the stages
+(epb_shard_forward_peer in include/epb.h).
+
 Integer density sums make the density map identical to the one-GPU result for
 any P.  The fields and the energy differ from it only by fp32 rounding.
 """
@@ -97,6 +102,33 @@ class EngineShard:
                                                       _ptr(grad_out), _stream_ptr(None, self.device),
                                                       _ptr(grad_x), _ptr(grad_y)))
 
+    # ---- peer transport (exchanges fused into the kernels) ----
+    def setup_peer(self, halo_rows, group=None):
+        """Create the IPC-shared receive buffers and map every shard's (collective)."""
+        buf = ctypes.create_string_buffer(4 * _lib.IPC_HANDLE_BYTES)
+        _lib.check(self._h, self.lib.epb_shard_peer_buffers(self._h, int(halo_rows), buf))
+        mine = torch.frombuffer(bytearray(buf.raw), dtype=torch.uint8).to(self.device)
+        allh = [torch.empty_like(mine) for _ in range(self.P)]
+        dist.all_gather(allh, mine, group=group)
+        blob = torch.cat(allh).cpu().numpy().tobytes()
+        _lib.check(self._h, self.lib.epb_shard_connect(self._h, blob))
+
+    def set_timeout(self, max_polls):
+        _lib.check(self._h, self.lib.epb_shard_set_timeout(self._h, int(max_polls)))
+
+    def forward_peer(self, cells, density_band, potential_band, fx_band, fy_band, energy):
+        _lib.check(self._h, self.lib.epb_shard_forward_peer(
+            self._h, self._cells(cells), _stream_ptr(None, self.device), _ptr(density_band), _ptr(potential_band),
+            _ptr(fx_band), _ptr(fy_band), _ptr(energy)))
+
+    def backward_peer(self, cells, grad_out, grad_x, grad_y):
+        _lib.check(self._h, self.lib.epb_shard_backward_peer(self._h, self._cells(cells), _ptr(grad_out),
+                                                             _stream_ptr(None, self.device), _ptr(grad_x),
+                                                             _ptr(grad_y)))
+
+    def wait_test(self, max_polls):
+        _lib.check(self._h, self.lib.epb_shard_wait_test(self._h, _stream_ptr(None, self.device), int(max_polls)))
+
     def profile_start(self, max_calls):
         _lib.check(self._h, self.lib.epb_profile_start(self._h, int(max_calls)))
 
@@ -109,7 +141,7 @@ class EngineShard:
     def error_flags(self):
         f = ctypes.c_uint32()
         st = self.lib.epb_error_flags(self._h, _stream_ptr(None, self.device), ctypes.byref(f))
-        if st not in (_lib.EPB_OK, _lib.EPB_EOVERFLOW):
+        if st not in (_lib.EPB_OK, _lib.EPB_EOVERFLOW, _lib.EPB_ETIMEOUT):
             _lib.check(self._h, st)
         return int(f.value)
 
@@ -124,7 +156,7 @@ class ShardedElectricPotential:
     """Forward/backward of one grid over the ranks of a process group."""
 
     def __init__(self, num_bins_x, num_bins_y, xl, yl, xh, yh, max_cell_size_x, group=None, device=None,
-                 backend=None, fixed_point_bits=0):
+                 backend=None, fixed_point_bits=0, transport="nccl"):
         self.group = group
         self.P = dist.get_world_size(group)
         self.p = dist.get_rank(group)
@@ -149,6 +181,13 @@ class ShardedElectricPotential:
         self.fxy_ext = torch.zeros((RB + H) * N * 2, **f32)  # room for the largest halo of any rank
         self.energy = torch.zeros(1, dtype=torch.float64, device=self.device)
         self._Hsend = min(H, RB) if self.p > 0 else 0  # rows the previous band needs from us
+        if transport not in ("nccl", "peer"):
+            raise ValueError(f"transport must be 'nccl' or 'peer', not {transport!r}")
+        self.transport = transport
+        if transport == "peer":
+            # exchanges fused into the kernels: stores into the peers' buffers over NVLink
+            self.be.setup_peer(H if self.P > 1 else 0, group)
+            self.energy = torch.zeros(1, dtype=torch.float32, device=self.device)
 
     @property
     def row_range(self):
@@ -178,6 +217,9 @@ class ShardedElectricPotential:
         phi = band("potential", want_potential)
         fx = band("field_x", want_fields)
         fy = band("field_y", want_fields)
+        if self.transport == "peer":
+            self.be.forward_peer(cells, dens, phi, fx, fy, self.energy)
+            return {"density": dens, "potential": phi, "field_x": fx, "field_y": fy, "energy": self.energy}
         self.be.rows_forward(cells, dens, self.t1_send)
         dist.all_to_all_single(self.t1_recv, self.t1_send, group=self.group)
         self.be.columns(self.t1_recv, self.g_send, want_potential, self.energy)
@@ -196,7 +238,10 @@ class ShardedElectricPotential:
             grad_x = torch.zeros(n, dtype=torch.float32, device=self.device)
         if grad_y is None:
             grad_y = torch.zeros(n, dtype=torch.float32, device=self.device)
-        self.be.gather(cells, self.fxy_ext, self.H, grad_out, grad_x, grad_y)
+        if self.transport == "peer":
+            self.be.backward_peer(cells, grad_out, grad_x, grad_y)
+        else:
+            self.be.gather(cells, self.fxy_ext, self.H, grad_out, grad_x, grad_y)
         return grad_x, grad_y
 
     def close(self):

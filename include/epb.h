@@ -191,6 +191,34 @@ int epb_shard_rows_inverse(epb_handle* h, const float* g_recv, epb_stream stream
 int epb_shard_gather(epb_handle* h, const epb_cells* cells, const float* fxy_ext, int32_t halo_rows,
                      const float* grad_out, epb_stream stream, float* grad_x, float* grad_y);
 
+/* Peer transport: the same stages with the exchanges fused into the kernels.
+ * The row pass stores its blocks directly into every shard's column strip, the
+ * column pass its outputs directly into every shard's row-band buffer and the
+ * row-inverse pass its first halo rows into the previous shard's field halo,
+ * all as plain stores to peer memory over NVLink (CUDA IPC mappings; no
+ * multicast).  After each producer a one-thread kernel publishes an epoch in
+ * every shard's signal slots; a one-thread kernel waits for all shards'
+ * epochs before the consumer runs, with a bounded number of polls (about 5 s
+ * by default, epb_shard_set_timeout): when the bound is hit it sets
+ * EPB_FLAG_TIMEOUT and returns, and epb_error_flags reports EPB_ETIMEOUT.
+ * Every shard must call the peer forward (and backward) the same number of
+ * times.  Buffers live in the engine; set-up is:
+ *   epb_shard_peer_buffers(h, halo_rows, handles)  -> 4 cudaIpcMemHandle_t (256 bytes)
+ *   (exchange the handles of all shards, in shard order)
+ *   epb_shard_connect(h, all_handles)              <- P x 256 bytes
+ * The energy output of epb_shard_forward_peer is the total over all shards. */
+#define EPB_FLAG_TIMEOUT 0x8u
+int epb_shard_peer_buffers(epb_handle* h, int32_t halo_rows, void* handles_out);
+int epb_shard_connect(epb_handle* h, const void* all_handles);
+int epb_shard_set_timeout(epb_handle* h, int64_t max_polls);
+int epb_shard_forward_peer(epb_handle* h, const epb_cells* cells, epb_stream stream, float* density_band,
+                           float* potential_band, float* field_x_band, float* field_y_band, float* energy);
+int epb_shard_backward_peer(epb_handle* h, const epb_cells* cells, const float* grad_out, epb_stream stream,
+                            float* grad_x, float* grad_y);
+/* Test hook: waits for an epoch nobody publishes, so the bounded wait runs out
+ * after max_polls polls and EPB_FLAG_TIMEOUT is set (no GPU fault, no hang). */
+int epb_shard_wait_test(epb_handle* h, epb_stream stream, int64_t max_polls);
+
 /* Stage timing.  Stages, in launch order: */
 #define EPB_STAGE_SCATTER   0  /* cells -> fixed-point grid                          */
 #define EPB_STAGE_ROW_FWD   1  /* grid -> density (+ initial density) -> row DCT-II  */

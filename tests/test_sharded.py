@@ -129,3 +129,67 @@ def test_single_shard_stages_match_forward(cuda_device):
         assert float(e.item()) == pytest.approx(float(ref["energy"].item()), rel=1e-7)
     finally:
         be.close()
+
+
+@pytest.mark.gpu
+def test_bounded_wait_times_out_without_hanging(cuda_device):
+    """A wait for a signal nobody publishes runs out of polls, sets the timeout
+    flag and returns; the context stays usable."""
+    from dreamplacett_framework_b200 import _lib
+    from dreamplacett_framework_b200.sharded import EngineShard
+    be = EngineShard(64, 64, 0.0, 0.0, 640.0, 640.0, 1, 0, cuda_device)
+    try:
+        buf = __import__("ctypes").create_string_buffer(4 * _lib.IPC_HANDLE_BYTES)
+        _lib.check(be._h, be.lib.epb_shard_peer_buffers(be._h, 0, buf))
+        be.wait_test(2000)
+        assert be.error_flags() & _lib.EPB_FLAG_TIMEOUT
+        assert be.error_flags() == 0  # cleared; the GPU keeps working
+        x = torch.ones(10, device=cuda_device)
+        assert float(x.sum()) == 10.0
+    finally:
+        be.close()
+
+
+def _failing_worker(rank, world, port, out_dir):
+    """Rank 1 leaves before the first exchange; rank 0 must get an error from
+    its next collective (process-group timeout), not hang."""
+    import datetime
+    import sys
+    sys.path.insert(0, HERE)
+    sys.path.insert(0, os.path.join(os.path.dirname(HERE), "oracle"))
+    import build_oracle
+    build_oracle.build_oracle()
+    import oracle as o
+    from shard_cpu_backend import CpuShard
+    from dreamplacett_framework_b200.sharded import ShardedElectricPotential
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=5))
+    p = _small_placement()
+    be = CpuShard(o, p.num_bins_x, p.num_bins_y, p.xl, p.yl, p.xh, p.yh, world, rank)
+    sh = ShardedElectricPotential(p.num_bins_x, p.num_bins_y, p.xl, p.yl, p.xh, p.yh,
+                                  float(p.size_x_clamped.max()), device=torch.device("cpu"), backend=be)
+    if rank == 1:
+        os._exit(0)  # the rank disappears between steps, with nothing in flight
+    try:
+        sh.forward(_cells_cpu(p))
+        result = "no error"
+    except Exception as e:  # noqa: BLE001 - any collective error is the expected outcome
+        result = f"error: {type(e).__name__}"
+    with open(os.path.join(out_dir, "rank0.txt"), "w") as f:
+        f.write(result)
+    os._exit(0)
+
+
+def test_lost_rank_gives_error_not_hang(tmp_path):
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for pr in procs:
+        pr.start()
+    for pr in procs:
+        pr.join(timeout=120)
+    alive = [pr for pr in procs if pr.is_alive()]
+    for pr in alive:
+        pr.kill()
+    assert not alive, "a rank hung"
+    assert (tmp_path / "rank0.txt").read_text().startswith("error")

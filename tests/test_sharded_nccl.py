@@ -22,7 +22,7 @@ def _free_port():
     return port
 
 
-def _worker(rank, world, port, out_dir, grid, scale):
+def _worker(rank, world, port, out_dir, grid, scale, transport):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     from dreamplacett_framework_b200 import synth
     from dreamplacett_framework_b200.engine import CellTensors
@@ -38,7 +38,7 @@ def _worker(rank, world, port, out_dir, grid, scale):
         cells = CellTensors(t(p.x), t(p.y), t(p.size_x_clamped), t(p.size_y_clamped), t(p.offset_x),
                             t(p.offset_y), t(p.ratio), ranges=p.ranges)
         sh = ShardedElectricPotential(p.num_bins_x, p.num_bins_y, p.xl, p.yl, p.xh, p.yh,
-                                      float(p.size_x_clamped.max()), device=dev)
+                                      float(p.size_x_clamped.max()), device=dev, transport=transport)
         sh.set_initial_density(t(p.initial_density_norm()))
         for _ in range(2):  # the second call checks the band grid was left zeroed
             out = sh.forward(cells)
@@ -49,14 +49,16 @@ def _worker(rank, world, port, out_dir, grid, scale):
                  **{k: out[k].cpu().numpy() for k in ("density", "potential", "field_x", "field_y", "energy")},
                  gx=gx.cpu().numpy(), gy=gy.cpu().numpy(), flags=np.array(flags))
         dist.barrier()
+        torch.cuda.synchronize(dev)
     finally:
         if sh is not None:
             sh.close()
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("transport", ["nccl", "peer"])
 @pytest.mark.parametrize("grid,scale", [(1024, 0.2), (2048, 1.0)])
-def test_nccl_shards_match_single_gpu(cuda_device, tmp_path, grid, scale):
+def test_nccl_shards_match_single_gpu(cuda_device, tmp_path, grid, scale, transport):
     ngpu = torch.cuda.device_count()
     if ngpu < 2:
         pytest.skip("needs 2+ GPUs")
@@ -72,7 +74,8 @@ def test_nccl_shards_match_single_gpu(cuda_device, tmp_path, grid, scale):
         ref = {k: v.cpu().numpy() for k, v in eng.forward(cells).items()}
         rgx, rgy = (a.cpu().numpy() for a in eng.backward(cells))
     port = _free_port()
-    mp.start_processes(_worker, args=(world, port, str(tmp_path), grid, scale), nprocs=world, start_method="spawn")
+    mp.start_processes(_worker, args=(world, port, str(tmp_path), grid, scale, transport), nprocs=world,
+                       start_method="spawn")
     parts = [np.load(tmp_path / f"rank{r}.npz") for r in range(world)]
     np.testing.assert_array_equal(np.concatenate([q["density"] for q in parts]), ref["density"])
     rel = lambda a, b: float(np.max(np.abs(a - b)) / np.max(np.abs(b)))
