@@ -7,6 +7,7 @@
 // the per-function mapping.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -266,6 +267,20 @@ int launch_row_inv(epb_handle* h, const RowInvArgs& a, cudaStream_t st) {
 #undef CALL_RI
 }
 
+int col_width(int M) {
+    switch (M) {
+        case 16: return ColCfg<16>::W;
+        case 32: return ColCfg<32>::W;
+        case 64: return ColCfg<64>::W;
+        case 128: return ColCfg<128>::W;
+        case 256: return ColCfg<256>::W;
+        case 512: return ColCfg<512>::W;
+        case 1024: return ColCfg<1024>::W;
+        case 2048: return ColCfg<2048>::W;
+        default: return ColCfg<4096>::W;
+    }
+}
+
 int col_blocks(int M, int N) {
     int W = 4;
     switch (M) {
@@ -323,6 +338,7 @@ int launch_columns(epb_handle* h, const float* t1, const DstTable& g, bool want_
     ca.g = g;
     ca.ostride = (int64_t)h->RB * h->NB;
     ca.lrb = ilog2(h->RB);
+    ca.lsw = ilog2(std::min(col_width(h->M), h->NB));
     ca.col_base = h->col0;
     ca.ku = (float)(2.0 * M_PI / h->M);
     ca.kv = (float)(2.0 * M_PI / h->N * (double)(h->bsx / h->bsy));
@@ -341,6 +357,8 @@ int launch_rows_inverse(epb_handle* h, const float* g, float* potential, float* 
     ra.ostride = (int64_t)h->RB * h->NB;
     ra.qstride = 3 * (int64_t)h->RB * h->NB;
     ra.lnb = ilog2(h->NB);
+    ra.lsw = ilog2(std::min(col_width(h->M), h->NB));
+    ra.lrb = ilog2(h->RB);
     ra.fx = field_x; ra.fy = field_y; ra.phi = want_phi ? potential : nullptr; ra.fxy = fxy;
     ra.halo_dst = halo_dst; ra.halo_rows = halo_dst ? halo_rows : 0;
     ra.tw = h->twN; ra.qw = h->qwN; ra.M = h->RB; ra.want_phi = want_phi;

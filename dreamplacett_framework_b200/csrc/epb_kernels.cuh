@@ -19,9 +19,11 @@
 //   T1 (row pass -> column pass): block q (destination) = rows of my band, columns of
 //       band q: t1[q][r][c], r < RB, c < NB; after the all-to-all GPU q holds its
 //       column strip as [M][NB] (source bands stacked in row order).
-//   G (column pass -> row pass): g[d][o][r][c]: destination band d, output o
-//       (0 = field_x form, 1 = field_y form, 2 = potential form), band row r, local
-//       column c; after the all-to-all GPU d holds g[q][o][r][c] from each source q.
+//   G (column pass -> row pass): g[d][o][s][r][w]: destination band d, output o
+//       (0 = field_x form, 1 = field_y form, 2 = potential form), column strip s of
+//       SW columns, band row r, column w in the strip (local column c = s*SW + w).
+//       Strip-major so every column-pass CTA writes whole contiguous blocks; after
+//       the all-to-all GPU d holds g[q][o][s][r][w] from each source q.
 //
 // Transform conventions follow the reference's matrices
 // (host/density_scatter_ttnn_server_host.cpp:124-181):
@@ -181,10 +183,11 @@ struct ColCfg {
 
 struct ColArgs {
     const float* t1;        // column strip [M][N] (N = local strip width, the row stride)
-    DstTable g;             // outputs for destination band d at g.p[d][o*ostride + r*N + c]:
+    DstTable g;             // outputs for destination band d at g.p[d][o*ostride + (c>>lsw)*(RB<<lsw) + r*SW + (c&(SW-1))]:
                             //   o = 0 (2 IDXST_M)(auv*wu), 1 (2 IDCT_M)(auv*wv), 2 IDCT_M(auv*inv) (want_phi)
     int64_t ostride;        // elements between outputs o
-    int lrb;                // log2 rows per destination band
+    int lrb;                // log2 rows per destination band (RB)
+    int lsw;                // log2 strip width SW of the output layout
     int col_base;           // global index of local column 0
     float ku;               // wu = u * ku,  ku = 2 pi / M
     float kv;               // wv = v * kv,  kv = 2 pi / N * bsx / bsy
@@ -200,24 +203,10 @@ struct ColArgs {
 };
 
 // Eigenvalue weights (host/density_scatter_ttnn_server_host.cpp:252-263 and
-// DREAMPlace's inv_wu2_plus_wv2): inv = 1/(wu^2+wv^2), wuh = wu*inv/2,
-// wvh = wv*inv/2, all zero at (0, 0).
-__device__ __forceinline__ void spectral_weights(float wu, float wv, float& wuh, float& wvh, float& inv) {
-    const float d = wu * wu + wv * wv;
-    inv = d == 0.0f ? 0.0f : __frcp_rn(d);
-    wuh = wu * inv * 0.5f;
-    wvh = wv * inv * 0.5f;
-}
-
-// Spectral input of the three column inverses for one column at row index u:
-// r = 0: b_u = a_{L-u} (IDXST via IDCT), a = auv * wu_half   (the caller mirrors)
-// r = 1: 2 * auv * wv_half
-// r = 2: auv * inv
-__device__ __forceinline__ float col_weight(int r, float wu, float wv) {
-    float wuh, wvh, inv;
-    spectral_weights(wu, wv, wuh, wvh, inv);
-    return r == 0 ? wuh : (r == 1 ? 2.0f * wvh : inv);
-}
+// DREAMPlace's inv_wu2_plus_wv2): with inv = 1/(wu^2+wv^2) (0 at (0,0)) the
+// reference's wu/(wu^2+wv^2)/2 and wv/(wu^2+wv^2)/2 weights are applied in the
+// column pass as b*wu/2 and b*wv (the field chain's left factor 2 folded in),
+// b = auv * inv.
 
 // V_n = (A_n - i A_{L-n}) e^{i pi n / 2L} of two packed real sequences (p=0 real, p=1 imaginary)
 __device__ __forceinline__ float2 idct_pre(float an0, float am0, float an1, float am1, float2 q) {
@@ -233,7 +222,9 @@ k_col(ColArgs a) {
     constexpr int S = C::S, W = C::W, T = C::T, LP = C::LP;
     extern __shared__ float2 sm_col[];
     float2* buf = sm_col;                                   // S x LP complex
-    float* auv = reinterpret_cast<float*>(sm_col + S * LP); // W x L real (one column after another)
+    // b = auv / (wu^2 + wv^2) per column (W x L): the potential's spectrum; the field
+    // spectra are b * wu / 2 and b * wv, so no weight is evaluated twice
+    float* bsp = reinterpret_cast<float*>(sm_col + S * LP);
     const int N = a.N;
     const int c0 = blockIdx.x * W;
     float2* myseq = buf + (threadIdx.x / C::P) * LP;
@@ -266,21 +257,19 @@ k_col(ColArgs a) {
         const float2 q = __ldg(a.qw + u);
         const float xa = scale * (Va.x * q.x + Va.y * q.y);
         const float xb = scale * (Vb.x * q.x + Vb.y * q.y);
-        auv[(2 * s) * L + u] = xa;
-        auv[(2 * s + 1) * L + u] = xb;
         const float wu = (float)u * a.ku;
         const double cu = u == 0 ? 1.0 : 2.0;
 #pragma unroll
         for (int p = 0; p < 2; ++p) {
             const int col = c0 + 2 * s + p;
-            if (col < N) {
-                const int gcol = a.col_base + col;
-                const float wv = (float)gcol * a.kv;
-                float wuh, wvh, inv;
-                spectral_weights(wu, wv, wuh, wvh, inv);
-                const double x = p ? xb : xa;
-                esum += cu * (gcol == 0 ? 1.0 : 2.0) * (double)inv * x * x;
-            }
+            const int gcol = a.col_base + col;
+            const float wv = (float)gcol * a.kv;
+            const float d = wu * wu + wv * wv;
+            const float inv = d == 0.0f ? 0.0f : __frcp_rn(d);
+            const float x = p ? xb : xa;
+            const float b = x * inv;
+            bsp[(2 * s + p) * L + u] = b;
+            if (col < N) esum += cu * (gcol == 0 ? 1.0 : 2.0) * (double)x * (double)b;
         }
     }
     __syncthreads();
@@ -293,18 +282,23 @@ k_col(ColArgs a) {
             const int s = e / (L / 2), n = e % (L / 2);
             const int nm = L - n;  // partner index (L when n == 0)
             float An[2], Am[2];    // A_n, A_{L-n} of the two packed columns (A_L = 0)
+            const float hku = 0.5f * a.ku;
 #pragma unroll
             for (int p = 0; p < 2; ++p) {
                 const int cl = 2 * s + p;
                 const float wv = (float)(a.col_base + c0 + cl) * a.kv;
-                const float* au = auv + cl * L;
+                const float* bc = bsp + cl * L;
+                const float bn = bc[n], bm = n == 0 ? 0.0f : bc[nm];
                 if (r == 0) {
-                    // b_n = a_{L-n}, b_0 = b_L = 0, a_u = auv_u * wu_half(u)
-                    An[p] = n == 0 ? 0.0f : au[nm] * col_weight(0, (float)nm * a.ku, wv);
-                    Am[p] = n == 0 ? 0.0f : au[n] * col_weight(0, (float)n * a.ku, wv);
+                    // IDXST via IDCT of c_n = a_{L-n} (c_0 = c_L = 0), a_u = b_u * wu / 2
+                    An[p] = n == 0 ? 0.0f : bm * ((float)nm * hku);
+                    Am[p] = n == 0 ? 0.0f : bn * ((float)n * hku);
+                } else if (r == 1) {
+                    An[p] = bn * wv;   // 2 * auv * wv_half = b * wv
+                    Am[p] = bm * wv;
                 } else {
-                    An[p] = au[n] * col_weight(r, (float)n * a.ku, wv);
-                    Am[p] = n == 0 ? 0.0f : au[nm] * col_weight(r, (float)nm * a.ku, wv);
+                    An[p] = bn;
+                    Am[p] = bm;
                 }
             }
             float2* sq = buf + s * LP;
@@ -318,7 +312,8 @@ k_col(ColArgs a) {
                 for (int p = 0; p < 2; ++p) {
                     const int cl = 2 * s + p;
                     const float wv = (float)(a.col_base + c0 + cl) * a.kv;
-                    h[p] = auv[cl * L + L / 2] * col_weight(r, (float)(L / 2) * a.ku, wv);
+                    const float bh = bsp[cl * L + L / 2];
+                    h[p] = r == 0 ? bh * ((float)(L / 2) * hku) : (r == 1 ? bh * wv : bh);
                 }
                 sq[pidx(L / 2)] = idct_pre(h[0], h[0], h[1], h[1], __ldg(a.qw + L / 2));
             }
@@ -336,7 +331,8 @@ k_col(ColArgs a) {
             float2 v1 = buf[(2 * q4 + 1) * LP + src];
             if (r == 0 && (k & 1)) { v0.x = -v0.x; v0.y = -v0.y; v1.x = -v1.x; v1.y = -v1.y; }
             if (col < N)
-                *reinterpret_cast<float4*>(a.g.p[k >> a.lrb] + oo + (int64_t)(k & rbm) * N + col) =
+                *reinterpret_cast<float4*>(a.g.p[k >> a.lrb] + oo + ((int64_t)(col >> a.lsw) << (a.lrb + a.lsw)) +
+                                           ((int64_t)(k & rbm) << a.lsw) + (col & ((1 << a.lsw) - 1))) =
                     make_float4(v0.x, v0.y, v1.x, v1.y);
         }
         __syncthreads();
@@ -396,7 +392,9 @@ struct RowInvArgs {
     const float* g;          // g[q][o][r][c] from every source band q (see the layout note at the top)
     int64_t ostride;         // elements between outputs o
     int64_t qstride;         // elements between source bands q
-    int lnb;                 // log2 columns per band
+    int lnb;                 // log2 columns per band (NB)
+    int lsw;                 // log2 strip width of the layout
+    int lrb;                 // log2 rows per band
     float* fx; float* fy; float* phi;                   // nullable outputs, [M][N] of this band
     float2* fxy;                                        // interleaved fields [M][N] of this band
     float2* halo_dst;        // nullable: the previous band's field halo (its rows RB..), peer memory
@@ -408,8 +406,9 @@ struct RowInvArgs {
 
 // element l of band row r of column-pass output o
 __device__ __forceinline__ float rowinv_load(const RowInvArgs& a, int o, int r, int l) {
-    const int nb = 1 << a.lnb;
-    return __ldg(a.g + (int64_t)(l >> a.lnb) * a.qstride + (int64_t)o * a.ostride + (int64_t)r * nb + (l & (nb - 1)));
+    const int c = l & ((1 << a.lnb) - 1);
+    return __ldg(a.g + (int64_t)(l >> a.lnb) * a.qstride + (int64_t)o * a.ostride +
+                 ((int64_t)(c >> a.lsw) << (a.lrb + a.lsw)) + ((int64_t)r << a.lsw) + (c & ((1 << a.lsw) - 1)));
 }
 
 template <int L>

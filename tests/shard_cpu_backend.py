@@ -23,6 +23,22 @@ def _idxst(a, axis):
     return np.moveaxis(0.5 * sf.dst(b, type=3, axis=-1), -1, axis)
 
 
+def strip_width(M, NB):
+    """Strip width SW of the exchanged column-pass layout: the column kernel's
+    columns per CTA (ColCfg<M>::W = 2 * max(2, 4096 / M)), at most NB."""
+    return min(2 * max(2, 4096 // M), NB)
+
+
+def to_strips(a, SW):
+    """[RB][NB] -> strip-major [NB/SW][RB][SW], flattened."""
+    RB, NB = a.shape
+    return a.reshape(RB, NB // SW, SW).transpose(1, 0, 2).ravel()
+
+
+def from_strips(v, RB, NB, SW):
+    return v.reshape(NB // SW, RB, SW).transpose(1, 0, 2).reshape(RB, NB)
+
+
 class CpuShard:
     def __init__(self, oracle, M, N, xl, yl, xh, yh, P, p):
         self.o = oracle
@@ -74,14 +90,17 @@ class CpuShard:
         energy.copy_(torch.tensor([self.M * self.N / 4.0 * float(np.sum(cu * cv * inv * auv * auv))],
                                   dtype=torch.float64))
         out = []
+        SW = strip_width(self.M, self.NB)
         for dd in range(self.P):
             rows = slice(dd * self.RB, (dd + 1) * self.RB)
-            out += [gx[rows].ravel(), gy[rows].ravel(), gp[rows].ravel()]
+            out += [to_strips(gx[rows], SW), to_strips(gy[rows], SW), to_strips(gp[rows], SW)]
         g_send.copy_(torch.from_numpy(np.concatenate(out).astype(np.float32)))
 
     def rows_inverse(self, g_recv, potential_band, fx_band, fy_band, fxy_ext):
-        g = g_recv.numpy().reshape(self.P, 3, self.RB, self.NB)
-        band = [np.concatenate([g[q, o] for q in range(self.P)], axis=1).astype(np.float64) for o in range(3)]
+        SW = strip_width(self.M, self.NB)
+        g = g_recv.numpy().reshape(self.P, 3, self.RB * self.NB)
+        band = [np.concatenate([from_strips(g[q, o], self.RB, self.NB, SW) for q in range(self.P)],
+                               axis=1).astype(np.float64) for o in range(3)]
         fx = _idct(band[0], 1).astype(np.float32)
         fy = _idxst(band[1], 1).astype(np.float32)
         phi = _idct(band[2], 1).astype(np.float32)
