@@ -104,20 +104,23 @@ k_row_fwd(long long* __restrict__ qgrid,            // FROM_FIXED: [M][L] int64 
           const float* __restrict__ init,           // nullable [M][L]
           double dscale, int M,
           float* __restrict__ rho_out,              // nullable
-          DstTable t1dst,                           // column block q goes to t1dst.p[q][(drow0 + row) * nb + c]
+          const __grid_constant__ DstTable t1dst,   // column block q goes to t1dst.p[q][(drow0 + row) * nb + c]
           int lnb, int drow0,                       // log2 block width nb; first row of this band there
           const float2* __restrict__ tw, const float2* __restrict__ qw,
           unsigned* __restrict__ flags) {
     using C = RowFwdCfg<L>;
-    constexpr int S = C::S, T = C::T, LP = C::LP;
+    constexpr int S = C::S, T = C::T, LP = C::LP, P = C::P;
+    constexpr bool GS = GroupSync<L, S>::value;  // sequences run on their own barriers
     extern __shared__ float2 sm_rowfwd[];
     float2* buf = sm_rowfwd;
     const int row0 = blockIdx.x * C::ROWS;
+    const int grp = threadIdx.x / P, lane = threadIdx.x % P;
     unsigned sat = 0;
-    // element m of row (row0 + 2s + p) goes to sequence s at makhoul_pos(m), real (p=0) or imag (p=1)
+    // element m of row (row0 + 2s + p) goes to sequence s at makhoul_pos(m), real (p=0) or imag (p=1);
+    // with GS each group loads only its own sequence
 #pragma unroll 4
-    for (int e = threadIdx.x; e < S * L; e += T) {
-        const int s = e / L, m = e % L;
+    for (int e = GS ? lane : threadIdx.x; e < (GS ? L : S * L); e += (GS ? P : T)) {
+        const int s = GS ? grp : e / L, m = GS ? e : e % L;
         float vals[2];
 #pragma unroll
         for (int p = 0; p < 2; ++p) {
@@ -142,12 +145,12 @@ k_row_fwd(long long* __restrict__ qgrid,            // FROM_FIXED: [M][L] int64 
         buf[s * LP + pidx(makhoul_pos(m, L))] = make_float2(vals[0], vals[1]);
     }
     if (FROM_FIXED && sat) atomicOr(flags, kFlagSaturated);
-    __syncthreads();
-    fft_seq<L, false>(buf + (threadIdx.x / C::P) * LP, threadIdx.x % C::P, tw);
+    seq_sync<P, GS>(grp);
+    fft_seq<L, false, GS>(buf + grp * LP, lane, tw, true, grp);
     const float scale = 2.0f / (float)L;
 #pragma unroll 4
-    for (int e = threadIdx.x; e < S * L; e += T) {
-        const int s = e / L, k = e % L;
+    for (int e = GS ? lane : threadIdx.x; e < (GS ? L : S * L); e += (GS ? P : T)) {
+        const int s = GS ? grp : e / L, k = GS ? e : e % L;
         const float2 Z = buf[s * LP + pidx(k)];
         const float2 Zr = buf[s * LP + pidx((L - k) & (L - 1))];
         // Va = (Z + conj(Zr))/2 ; Vb = -i (Z - conj(Zr))/2
@@ -161,10 +164,11 @@ k_row_fwd(long long* __restrict__ qgrid,            // FROM_FIXED: [M][L] int64 
         if (ra + 1 < M) tb[(int64_t)(ra + 1) * nb] = scale * (Vb.x * q.x + Vb.y * q.y);
     }
     if (FROM_FIXED) {
-        // leave this CTA's rows of the grid zeroed for the next scatter
-        const int nrows = min(C::ROWS, M - row0);
-        longlong2* g2 = reinterpret_cast<longlong2*>(qgrid + (int64_t)row0 * L);
-        for (int e = threadIdx.x; e < nrows * L / 2; e += T) g2[e] = make_longlong2(0ll, 0ll);
+        // leave the rows this CTA (GS: this group) read zeroed for the next scatter
+        const int r0 = GS ? row0 + 2 * grp : row0;
+        const int nrows = min(GS ? 2 : C::ROWS, M - r0);
+        longlong2* g2 = reinterpret_cast<longlong2*>(qgrid + (int64_t)r0 * L);
+        for (int e = GS ? lane : threadIdx.x; e < nrows * L / 2; e += (GS ? P : T)) g2[e] = make_longlong2(0ll, 0ll);
     }
 }
 
@@ -219,7 +223,9 @@ template <int L>
 __global__ void __launch_bounds__(ColCfg<L>::T)
 k_col(ColArgs a) {
     using C = ColCfg<L>;
-    constexpr int S = C::S, W = C::W, T = C::T, LP = C::LP;
+    constexpr int S = C::S, W = C::W, T = C::T, LP = C::LP, P = C::P;
+    // CTA-wide phases: the strip's float4 loads and stores span both sequences of a CTA
+    constexpr bool GS = false;
     extern __shared__ float2 sm_col[];
     float2* buf = sm_col;                                   // S x LP complex
     // b = auv / (wu^2 + wv^2) per column (W x L): the potential's spectrum; the field
@@ -227,8 +233,9 @@ k_col(ColArgs a) {
     float* bsp = reinterpret_cast<float*>(sm_col + S * LP);
     const int N = a.N;
     const int c0 = blockIdx.x * W;
-    float2* myseq = buf + (threadIdx.x / C::P) * LP;
-    const int lane = threadIdx.x % C::P;
+    const int grp = threadIdx.x / P;
+    float2* myseq = buf + grp * LP;
+    const int lane = threadIdx.x % P;
 
     // ---- load T1 strip [L rows][W cols], Makhoul reorder along rows ----
 #pragma unroll 4
@@ -242,14 +249,14 @@ k_col(ColArgs a) {
         buf[s0 * LP + pos] = make_float2(v.x, v.y);
         buf[(s0 + 1) * LP + pos] = make_float2(v.z, v.w);
     }
-    __syncthreads();
-    fft_seq<L, false>(myseq, lane, a.tw);
+    seq_sync<P, GS>(grp);
+    fft_seq<L, false, GS>(myseq, lane, a.tw, true, grp);
 
     // ---- auv + energy ----
     const float scale = 2.0f / (float)L;
     double esum = 0.0;
-    for (int e = threadIdx.x; e < S * L; e += T) {
-        const int s = e / L, u = e % L;
+    for (int e = GS ? lane : threadIdx.x; e < (GS ? L : S * L); e += (GS ? P : T)) {
+        const int s = GS ? grp : e / L, u = GS ? e : e % L;
         const float2 Z = buf[s * LP + pidx(u)];
         const float2 Zr = buf[s * LP + pidx((L - u) & (L - 1))];
         const float2 Va = make_float2(0.5f * (Z.x + Zr.x), 0.5f * (Z.y - Zr.y));
@@ -272,14 +279,14 @@ k_col(ColArgs a) {
             if (col < N) esum += cu * (gcol == 0 ? 1.0 : 2.0) * (double)x * (double)b;
         }
     }
-    __syncthreads();
+    seq_sync<P, GS>(grp);
 
     // ---- three inverse transforms along x: 0 -> gx (IDXST form), 1 -> gy, 2 -> gp ----
     const int rounds = a.want_phi ? 3 : 2;
     for (int r = 0; r < rounds; ++r) {
         // build V for seq s = columns (2s, 2s+1); one thread makes V_n and V_{L-n}
-        for (int e = threadIdx.x; e < S * (L / 2); e += T) {
-            const int s = e / (L / 2), n = e % (L / 2);
+        for (int e = GS ? lane : threadIdx.x; e < (GS ? L / 2 : S * (L / 2)); e += (GS ? P : T)) {
+            const int s = GS ? grp : e / (L / 2), n = GS ? e : e % (L / 2);
             const int nm = L - n;  // partner index (L when n == 0)
             float An[2], Am[2];    // A_n, A_{L-n} of the two packed columns (A_L = 0)
             const float hku = 0.5f * a.ku;
@@ -318,8 +325,8 @@ k_col(ColArgs a) {
                 sq[pidx(L / 2)] = idct_pre(h[0], h[0], h[1], h[1], __ldg(a.qw + L / 2));
             }
         }
-        __syncthreads();
-        fft_seq<L, true>(myseq, lane, a.tw);
+        seq_sync<P, GS>(grp);
+        fft_seq<L, true, GS>(myseq, lane, a.tw, true, grp);
         const int64_t oo = (int64_t)r * a.ostride;
         const int rbm = (1 << a.lrb) - 1;
 #pragma unroll 4
@@ -339,6 +346,7 @@ k_col(ColArgs a) {
     }
 
     // ---- deterministic energy reduction: block partial, last block sums in order ----
+    __syncthreads();  // every group is done with its sequence before red[] reuses the buffer
     double* red = reinterpret_cast<double*>(sm_col);
     red[threadIdx.x] = esum;
     __syncthreads();
@@ -415,14 +423,17 @@ template <int L>
 __global__ void __launch_bounds__(RowInvCfg<L>::T, RowInvCfg<L>::MINB)
 k_row_inv(RowInvArgs a) {
     using C = RowInvCfg<L>;
-    constexpr int S = C::S, ROWS = C::ROWS, T = C::T, LP = C::LP;
+    constexpr int S = C::S, ROWS = C::ROWS, T = C::T, LP = C::LP, P = C::P;
+    constexpr bool GS = GroupSync<L, S>::value;  // sequences run on their own barriers
     extern __shared__ float2 sm_rowinv[];
     float2* buf = sm_rowinv;
     const int row0 = blockIdx.x * ROWS;
-    // one thread builds V_n and V_{L-n} from the same four loads
+    const int grp = threadIdx.x / P, lane = threadIdx.x % P;
+    // one thread builds V_n and V_{L-n} from the same four loads; with GS each
+    // group fills only its own sequence
 #pragma unroll 2
-    for (int e = threadIdx.x; e < S * (L / 2); e += T) {
-        const int s = e / (L / 2), n = e % (L / 2);
+    for (int e = GS ? lane : threadIdx.x; e < (GS ? L / 2 : S * (L / 2)); e += (GS ? P : T)) {
+        const int s = GS ? grp : e / (L / 2), n = GS ? e : e % (L / 2);
         const int nm = L - n;
         const int h = L / 2;
         float An[2] = {0.f, 0.f}, Am[2] = {0.f, 0.f}, Ah[2] = {0.f, 0.f};  // A_n, A_{L-n}, A_{L/2}
@@ -453,11 +464,11 @@ k_row_inv(RowInvArgs a) {
         if (n != 0) sq[pidx(nm)] = idct_pre(Am[0], An[0], Am[1], An[1], __ldg(a.qw + nm));
         else sq[pidx(h)] = idct_pre(Ah[0], Ah[0], Ah[1], Ah[1], __ldg(a.qw + h));
     }
-    __syncthreads();
-    fft_seq<L, true>(buf + (threadIdx.x / C::P) * LP, threadIdx.x % C::P, a.tw);
+    seq_sync<P, GS>(grp);
+    fft_seq<L, true, GS>(buf + grp * LP, lane, a.tw, true, grp);
 #pragma unroll 2
-    for (int e = threadIdx.x; e < S * L; e += T) {
-        const int s = e / L, l = e % L;
+    for (int e = GS ? lane : threadIdx.x; e < (GS ? L : S * L); e += (GS ? P : T)) {
+        const int s = GS ? grp : e / L, l = GS ? e : e % L;
         const float2 v = buf[s * LP + pidx(makhoul_pos(l, L))];
         if (s < ROWS) {
             const int row = row0 + s;

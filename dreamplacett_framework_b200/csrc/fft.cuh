@@ -50,6 +50,22 @@ __device__ __forceinline__ int pidx(int p) { return p + (p >> 4); }
 template <int L>
 struct Padded { static constexpr int value = L + L / 16; };
 
+// Barrier of one sequence's P threads (named barrier 1 + group) when GROUP,
+// else of the whole CTA.  With per-sequence barriers the sequences of a CTA
+// drift apart, so one group's loads overlap another group's arithmetic.
+template <int P, bool GROUP>
+__device__ __forceinline__ void seq_sync(int group) {
+    if constexpr (GROUP) {
+        asm volatile("bar.sync %0, %1;" ::"r"(group + 1), "r"(P) : "memory");
+    } else {
+        __syncthreads();
+    }
+}
+
+// Per-sequence barriers need whole warps per sequence and at most 15 groups.
+template <int L, int S>
+struct GroupSync { static constexpr bool value = (L / 16) % 32 == 0 && S <= 15; };
+
 // ---- small DFTs in registers, natural order in and out ----
 template <bool INV>
 __device__ __forceinline__ void dft2(float2* v) {
@@ -128,8 +144,8 @@ __device__ __forceinline__ void dft(float2* v) {
     else dft16<INV>(v);
 }
 
-template <int L, int R, int NS, bool INV>
-__device__ __forceinline__ void fft_pass(float2* seq, int lane, const float2* __restrict__ tw, bool active) {
+template <int L, int R, int NS, bool INV, bool GROUP>
+__device__ __forceinline__ void fft_pass(float2* seq, int lane, const float2* __restrict__ tw, bool active, int group) {
     constexpr int NB = L / R;      // butterflies per sequence
     constexpr int P = L / 16;      // threads per sequence
     constexpr int BPT = NB / P;    // butterflies per thread (16 / R)
@@ -142,7 +158,7 @@ __device__ __forceinline__ void fft_pass(float2* seq, int lane, const float2* __
             for (int r = 0; r < R; ++r) v[bb][r] = seq[pidx(b + r * NB)];
         }
     }
-    __syncthreads();
+    seq_sync<P, GROUP>(group);
 #pragma unroll
     for (int bb = 0; bb < BPT; ++bb) {
         if (!active) break;
@@ -161,25 +177,29 @@ __device__ __forceinline__ void fft_pass(float2* seq, int lane, const float2* __
 #pragma unroll
         for (int r = 0; r < R; ++r) seq[pidx(base + r * NS)] = v[bb][r];
     }
-    __syncthreads();
+    seq_sync<P, GROUP>(group);
 }
 
-template <int L, int NS, bool INV>
-__device__ __forceinline__ void fft_passes(float2* seq, int lane, const float2* __restrict__ tw, bool active) {
+template <int L, int NS, bool INV, bool GROUP>
+__device__ __forceinline__ void fft_passes(float2* seq, int lane, const float2* __restrict__ tw, bool active,
+                                           int group) {
     if constexpr (NS < L) {
         constexpr int REM = L / NS;
         constexpr int R = REM >= 16 ? 16 : REM;
-        fft_pass<L, R, NS, INV>(seq, lane, tw, active);
-        fft_passes<L, NS * R, INV>(seq, lane, tw, active);
+        fft_pass<L, R, NS, INV, GROUP>(seq, lane, tw, active, group);
+        fft_passes<L, NS * R, INV, GROUP>(seq, lane, tw, active, group);
     }
 }
 
 // Transform the padded sequence at `seq` in place; lane in [0, L/16).  Threads
 // with active == false skip the arithmetic but still meet every barrier.
-template <int L, bool INV>
-__device__ __forceinline__ void fft_seq(float2* seq, int lane, const float2* __restrict__ tw, bool active = true) {
+// GROUP selects per-sequence barriers (group = sequence index); the caller's
+// own phases around the FFT must then touch only this group's sequence.
+template <int L, bool INV, bool GROUP = false>
+__device__ __forceinline__ void fft_seq(float2* seq, int lane, const float2* __restrict__ tw, bool active = true,
+                                        int group = 0) {
     static_assert(L >= 16 && (L & (L - 1)) == 0, "power-of-two length >= 16");
-    fft_passes<L, 1, INV>(seq, lane, tw, active);
+    fft_passes<L, 1, INV, GROUP>(seq, lane, tw, active, group);
 }
 
 // Makhoul (1980) even/odd reordering used by both directions:
