@@ -9,9 +9,12 @@ plus the backward (per-cell gradients) over BASELINE config 3 by default:
 Inputs are seeded synthetic stand-ins for the ISPD-2005 designs.
 
 Timing: W untimed warm-up steps, then exactly K steps bracketed by a barrier
-and torch.cuda.synchronize() on both sides.  Each step is timed with CUDA
-events on the launching stream and L2 is flushed (a write of twice its size)
-between steps, outside the events.  Multi-GPU runs report the max over ranks.
+and torch.cuda.synchronize() on both sides.  Each timed step replays one
+captured CUDA graph of forward + backward (single GPU), is timed with CUDA
+events on the launching stream, and L2 is flushed (a write of twice its size)
+between steps, outside the events.  Per-kernel durations come from a separate
+eager pass with events between the kernels; `e2e` is eager API calls with host
+buffers.  Multi-GPU runs report the max over ranks.
 
 `--impl reference` times the CPU path instead (the oracle port: OpenMP
 fixed-point density, scipy.fft DCT chain, OpenMP gather) on all host cores,
@@ -371,6 +374,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
     ap.add_argument("--ref-seconds", type=float, default=120.0, help="reference arm time cap")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-loop", action="store_true", help="skip the C5 200-step placement-loop line item")
     ap.add_argument("--transport", default="peer", choices=["peer", "nccl"],
                     help="multi-GPU exchange: stores into peer memory fused into the kernels, or NCCL collectives")
     args = ap.parse_args()
@@ -445,26 +449,49 @@ def main():
         raise SystemExit("engine flagged non-finite cells during warm-up")
 
     K = args.steps
+    # per-kernel durations: an eager pass with CUDA events between the engine's kernels
+    K_prof = max(10, min(K, 500))
+    eng.profile_start(2 * K_prof)  # forward + backward per step
+    for _ in range(K_prof):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize(dev)
+    stages = eng.profile_stop()
+
+    # the timed steps replay one CUDA graph of forward + backward (the engine's calls are
+    # stream-ordered and allocation-free, so they capture as they are)
+    graph = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream(dev)
+    cap.wait_stream(stream)
+    with torch.cuda.stream(cap):
+        step()  # one eager call on the capture stream before capture
+    stream.wait_stream(cap)
+    torch.cuda.synchronize(dev)
+    with torch.cuda.graph(graph, stream=cap):
+        step()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize(dev)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
-    eng.profile_start(2 * K)  # forward + backward per step
     barrier()
     torch.cuda.synchronize(dev)
     t_wall0 = time.perf_counter()
     for i in range(K):
         flush.zero_()
         ev[i][0].record(stream)
-        step()
+        graph.replay()
         ev[i][1].record(stream)
     torch.cuda.synchronize(dev)
     barrier()
     t_wall1 = time.perf_counter()
-    stages = eng.profile_stop()
     step_ms = [a.elapsed_time(b) for a, b in ev]
     total_ms = sum(step_ms)
     clocks = sampler.summary(t_wall0, t_wall1)
     if clocks["samples"] < 3:  # timed region shorter than the sampling period: widen to warm-up
         clocks = sampler.summary(t_warm0, t_wall1)
         clocks["window"] = "warm-up and timed region"
+    if eng.error_flags() != 0:
+        raise SystemExit("engine flagged an error during the graph replays")
 
     # --- end to end through the engine API with host buffers (pos in, grad + energy out)
     pos_host = torch.empty(2 * n, dtype=torch.float32).pin_memory()
@@ -530,10 +557,24 @@ def main():
                     "h2d_bytes_per_step": 2 * n * 4, "d2h_bytes_per_step": 2 * n * 4 + 4,
                     "path": "engine API: pinned pos[2n] H2D, forward+backward, grad[2n] + energy D2H"},
             "gpu_launches": 5 * K,
+            "cuda_graph": "timed steps replay one captured graph of forward+backward; per-kernel "
+                          f"times from {K_prof} eager profiled steps; e2e is eager API calls",
             "clocks": clocks,
             "error_flags": flags,
             "wall_s_timed_region": t_wall1 - t_wall0,
         }
+        if world == 1 and not args.no_loop:
+            from dreamplacett_framework_b200.placement import DensityDescent
+            p5 = synth.make_placement("c5")
+            with DensityDescent(p5, device=dev) as loop:
+                r5 = loop.run(200, graph=True)
+            line["placement_loop"] = {
+                "workload": f"C5: {p5.num_cells} cells, {p5.num_bins_x}x{p5.num_bins_y} bins, 200 normalised "
+                            "density-descent steps (overflow + forward + backward + step per iteration, one "
+                            "CUDA graph per step, no host reads inside the loop)",
+                "ms_per_step": r5["ms"] / 200, "steps_per_s": 200 * 1000.0 / r5["ms"],
+                "overflow_first": float(r5["overflow"][0]), "overflow_final": float(r5["overflow"][-1]),
+                "max_density_final": float(r5["max_density"][-1]), "error_flags": r5["flags"]}
         if world == 1 and not args.no_cpu_baseline:
             nthreads = os.cpu_count() or 1
             cstep = cpu_step_factory(p, nthreads)

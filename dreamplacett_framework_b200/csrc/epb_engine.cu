@@ -17,6 +17,7 @@
 
 #include "../../include/epb.h"
 #include "epb_kernels.cuh"
+#include "placement_kernels.cuh"
 
 using namespace epb;
 
@@ -43,6 +44,10 @@ struct epb_handle {
     unsigned* counter = nullptr;
     double* energy_d = nullptr;
     unsigned* flags = nullptr;
+    // placement-loop scratch (epb_overflow, epb_descent_step)
+    double* ovf_partials = nullptr;   // [2 * kOvfMaxBlocks]
+    unsigned* ovf_counter = nullptr;
+    unsigned* linf_bits = nullptr;
     // peer transport (epb_shard_peer_buffers / epb_shard_connect)
     float* p_t1 = nullptr;      // t1_recv [M*NB]
     float* p_g = nullptr;       // g_recv [3*M*NB]
@@ -157,7 +162,8 @@ int dev_alloc(epb_handle* h, T** p, size_t count) {
 
 void free_all(epb_handle* h) {
     void* ptrs[] = {h->grid, h->init, h->t1, h->g, h->fxy, h->twM, h->qwM,
-                    h->twN, h->qwN, h->partials, h->counter, h->energy_d, h->flags};
+                    h->twN, h->qwN, h->partials, h->counter, h->energy_d, h->flags,
+                    h->ovf_partials, h->ovf_counter, h->linf_bits};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     for (int q = 0; q < kMaxShards; ++q) {
@@ -463,6 +469,9 @@ int create_handle(const epb_config* cfg, int P, int p, epb_handle** out) {
     if (!rc) rc = dev_alloc(h, &h->counter, 1);
     if (!rc) rc = dev_alloc(h, &h->energy_d, 1);
     if (!rc) rc = dev_alloc(h, &h->flags, 1);
+    if (!rc) rc = dev_alloc(h, &h->ovf_partials, 2 * (size_t)kOvfMaxBlocks);
+    if (!rc) rc = dev_alloc(h, &h->ovf_counter, 1);
+    if (!rc) rc = dev_alloc(h, &h->linf_bits, 1);
     if (rc) { free_all(h); delete h; return rc; }
 
     std::vector<float2> tw, qw;
@@ -475,6 +484,7 @@ int create_handle(const epb_config* cfg, int P, int p, epb_handle** out) {
     if (e == cudaSuccess) e = cudaMemcpy(h->qwN, qw.data(), qw.size() * sizeof(float2), cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemset(h->grid, 0, band * sizeof(long long));
     if (e == cudaSuccess) e = cudaMemset(h->counter, 0, sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMemset(h->ovf_counter, 0, sizeof(unsigned));
     if (e == cudaSuccess) e = cudaMemset(h->flags, 0, sizeof(unsigned));
     if (e == cudaSuccess) e = cudaMemset(h->energy_d, 0, sizeof(double));
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
@@ -616,6 +626,53 @@ int epb_gather(epb_handle* h, const epb_cells* cells, const float* field_x, cons
     k_gather<<<cell_blocks(v.n), 256, 0, (cudaStream_t)stream>>>(v, geom(h), nullptr, field_x, field_y, 0, h->M, 0, 0,
                                                                grad_out, grad_x, grad_y, h->flags);
     EPB_LAUNCHED(h, "k_gather launch");
+    return EPB_OK;
+}
+
+int epb_overflow(epb_handle* h, const epb_cells* cells, float target_density, epb_stream stream, double* out) {
+    if (!h) return EPB_EINVAL;
+    if (!out) return fail(h, EPB_EINVAL, "out is NULL");
+    if (!std::isfinite(target_density)) return fail(h, EPB_EINVAL, "target_density must be finite");
+    CellView v;
+    if (int rc = make_view(h, cells, v)) return rc;
+    DeviceGuard guard(h->dev);
+    cudaStream_t st = (cudaStream_t)stream;
+    const int64_t nbins = (int64_t)h->RB * h->N;
+    if (h->grid_dirty) {
+        EPB_CUDA(h, cudaMemsetAsync(h->grid, 0, (size_t)nbins * sizeof(long long), st));
+        h->grid_dirty = false;
+    }
+    h->grid_dirty = true;  // until k_overflow has consumed and re-zeroed it
+    if (int rc = scatter_into(h, v, st, h->grid)) return rc;
+    k_overflow<<<ovf_blocks(nbins), kOvfThreads, 0, st>>>(h->grid, h->has_init ? h->init : nullptr, h->dscale, nbins,
+                                                          target_density, (double)h->bsx * (double)h->bsy,
+                                                          h->ovf_partials, h->ovf_counter, out, h->flags);
+    EPB_LAUNCHED(h, "k_overflow launch");
+    h->grid_dirty = false;
+    return EPB_OK;
+}
+
+int epb_descent_step(epb_handle* h, const epb_cells* cells, float* x, float* y, const float* grad_x,
+                     const float* grad_y, const float* width, const float* height, float step_bins,
+                     epb_stream stream, float* grad_linf) {
+    if (!h) return EPB_EINVAL;
+    CellView v;
+    if (int rc = make_view(h, cells, v)) return rc;
+    if (!std::isfinite(step_bins) || step_bins < 0.0f) return fail(h, EPB_EINVAL, "step_bins must be finite and >= 0");
+    if (v.n > 0 && (!x || !y || !grad_x || !grad_y || !width || !height))
+        return fail(h, EPB_EINVAL, "x, y, grad_x, grad_y, width and height must be non-NULL");
+    DeviceGuard guard(h->dev);
+    cudaStream_t st = (cudaStream_t)stream;
+    EPB_CUDA(h, cudaMemsetAsync(h->linf_bits, 0, sizeof(unsigned), st));
+    if (v.n > 0) {
+        k_grad_linf<<<cell_blocks(v.n), 256, 0, st>>>(v, grad_x, grad_y, h->linf_bits, h->flags);
+        EPB_LAUNCHED(h, "k_grad_linf launch");
+    }
+    // the step lengths as fp32 products, the same rounding as the CPU restatement
+    const float step_x = step_bins * h->bsx, step_y = step_bins * h->bsy;
+    k_descent<<<cell_blocks(v.n), 256, 0, st>>>(v, x, y, grad_x, grad_y, width, height, h->linf_bits, step_x, step_y,
+                                                (float)h->xl, (float)h->yl, (float)h->xh, (float)h->yh, grad_linf);
+    EPB_LAUNCHED(h, "k_descent launch");
     return EPB_OK;
 }
 

@@ -68,13 +68,24 @@ struct Footprint {
 // Returns -1 for a non-finite cell (skipped and flagged), 0 when the cell
 // contributes nothing (non-positive size or off the die), 2 when it is outside
 // the row band [row_lo, row_hi) (owner == false: its rows do not meet the band;
-// owner == true: its first row is not in the band), 1 otherwise.  The x data is
-// read first so cells of other bands cost three loads, not seven.
+// owner == true: its first row is not in the band), 1 otherwise.
+//
+// On the whole grid every load is issued before any test (one memory round
+// trip per cell).  On a row band the x data is read first, so a cell of another
+// band costs three loads instead of seven; the test is uniform across the grid.
 __device__ __forceinline__ int cell_footprint(const CellView& c, const GridGeom& g, int64_t node,
                                               Footprint& f, int row_lo, int row_hi, bool owner) {
+    const bool banded = row_lo > 0 || row_hi < g.M;
     float x = __ldg(c.x + node);
     if (c.ox) x = __fadd_rn(x, __ldg(c.ox + node));
     const float sx = __ldg(c.sx + node);
+    float y = 0.0f, sy = 0.0f, r = 1.0f;
+    if (!banded) {
+        y = __ldg(c.y + node);
+        if (c.oy) y = __fadd_rn(y, __ldg(c.oy + node));
+        sy = __ldg(c.sy + node);
+        if (c.ratio) r = __ldg(c.ratio + node);
+    }
     if (!isfinite(x) || !isfinite(sx)) return -1;
     bool empty = !(sx > 0.0f);
     if (!empty) {
@@ -85,12 +96,14 @@ __device__ __forceinline__ int cell_footprint(const CellView& c, const GridGeom&
         if (!empty && (owner ? (f.kx0 < row_lo || f.kx0 >= row_hi) : (f.kx1 < row_lo || f.kx0 >= row_hi)))
             return 2;
     }
-    // the rest is read for cells of this band, and for empty cells so every
-    // non-finite input is reported as on one GPU
-    float y = __ldg(c.y + node);
-    if (c.oy) y = __fadd_rn(y, __ldg(c.oy + node));
-    const float sy = __ldg(c.sy + node);
-    const float r = c.ratio ? __ldg(c.ratio + node) : 1.0f;
+    if (banded) {
+        // the rest is read for cells of this band, and for empty cells so every
+        // non-finite input is reported as on one GPU
+        y = __ldg(c.y + node);
+        if (c.oy) y = __fadd_rn(y, __ldg(c.oy + node));
+        sy = __ldg(c.sy + node);
+        if (c.ratio) r = __ldg(c.ratio + node);
+    }
     if (!isfinite(y) || !isfinite(sy) || !isfinite(r)) return -1;
     if (empty || !(sy > 0.0f)) return 0;
     f.ey = __fadd_rn(y, sy);

@@ -226,6 +226,40 @@ class ElectricPotentialEngine:
         _lib.check(self._h, st)
         return grad_x, grad_y
 
+    def overflow(self, cells: CellTensors, target_density: float = 1.0, out: Optional[torch.Tensor] = None,
+                 stream=None) -> torch.Tensor:
+        """Device float64[2]: bin_area * sum_b max(rho_b - target, 0) and max_b rho_b
+        of the cells' density map plus the initial density (epb_overflow)."""
+        if out is None:
+            out = torch.empty(2, dtype=torch.float64, device=self.device)
+        if out.dtype != torch.float64 or out.device != self.device or out.numel() < 2 or not out.is_contiguous():
+            raise ValueError("out must be a contiguous float64 tensor of 2 elements on the engine's device")
+        st = self.lib.epb_overflow(self._h, self._cells(cells), float(target_density),
+                                   _stream_ptr(stream, self.device), _ptr(out))
+        _lib.check(self._h, st)
+        return out
+
+    def descent_step(self, cells: CellTensors, grad_x: torch.Tensor, grad_y: torch.Tensor, width: torch.Tensor,
+                     height: torch.Tensor, step_bins: float = 0.5, x: Optional[torch.Tensor] = None,
+                     y: Optional[torch.Tensor] = None, grad_linf: Optional[torch.Tensor] = None, stream=None):
+        """Normalised descent step in place on x, y (default: cells.x, cells.y)
+        for the nodes of the cells' ranges (epb_descent_step).  Returns the
+        device scalar max(|grad|) used to normalise."""
+        x = cells.x if x is None else x
+        y = cells.y if y is None else y
+        n = cells.num_nodes
+        for name, t in (("x", x), ("y", y), ("grad_x", grad_x), ("grad_y", grad_y), ("width", width),
+                        ("height", height)):
+            _check_f32(name, t, self.device, n)
+        if grad_linf is None:
+            grad_linf = torch.empty(1, dtype=torch.float32, device=self.device)
+        _check_f32("grad_linf", grad_linf, self.device, 1)
+        st = self.lib.epb_descent_step(self._h, self._cells(cells), _ptr(x), _ptr(y), _ptr(grad_x), _ptr(grad_y),
+                                       _ptr(width), _ptr(height), float(step_bins),
+                                       _stream_ptr(stream, self.device), _ptr(grad_linf))
+        _lib.check(self._h, st)
+        return grad_linf
+
     def profile_start(self, max_calls: int):
         """Record CUDA events between this engine's kernels for the next
         max_calls forward/backward calls (no host synchronisation)."""

@@ -219,6 +219,42 @@ int epb_shard_backward_peer(epb_handle* h, const epb_cells* cells, const float* 
  * after max_polls polls and EPB_FLAG_TIMEOUT is set (no GPU fault, no hang). */
 int epb_shard_wait_test(epb_handle* h, epb_stream stream, int64_t max_polls);
 
+/* ---- Global-placement loop pieces (the operator's callers) -------------
+ *
+ * Overflow metric.  Replaces the per-iteration overflow that the reference
+ * reads back from DREAMPlace's EvalMetrics on the host
+ * (integration/run_dreamplace.py:333-370; DREAMPlace computes it with its
+ * ElectricOverflow operator, which is not in the reference tree).  The cells
+ * (normally the movable range alone) are scattered exactly as by epb_forward,
+ * the normalised initial density is added, and with rho_b the resulting
+ * density-map value of bin b:
+ *   out[0] = bin_area * sum_b max(rho_b - target_density, 0)   (area units)
+ *   out[1] = max_b rho_b
+ * as two device doubles.  Overflow as the placer reports it is out[0] divided
+ * by the total movable area.  The sum is reduced in fp64 over a fixed
+ * partition of the grid (deterministic).  On a shard handle both cover the
+ * band's rows; combine the ranks with a sum and a max.  Stream-ordered, no
+ * host synchronisation; uses the handle's grid, so calls on one handle must
+ * not overlap with its forward. */
+int epb_overflow(epb_handle* h, const epb_cells* cells, float target_density, epb_stream stream, double* out);
+
+/* One normalised density-descent step of every node in the cells' ranges:
+ *   linf = max over those nodes of max(|grad_x|, |grad_y|)
+ *   x <- max(min(x - (step_bins * bin_size_x / linf) * grad_x, xh - width), xl)
+ *   y <- max(min(y - (step_bins * bin_size_y / linf) * grad_y, yh - height), yl)
+ * with each fp32 operation rounded once (no contraction).  Nodes with a
+ * non-finite gradient stay put and set EPB_FLAG_NONFINITE_CELL; nothing moves
+ * when linf is 0.  x, y, grad_*, width, height are node-indexed device arrays
+ * (DREAMPlace's pos[:n], pos[n:], its gradient halves and the unstretched node
+ * sizes).  grad_linf (nullable, device) receives linf.  This is the position
+ * update of the benchmark's 200-step density loop: the step that the
+ * reference's placer (DREAMPlace's Nesterov optimiser, driven from
+ * integration/run_dreamplace.py:315-331) takes between operator calls, reduced
+ * to its density term. */
+int epb_descent_step(epb_handle* h, const epb_cells* cells, float* x, float* y, const float* grad_x,
+                     const float* grad_y, const float* width, const float* height, float step_bins,
+                     epb_stream stream, float* grad_linf);
+
 /* Stage timing.  Stages, in launch order: */
 #define EPB_STAGE_SCATTER   0  /* cells -> fixed-point grid                          */
 #define EPB_STAGE_ROW_FWD   1  /* grid -> density (+ initial density) -> row DCT-II  */

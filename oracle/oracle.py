@@ -283,3 +283,86 @@ def electric_potential(cells: Cells, g: Geometry, S: int, init_norm=None, nthrea
     gx, gy = gather(cells, g, fx32, fy32, 1.0, nthreads=nthreads)
     sol.update(grid=grid, density=rho, grad_x=gx, grad_y=gy, bad=bad, saturated=sat)
     return sol
+
+
+# --------------------------------------------------------------------------
+# Global-placement loop pieces (the operator's callers)
+# --------------------------------------------------------------------------
+
+def overflow(cells: Cells, g: Geometry, S: int, init_norm=None, target=1.0, nthreads=1):
+    """(bin_area * sum_b max(rho_b - target, 0), max_b rho_b) of the cells'
+    fixed-point density map plus the initial density, in float64.
+
+    DREAMPlace's ElectricOverflow (not in the reference tree; the reference
+    reads its result per iteration in integration/run_dreamplace.py:333-370)
+    sums relu(density_map - target * bin_area) over bins; in normalised units
+    that is bin_area * sum relu(rho - target)."""
+    grid, _ = density_fixed(cells, g, S, nthreads=nthreads)
+    rho, _ = fixed_to_density(grid, g, S, init_norm)
+    ex = rho.astype(np.float64) - float(np.float32(target))
+    return float(np.sum(np.maximum(ex, 0.0))) * g.bin_area, float(rho.max())
+
+
+def descent_step(x, y, grad_x, grad_y, width, height, nodes, g: Geometry, step_bins=0.5):
+    """One normalised density-descent step in place (fp32, one rounding per
+    operation, as epb_descent_step):
+        linf = max over nodes of max(|gx|, |gy|) (finite gradients only)
+        x <- max(min(x - (step_bins*bsx / linf) * gx, xh - w), xl), same for y.
+    Returns linf (float32)."""
+    f32 = np.float32
+    gx, gy = grad_x[nodes], grad_y[nodes]
+    ok = np.isfinite(gx) & np.isfinite(gy)
+    linf = f32(0.0)
+    if ok.any():
+        linf = f32(max(np.max(np.abs(gx[ok])), np.max(np.abs(gy[ok]))))
+    if not linf > 0:
+        return linf
+    sx = f32(f32(step_bins) * f32(g.bsx)) / linf
+    sy = f32(f32(step_bins) * f32(g.bsy)) / linf
+    n = nodes[ok]
+    nx = x[n] - sx * grad_x[n]
+    ny = y[n] - sy * grad_y[n]
+    nx = np.maximum(np.minimum(nx, f32(g.xh) - width[n]), f32(g.xl))
+    ny = np.maximum(np.minimum(ny, f32(g.yh) - height[n]), f32(g.yl))
+    x[n] = nx.astype(np.float32)
+    y[n] = ny.astype(np.float32)
+    return linf
+
+
+def descent_trajectory(x, y, size_x, size_y, size_x_clamped, size_y_clamped, offset_x, offset_y, ratio,
+                       ranges, movable_range, g: Geometry, S: int, init_norm=None, steps=200, step_bins=0.5,
+                       target=1.0, lam0=8e-5, lam_every=50, nthreads=1, workers=1, solve_dtype=np.float64):
+    """The benchmark's density-only placement loop (config C5) on the CPU.
+
+    Per step t: electric-potential forward + backward of every scattered cell,
+    the overflow of the movable cells, then one normalised descent step of all
+    scattered cells; lambda_t = lam0 * 2^(t // lam_every) scales the reported
+    objective lambda_t * energy (it cancels in the normalised step).  Returns
+    per-step arrays (overflow ratio, max density, energy, objective, linf) and
+    the final positions; overflow has steps + 1 entries (the last one after
+    the final step)."""
+    x = np.array(x, dtype=np.float32, copy=True)
+    y = np.array(y, dtype=np.float32, copy=True)
+    (m0, m1) = movable_range
+    mov_area = float(np.sum(size_x[m0:m1].astype(np.float64) * size_y[m0:m1].astype(np.float64)))
+    ovf = np.zeros(steps + 1)
+    maxd = np.zeros(steps + 1)
+    energy = np.zeros(steps)
+    objective = np.zeros(steps)
+    linf = np.zeros(steps, dtype=np.float32)
+    for t in range(steps + 1):
+        mov = Cells(x, y, size_x_clamped, size_y_clamped, offset_x, offset_y, ratio, ranges=((m0, m1), (0, 0)))
+        a, mx = overflow(mov, g, S, init_norm, target, nthreads)
+        ovf[t], maxd[t] = a / mov_area, mx
+        if t == steps:
+            break
+        cells = Cells(x, y, size_x_clamped, size_y_clamped, offset_x, offset_y, ratio, ranges=ranges)
+        grid, _ = density_fixed(cells, g, S, nthreads=nthreads)
+        rho, _ = fixed_to_density(grid, g, S, init_norm)
+        sol = solve_fft(rho, g.bsx, g.bsy, workers, dtype=solve_dtype)
+        gx, gy = gather(cells, g, sol["field_x"].astype(np.float32), sol["field_y"].astype(np.float32), 1.0,
+                        nthreads=nthreads)
+        energy[t] = sol["energy"]
+        objective[t] = lam0 * 2.0 ** (t // lam_every) * sol["energy"]
+        linf[t] = descent_step(x, y, gx, gy, size_x, size_y, cells.nodes(), g, step_bins)
+    return dict(overflow=ovf, max_density=maxd, energy=energy, objective=objective, linf=linf, x=x, y=y)

@@ -61,12 +61,10 @@ class CpuShard:
     def rows_forward(self, cells, density_band, t1_send):
         grid, _ = self.o.density_fixed(self._ocells(cells), self.g, self.S)
         band = np.ascontiguousarray(grid[self.row0:self.row0 + self.RB])
-        gb = self.o.Geometry(self.RB, self.N, 0, 0, 1, 1)  # only M*N is used by the conversion
         rho = np.empty((self.RB, self.N), np.float32)
         self.o.lib().ora_fixed_to_density(band.ctypes.data_as(self.o._i64p),
                                           None if self.init is None else self.o._fp(self.init),
                                           self.RB * self.N, self.g.density_scale(self.S), self.o._fp(rho))
-        del gb
         if density_band is not None:
             density_band.copy_(torch.from_numpy(rho))
         t1 = _dct2(rho.astype(np.float64), 1)
