@@ -42,14 +42,14 @@ UNIT = "iters/s"
 # every grid the stage must touch, counted once (n = scattered cells, B = bins).
 #   scatter : x,y,size_x,size_y,offset_x,offset_y,ratio (28 B/cell) + int64 grid (8 B/bin)
 #   row_fwd : int64 grid read + re-zero (16) + initial density (4) + density out (4) + row DCT out (4)
-#   column  : row DCT in (4) + three column-pass outputs (12)
-#   row_inv : three column-pass maps in (12) + potential, field_x, field_y (12) + interleaved fields (8)
+#   column  : row DCT in (4) + two column-pass outputs (8: field_x form, potential form)
+#   row_inv : two column-pass maps in (8) + potential, field_x, field_y (12) + interleaved fields (8)
 #   gather  : cell arrays (28 B/cell) + gradient out (8 B/cell) + interleaved fields (8 B/bin)
 STAGE_BYTES = {
     "scatter": (28, 8),
     "row_fwd": (0, 28),
-    "column": (0, 16),
-    "row_inv": (0, 32),
+    "column": (0, 12),
+    "row_inv": (0, 28),
     "gather": (36, 8),
 }
 

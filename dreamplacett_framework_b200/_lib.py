@@ -23,6 +23,8 @@ EPB_FLAG_SATURATED = 0x2
 EPB_FLAG_HALO = 0x4
 EPB_FLAG_TIMEOUT = 0x8
 IPC_HANDLE_BYTES = 64
+# Column-pass outputs per bin in the exchanged layout (field_x form, potential form).
+COL_OUTPUTS = 2
 
 # Every symbol include/epb.h declares (the CPU tests check the exports).
 EXPORTS = (

@@ -36,7 +36,7 @@ struct epb_handle {
     float* init = nullptr;      // normalised initial density of this band [RB*N]
     bool has_init = false;
     float* t1 = nullptr;        // [M*N] row-DCT output (P == 1 only; shards use the caller's buffers)
-    float* g = nullptr;         // [3*M*N] column-pass outputs (P == 1 only)
+    float* g = nullptr;         // [kColOutputs*M*N] column-pass outputs (P == 1 only)
     float2* fxy = nullptr;      // interleaved fields of the last forward (P == 1 only)
     bool have_fields = false;
     float2 *twM = nullptr, *qwM = nullptr, *twN = nullptr, *qwN = nullptr;
@@ -50,8 +50,8 @@ struct epb_handle {
     unsigned* linf_bits = nullptr;
     // peer transport (epb_shard_peer_buffers / epb_shard_connect)
     float* p_t1 = nullptr;      // t1_recv [M*NB]
-    float* p_g = nullptr;       // g_recv [3*M*NB]
-    float* p_gsend = nullptr;   // column-pass blocks bound for other shards [3*M*NB]
+    float* p_g = nullptr;       // g_recv [kColOutputs*M*NB]
+    float* p_gsend = nullptr;   // column-pass blocks bound for other shards [kColOutputs*M*NB]
     float2* p_fxy = nullptr;    // fxy_ext [(RB+Hmax)*N]
     unsigned char* p_sig = nullptr;  // signal slots [3][kMaxShards] uint32, then energies [kMaxShards] double
     int p_halo = 0;             // halo rows this band receives (0 for the last band)
@@ -337,8 +337,7 @@ DstTable blocked(float* base, int64_t block, int P) {
 // Column pass: t1 = column strip [M][NB] of this handle's column band; g =
 // outputs laid out g[d][o][r][c] (d destination row band).  The energy of the
 // strip (times MN/4) lands in h->energy_d and, when given, energy_out.
-int launch_columns(epb_handle* h, const float* t1, const DstTable& g, bool want_phi, float* energy_out,
-                   cudaStream_t st) {
+int launch_columns(epb_handle* h, const float* t1, const DstTable& g, float* energy_out, cudaStream_t st) {
     ColArgs ca;
     ca.t1 = t1;
     ca.g = g;
@@ -350,7 +349,7 @@ int launch_columns(epb_handle* h, const float* t1, const DstTable& g, bool want_
     ca.kv = (float)(2.0 * M_PI / h->N * (double)(h->bsx / h->bsy));
     ca.tw = h->twM; ca.qw = h->qwM;
     ca.partials = h->partials; ca.counter = h->counter; ca.energy_d = h->energy_d;
-    ca.energy_out = energy_out; ca.N = h->NB; ca.want_phi = want_phi;
+    ca.energy_out = energy_out; ca.N = h->NB;
     ca.energy_scale = (double)h->M * (double)h->N / 4.0;
     return launch_col(h, ca, st);
 }
@@ -361,7 +360,8 @@ int launch_rows_inverse(epb_handle* h, const float* g, float* potential, float* 
     RowInvArgs ra;
     ra.g = g;
     ra.ostride = (int64_t)h->RB * h->NB;
-    ra.qstride = 3 * (int64_t)h->RB * h->NB;
+    ra.qstride = kColOutputs * (int64_t)h->RB * h->NB;
+    ra.kv = (float)(2.0 * M_PI / h->N * (double)(h->bsx / h->bsy));
     ra.lnb = ilog2(h->NB);
     ra.lsw = ilog2(std::min(col_width(h->M), h->NB));
     ra.lrb = ilog2(h->RB);
@@ -375,7 +375,7 @@ int launch_rows_inverse(epb_handle* h, const float* g, float* potential, float* 
 int solve_from_t1(epb_handle* h, cudaStream_t st, float* potential, float* field_x, float* field_y,
                   float* energy, ProfCall& pc) {
     const bool want_phi = potential != nullptr;
-    if (int rc = launch_columns(h, h->t1, blocked(h->g, 0, 1), want_phi, energy, st)) return rc;
+    if (int rc = launch_columns(h, h->t1, blocked(h->g, 0, 1), energy, st)) return rc;
     pc.end_stage(EPB_STAGE_COLUMN);
     if (int rc = launch_rows_inverse(h, h->g, potential, field_x, field_y, h->fxy, want_phi, st)) return rc;
     pc.end_stage(EPB_STAGE_ROW_INV);
@@ -458,7 +458,7 @@ int create_handle(const epb_config* cfg, int P, int p, epb_handle** out) {
     if (!rc) rc = dev_alloc(h, &h->init, band);
     if (P == 1) {
         if (!rc) rc = dev_alloc(h, &h->t1, MN);
-        if (!rc) rc = dev_alloc(h, &h->g, 3 * MN);
+        if (!rc) rc = dev_alloc(h, &h->g, kColOutputs * MN);
         if (!rc) rc = dev_alloc(h, &h->fxy, MN);
     }
     if (!rc) rc = dev_alloc(h, &h->twM, (size_t)h->M);
@@ -734,8 +734,8 @@ int epb_shard_columns(epb_handle* h, const float* t1_recv, epb_stream stream, fl
     cudaStream_t st = (cudaStream_t)stream;
     ProfCall pc(h, st);
     pc.begin();
-    if (int rc = launch_columns(h, t1_recv, blocked(g_send, 3 * (int64_t)h->RB * h->NB, h->P), want_potential != 0,
-                                nullptr, st))
+    (void)want_potential;  // the column pass produces the potential form in every case
+    if (int rc = launch_columns(h, t1_recv, blocked(g_send, kColOutputs * (int64_t)h->RB * h->NB, h->P), nullptr, st))
         return rc;
     pc.end_stage(EPB_STAGE_COLUMN);
     if (energy_partial)
@@ -794,8 +794,8 @@ int epb_shard_peer_buffers(epb_handle* h, int32_t halo_rows, void* handles_out) 
     const size_t sig_bytes = 3 * kMaxShards * sizeof(unsigned) + kMaxShards * sizeof(double) + 64;
     int rc = EPB_OK;
     if (!rc) rc = dev_alloc(h, &h->p_t1, strip);
-    if (!rc) rc = dev_alloc(h, &h->p_g, 3 * strip);
-    if (!rc && h->P > 1) rc = dev_alloc(h, &h->p_gsend, 3 * strip);
+    if (!rc) rc = dev_alloc(h, &h->p_g, kColOutputs * strip);
+    if (!rc && h->P > 1) rc = dev_alloc(h, &h->p_gsend, kColOutputs * strip);
     if (!rc) rc = dev_alloc(h, &h->p_fxy, (size_t)(h->RB + halo_rows) * h->N);
     if (!rc) rc = dev_alloc(h, &h->p_sig, sig_bytes);
     if (!rc) rc = dev_alloc(h, &h->energy_total, 1);
@@ -895,12 +895,12 @@ int epb_shard_forward_peer(epb_handle* h, const epb_cells* cells, epb_stream str
     // column outputs: this band's block in place, the other bands' blocks staged
     // locally (each row of a strip is only 4 columns wide) and pushed as whole
     // contiguous blocks into the peers' row-band buffers
-    const int64_t gblock = 3 * (int64_t)h->RB * h->NB;
+    const int64_t gblock = kColOutputs * (int64_t)h->RB * h->NB;
     DstTable g;
     for (int q = 0; q < kMaxShards; ++q)
         g.p[q] = q >= h->P ? nullptr : (q == h->p ? h->p_g + h->p * gblock : h->p_gsend + q * gblock);
     const bool want_phi = potential_band != nullptr;
-    if (int rc = launch_columns(h, h->p_t1, g, want_phi, nullptr, st)) return rc;
+    if (int rc = launch_columns(h, h->p_t1, g, nullptr, st)) return rc;
     if (h->P > 1) {
         PushArgs pa;
         pa.nblocks = 0;

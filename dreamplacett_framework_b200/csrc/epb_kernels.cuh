@@ -20,8 +20,8 @@
 //       band q: t1[q][r][c], r < RB, c < NB; after the all-to-all GPU q holds its
 //       column strip as [M][NB] (source bands stacked in row order).
 //   G (column pass -> row pass): g[d][o][s][r][w]: destination band d, output o
-//       (0 = field_x form, 1 = field_y form, 2 = potential form), column strip s of
-//       SW columns, band row r, column w in the strip (local column c = s*SW + w).
+//       (0 = field_x form, 1 = potential form), column strip s of SW columns, band
+//       row r, column w in the strip (local column c = s*SW + w).
 //       Strip-major so every column-pass CTA writes whole contiguous blocks; after
 //       the all-to-all GPU d holds g[q][o][s][r][w] from each source q.
 //
@@ -47,6 +47,11 @@ constexpr unsigned kFlagSaturated = 0x2u;
 constexpr unsigned kFlagHalo = 0x4u;       // a gathered footprint reached past the field halo
 constexpr unsigned kFlagTimeout = 0x8u;    // a wait for another GPU's signal gave up
 constexpr int kMaxShards = 8;
+// Outputs of the column pass per bin: the field_x form (IDXST_M of b*wu) and the
+// potential form (IDCT_M of b).  The field_y form IDCT_M(b*wv) is not a third
+// transform: wv depends on the column only, so it equals wv * IDCT_M(b), and the
+// row pass applies wv when it loads the potential form.
+constexpr int kColOutputs = 2;
 
 // Destination of each column block / row band of an exchanged buffer: this
 // GPU's send buffer (NCCL transport) or the peer's receive buffer mapped over
@@ -188,7 +193,7 @@ struct ColCfg {
 struct ColArgs {
     const float* t1;        // column strip [M][N] (N = local strip width, the row stride)
     DstTable g;             // outputs for destination band d at g.p[d][o*ostride + (c>>lsw)*(RB<<lsw) + r*SW + (c&(SW-1))]:
-                            //   o = 0 (2 IDXST_M)(auv*wu), 1 (2 IDCT_M)(auv*wv), 2 IDCT_M(auv*inv) (want_phi)
+                            //   o = 0 (2 IDXST_M)(auv*wu_half), 1 IDCT_M(auv*inv)
     int64_t ostride;        // elements between outputs o
     int lrb;                // log2 rows per destination band (RB)
     int lsw;                // log2 strip width SW of the output layout
@@ -202,15 +207,15 @@ struct ColArgs {
     double* energy_d;       // device double energy
     float* energy_out;      // nullable caller scalar
     int N;
-    int want_phi;
     double energy_scale;    // M*N/4
 };
 
 // Eigenvalue weights (host/density_scatter_ttnn_server_host.cpp:252-263 and
-// DREAMPlace's inv_wu2_plus_wv2): with inv = 1/(wu^2+wv^2) (0 at (0,0)) the
-// reference's wu/(wu^2+wv^2)/2 and wv/(wu^2+wv^2)/2 weights are applied in the
-// column pass as b*wu/2 and b*wv (the field chain's left factor 2 folded in),
-// b = auv * inv.
+// DREAMPlace's inv_wu2_plus_wv2): with inv = 1/(wu^2+wv^2) (0 at (0,0)) and
+// b = auv * inv, the reference's wu/(wu^2+wv^2)/2 weight is applied in the
+// column pass as b*wu/2 (the field chain's left factor 2 folded into the
+// IDXST), and its wv/(wu^2+wv^2)/2 weight in the row pass: (2 IDCT_M)(b*wv/2)
+// = wv * IDCT_M(b) because wv is constant along a column.
 
 // V_n = (A_n - i A_{L-n}) e^{i pi n / 2L} of two packed real sequences (p=0 real, p=1 imaginary)
 __device__ __forceinline__ float2 idct_pre(float an0, float am0, float an1, float am1, float2 q) {
@@ -281,9 +286,8 @@ k_col(ColArgs a) {
     }
     seq_sync<P, GS>(grp);
 
-    // ---- three inverse transforms along x: 0 -> gx (IDXST form), 1 -> gy, 2 -> gp ----
-    const int rounds = a.want_phi ? 3 : 2;
-    for (int r = 0; r < rounds; ++r) {
+    // ---- two inverse transforms along x: 0 -> gx (IDXST form), 1 -> gp ----
+    for (int r = 0; r < kColOutputs; ++r) {
         // build V for seq s = columns (2s, 2s+1); one thread makes V_n and V_{L-n}
         for (int e = GS ? lane : threadIdx.x; e < (GS ? L / 2 : S * (L / 2)); e += (GS ? P : T)) {
             const int s = GS ? grp : e / (L / 2), n = GS ? e : e % (L / 2);
@@ -292,17 +296,12 @@ k_col(ColArgs a) {
             const float hku = 0.5f * a.ku;
 #pragma unroll
             for (int p = 0; p < 2; ++p) {
-                const int cl = 2 * s + p;
-                const float wv = (float)(a.col_base + c0 + cl) * a.kv;
-                const float* bc = bsp + cl * L;
+                const float* bc = bsp + (2 * s + p) * L;
                 const float bn = bc[n], bm = n == 0 ? 0.0f : bc[nm];
                 if (r == 0) {
                     // IDXST via IDCT of c_n = a_{L-n} (c_0 = c_L = 0), a_u = b_u * wu / 2
                     An[p] = n == 0 ? 0.0f : bm * ((float)nm * hku);
                     Am[p] = n == 0 ? 0.0f : bn * ((float)n * hku);
-                } else if (r == 1) {
-                    An[p] = bn * wv;   // 2 * auv * wv_half = b * wv
-                    Am[p] = bm * wv;
                 } else {
                     An[p] = bn;
                     Am[p] = bm;
@@ -317,10 +316,8 @@ k_col(ColArgs a) {
                 float h[2];
 #pragma unroll
                 for (int p = 0; p < 2; ++p) {
-                    const int cl = 2 * s + p;
-                    const float wv = (float)(a.col_base + c0 + cl) * a.kv;
-                    const float bh = bsp[cl * L + L / 2];
-                    h[p] = r == 0 ? bh * ((float)(L / 2) * hku) : (r == 1 ? bh * wv : bh);
+                    const float bh = bsp[(2 * s + p) * L + L / 2];
+                    h[p] = r == 0 ? bh * ((float)(L / 2) * hku) : bh;
                 }
                 sq[pidx(L / 2)] = idct_pre(h[0], h[0], h[1], h[1], __ldg(a.qw + L / 2));
             }
@@ -382,7 +379,7 @@ k_col(ColArgs a) {
 
 // ---------------------------------------------------------------------------
 // Pass 3: inverse along y (rows).  ROWS rows per CTA; sequences:
-//   j < ROWS : fx row j (IDCT of Gx) + i * fy row j (IDXST of Gy)
+//   j < ROWS : fx row j (IDCT of Gx) + i * fy row j (IDXST of wv * Gp)
 //   then     : potential rows packed in pairs (IDCT of Gp)
 // ---------------------------------------------------------------------------
 template <int L>
@@ -398,6 +395,7 @@ struct RowInvCfg {
 
 struct RowInvArgs {
     const float* g;          // g[q][o][r][c] from every source band q (see the layout note at the top)
+    float kv;                // wv = v * kv for global column v (as in the column pass)
     int64_t ostride;         // elements between outputs o
     int64_t qstride;         // elements between source bands q
     int lnb;                 // log2 columns per band (NB)
@@ -441,21 +439,22 @@ k_row_inv(RowInvArgs a) {
             const int row = row0 + s;
             if (row < a.M) {
                 // fx: IDCT of the Gx row; fy: IDXST of the Gy row = IDCT of b (b_0 = 0,
-                // b_m = a_{L-m}) with the 1/2 folded in
+                // b_m = a_{L-m}) with the 1/2 folded in, Gy_l = wv_l * Gp_l
+                const float hkv = 0.5f * a.kv;
                 An[0] = rowinv_load(a, 0, row, n);
                 Am[0] = n == 0 ? 0.0f : rowinv_load(a, 0, row, nm);
-                An[1] = n == 0 ? 0.0f : 0.5f * rowinv_load(a, 1, row, nm);
-                Am[1] = n == 0 ? 0.0f : 0.5f * rowinv_load(a, 1, row, n);
-                if (n == 0) { Ah[0] = rowinv_load(a, 0, row, h); Ah[1] = 0.5f * rowinv_load(a, 1, row, h); }
+                An[1] = n == 0 ? 0.0f : rowinv_load(a, 1, row, nm) * ((float)nm * hkv);
+                Am[1] = n == 0 ? 0.0f : rowinv_load(a, 1, row, n) * ((float)n * hkv);
+                if (n == 0) { Ah[0] = rowinv_load(a, 0, row, h); Ah[1] = rowinv_load(a, 1, row, h) * ((float)h * hkv); }
             }
         } else if (a.want_phi) {
             const int row = row0 + 2 * (s - ROWS);
 #pragma unroll
             for (int p = 0; p < 2; ++p) {
                 if (row + p < a.M) {
-                    An[p] = rowinv_load(a, 2, row + p, n);
-                    Am[p] = n == 0 ? 0.0f : rowinv_load(a, 2, row + p, nm);
-                    if (n == 0) Ah[p] = rowinv_load(a, 2, row + p, h);
+                    An[p] = rowinv_load(a, 1, row + p, n);
+                    Am[p] = n == 0 ? 0.0f : rowinv_load(a, 1, row + p, nm);
+                    if (n == 0) Ah[p] = rowinv_load(a, 1, row + p, h);
                 }
             }
         }

@@ -176,8 +176,8 @@ class ShardedElectricPotential:
         f32 = dict(dtype=torch.float32, device=self.device)
         self.t1_send = torch.empty(RB * N, **f32)
         self.t1_recv = torch.empty(M * NB, **f32)
-        self.g_send = torch.empty(3 * M * NB, **f32)
-        self.g_recv = torch.empty(3 * M * NB, **f32)
+        self.g_send = torch.empty(_lib.COL_OUTPUTS * M * NB, **f32)
+        self.g_recv = torch.empty(_lib.COL_OUTPUTS * M * NB, **f32)
         self.fxy_ext = torch.zeros((RB + H) * N * 2, **f32)  # room for the largest halo of any rank
         self.energy = torch.zeros(1, dtype=torch.float64, device=self.device)
         self._Hsend = min(H, RB) if self.p > 0 else 0  # rows the previous band needs from us

@@ -161,9 +161,9 @@ int epb_error_flags(epb_handle* h, epb_stream stream, uint32_t* flags);
  * [p*NB, (p+1)*NB), RB = M/P, NB = N/P.  Buffers are caller-owned device arrays:
  *   t1_send  RB*N floats  block q = [RB][NB] rows of this band, columns of band q
  *   t1_recv  M*NB floats  after all-to-all(t1_send): block q = rows of band q (= [M][NB])
- *   g_send   3*M*NB       block d = [3][RB][NB]: outputs (field_x form, field_y form,
- *                          potential form) for band d's rows, columns of this band
- *   g_recv   3*M*NB       after all-to-all(g_send): block q = [3][RB][NB] from band q
+ *   g_send   2*M*NB       block d = [2][RB][NB]: outputs (field_x form, potential
+ *                          form) for band d's rows, columns of this band
+ *   g_recv   2*M*NB       after all-to-all(g_send): block q = [2][RB][NB] from band q
  *   fxy_ext  (RB+halo)*N*2 floats: interleaved (field_x, field_y) of this band,
  *                          then `halo` rows of the next band (point-to-point)
  * Every cell that overlaps the band is scattered (clipped to it), so the
@@ -179,7 +179,10 @@ int epb_shard_geometry(const epb_handle* h, int32_t* num_shards, int32_t* shard,
 int epb_shard_rows_forward(epb_handle* h, const epb_cells* cells, epb_stream stream, float* density_band,
                            float* t1_send);
 /* column DCT-II, weights, column inverses -> g_send; this strip's share of the
- * energy (double, device scalar, nullable) to be summed over shards */
+ * energy (double, device scalar, nullable) to be summed over shards.  Both
+ * outputs are produced whatever want_potential says (the field_y chain is
+ * derived from the potential form); the argument is kept for the caller's
+ * symmetry with epb_shard_rows_inverse. */
 int epb_shard_columns(epb_handle* h, const float* t1_recv, epb_stream stream, float* g_send, int32_t want_potential,
                       double* energy_partial);
 /* row inverses of this band from g_recv -> potential / field_x / field_y bands

@@ -81,8 +81,7 @@ class CpuShard:
         d = wu * wu + wv * wv
         inv = np.where(d == 0, 0.0, 1.0 / np.where(d == 0, 1.0, d))
         gx = 2.0 * _idxst(auv * wu * inv * 0.5, 0)
-        gy = 2.0 * _idct(auv * wv * inv * 0.5, 0)
-        gp = _idct(auv * inv, 0) if want_potential else np.zeros_like(auv)
+        gp = _idct(auv * inv, 0)  # the field_y form is wv * gp, applied in the row pass
         cu = np.where(u == 0, 1.0, 2.0)
         cv = np.where(v == 0, 1.0, 2.0)
         energy.copy_(torch.tensor([self.M * self.N / 4.0 * float(np.sum(cu * cv * inv * auv * auv))],
@@ -91,17 +90,19 @@ class CpuShard:
         SW = strip_width(self.M, self.NB)
         for dd in range(self.P):
             rows = slice(dd * self.RB, (dd + 1) * self.RB)
-            out += [to_strips(gx[rows], SW), to_strips(gy[rows], SW), to_strips(gp[rows], SW)]
+            out += [to_strips(gx[rows], SW), to_strips(gp[rows], SW)]
         g_send.copy_(torch.from_numpy(np.concatenate(out).astype(np.float32)))
 
     def rows_inverse(self, g_recv, potential_band, fx_band, fy_band, fxy_ext):
         SW = strip_width(self.M, self.NB)
-        g = g_recv.numpy().reshape(self.P, 3, self.RB * self.NB)
+        g = g_recv.numpy().reshape(self.P, 2, self.RB * self.NB)
         band = [np.concatenate([from_strips(g[q, o], self.RB, self.NB, SW) for q in range(self.P)],
-                               axis=1).astype(np.float64) for o in range(3)]
+                               axis=1).astype(np.float64) for o in range(2)]
+        v = np.arange(self.N)[None, :]
+        wv = 2 * np.pi * v / self.N * (self.g.bsx / self.g.bsy)
         fx = _idct(band[0], 1).astype(np.float32)
-        fy = _idxst(band[1], 1).astype(np.float32)
-        phi = _idct(band[2], 1).astype(np.float32)
+        fy = _idxst(wv * band[1], 1).astype(np.float32)
+        phi = _idct(band[1], 1).astype(np.float32)
         if fx_band is not None:
             fx_band.copy_(torch.from_numpy(fx))
             fy_band.copy_(torch.from_numpy(fy))
