@@ -92,6 +92,24 @@ k_scatter(CellView c, GridGeom g, float qscale, unsigned long long* __restrict__
 // S sequences of length L = N per CTA (two rows packed per sequence), P = L/16
 // threads per sequence.
 // ---------------------------------------------------------------------------
+// Minimum resident CTAs per SM requested from the compiler (a register cap) for
+// the three DCT passes; compile-time tuning knobs.  0 leaves the bound out:
+// ptxas then picks its own register budget, which differs from an explicit 1.
+#ifndef EPB_ROWFWD_MINB
+#define EPB_ROWFWD_MINB 4
+#endif
+#ifndef EPB_COL_MINB
+#define EPB_COL_MINB 2
+#endif
+#ifndef EPB_ROWINV_MINB
+#define EPB_ROWINV_MINB 3
+#endif
+#if EPB_ROWFWD_MINB > 0
+#define EPB_ROWFWD_BOUNDS(T) __launch_bounds__(T, EPB_ROWFWD_MINB)
+#else
+#define EPB_ROWFWD_BOUNDS(T) __launch_bounds__(T)
+#endif
+
 template <int L>
 struct RowFwdCfg {
     static constexpr int P = L / 16;
@@ -103,7 +121,7 @@ struct RowFwdCfg {
 };
 
 template <int L, bool FROM_FIXED>
-__global__ void __launch_bounds__(RowFwdCfg<L>::T)
+__global__ void EPB_ROWFWD_BOUNDS(RowFwdCfg<L>::T)
 k_row_fwd(long long* __restrict__ qgrid,            // FROM_FIXED: [M][L] int64 (zeroed after read)
           const float* __restrict__ rho_in,         // !FROM_FIXED: [M][L] fp32
           const float* __restrict__ init,           // nullable [M][L]
@@ -188,6 +206,8 @@ struct ColCfg {
     static constexpr int W = 2 * S;
     static constexpr int LP = Padded<L>::value;
     static constexpr size_t SMEM = (size_t)S * LP * sizeof(float2) + (size_t)W * L * sizeof(float);
+    // the register cap applies to the 256-thread configurations (L <= 2048)
+    static constexpr int MINB = T <= 256 ? EPB_COL_MINB : 1;
 };
 
 struct ColArgs {
@@ -217,6 +237,13 @@ struct ColArgs {
 // IDXST), and its wv/(wu^2+wv^2)/2 weight in the row pass: (2 IDCT_M)(b*wv/2)
 // = wv * IDCT_M(b) because wv is constant along a column.
 
+// Sum over a warp in a fixed order (lane 0 receives the total).
+__device__ __forceinline__ double warp_sum(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
+    return v;
+}
+
 // V_n = (A_n - i A_{L-n}) e^{i pi n / 2L} of two packed real sequences (p=0 real, p=1 imaginary)
 __device__ __forceinline__ float2 idct_pre(float an0, float am0, float an1, float am1, float2 q) {
     const float2 va = make_float2(an0 * q.x + am0 * q.y, an0 * q.y - am0 * q.x);
@@ -225,8 +252,8 @@ __device__ __forceinline__ float2 idct_pre(float an0, float am0, float an1, floa
 }
 
 template <int L>
-__global__ void __launch_bounds__(ColCfg<L>::T)
-k_col(ColArgs a) {
+__global__ void __launch_bounds__(ColCfg<L>::T, ColCfg<L>::MINB)
+k_col(const __grid_constant__ ColArgs a) {
     using C = ColCfg<L>;
     constexpr int S = C::S, W = C::W, T = C::T, LP = C::LP, P = C::P;
     // CTA-wide phases: the strip's float4 loads and stores span both sequences of a CTA
@@ -248,7 +275,8 @@ k_col(ColArgs a) {
         const int m = e / (W / 4), q4 = e % (W / 4);
         const int col = c0 + 4 * q4;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (col < N) v = __ldg(reinterpret_cast<const float4*>(a.t1 + (int64_t)m * N + col));
+        // read once per launch: keep it out of L1, which serves the twiddle table
+        if (col < N) v = __ldcg(reinterpret_cast<const float4*>(a.t1 + (int64_t)m * N + col));
         const int pos = pidx(makhoul_pos(m, L));
         const int s0 = 2 * q4;  // columns 4q4, 4q4+1 -> seq 2q4 ; 4q4+2, 4q4+3 -> seq 2q4+1
         buf[s0 * LP + pos] = make_float2(v.x, v.y);
@@ -282,6 +310,40 @@ k_col(ColArgs a) {
             const float b = x * inv;
             bsp[(2 * s + p) * L + u] = b;
             if (col < N) esum += cu * (gcol == 0 ? 1.0 : 2.0) * (double)x * (double)b;
+        }
+    }
+    // ---- deterministic energy reduction, done before the inverse rounds so the
+    //      fp64 partial is not live across them: warps, then the block in warp
+    //      order; the last block to finish sums the block partials in order ----
+    {
+        __shared__ double wred[T / 32];
+        __shared__ bool is_last;
+        const double v = warp_sum(esum);
+        if ((threadIdx.x & 31) == 0) wred[threadIdx.x >> 5] = v;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            double bsum = 0.0;
+            for (int w = 0; w < T / 32; ++w) bsum += wred[w];
+            a.partials[blockIdx.x] = bsum;
+            __threadfence();
+            const unsigned t = atomicInc(a.counter, gridDim.x - 1);
+            is_last = (t == gridDim.x - 1);
+        }
+        __syncthreads();
+        if (is_last) {
+            __threadfence();
+            double tot = 0.0;
+            for (int b = threadIdx.x; b < (int)gridDim.x; b += T) tot += __ldcg(a.partials + b);
+            tot = warp_sum(tot);
+            if ((threadIdx.x & 31) == 0) wred[threadIdx.x >> 5] = tot;
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                double e = 0.0;
+                for (int w = 0; w < T / 32; ++w) e += wred[w];
+                e *= a.energy_scale;
+                *a.energy_d = e;
+                if (a.energy_out) *a.energy_out = (float)e;
+            }
         }
     }
     seq_sync<P, GS>(grp);
@@ -341,40 +403,6 @@ k_col(ColArgs a) {
         }
         __syncthreads();
     }
-
-    // ---- deterministic energy reduction: block partial, last block sums in order ----
-    __syncthreads();  // every group is done with its sequence before red[] reuses the buffer
-    double* red = reinterpret_cast<double*>(sm_col);
-    red[threadIdx.x] = esum;
-    __syncthreads();
-    for (int w = T / 2; w > 0; w >>= 1) {
-        if (threadIdx.x < w) red[threadIdx.x] += red[threadIdx.x + w];
-        __syncthreads();
-    }
-    __shared__ bool is_last;
-    if (threadIdx.x == 0) {
-        a.partials[blockIdx.x] = red[0];
-        __threadfence();
-        const unsigned t = atomicInc(a.counter, gridDim.x - 1);
-        is_last = (t == gridDim.x - 1);
-    }
-    __syncthreads();
-    if (is_last) {
-        __threadfence();
-        double s = 0.0;
-        for (int b = threadIdx.x; b < (int)gridDim.x; b += T) s += __ldcg(a.partials + b);
-        red[threadIdx.x] = s;
-        __syncthreads();
-        for (int w = T / 2; w > 0; w >>= 1) {
-            if (threadIdx.x < w) red[threadIdx.x] += red[threadIdx.x + w];
-            __syncthreads();
-        }
-        if (threadIdx.x == 0) {
-            const double e = red[0] * a.energy_scale;
-            *a.energy_d = e;
-            if (a.energy_out) *a.energy_out = (float)e;
-        }
-    }
 }
 
 // ---------------------------------------------------------------------------
@@ -390,7 +418,7 @@ struct RowInvCfg {
     static constexpr int T = P * S;
     static constexpr int LP = Padded<L>::value;
     static constexpr size_t SMEM = (size_t)S * LP * sizeof(float2);
-    static constexpr int MINB = T <= 384 ? 3 : 1;
+    static constexpr int MINB = T <= 384 ? EPB_ROWINV_MINB : 1;
 };
 
 struct RowInvArgs {
