@@ -19,6 +19,9 @@ With `graph=True` one step is captured as a CUDA graph (the step index lives
 on the device) and replayed.
 
     python -m dreamplacett_framework_b200.placement [--config c5] [--steps 200]
+    python -m dreamplacett_framework_b200.placement --design benchmarks/configs/adaptec1_2048.json
+
+(--design takes a reference-style benchmark config naming a bookshelf design.)
 """
 from __future__ import annotations
 
@@ -155,9 +158,15 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--scale", type=float, default=1.0)
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--design", help="reference-style JSON config with aux_input (bookshelf files)")
     args = ap.parse_args()
-    from . import synth
-    p = synth.make_placement(args.config, scale=args.scale)
+    if args.design:
+        from . import bookshelf
+        p = bookshelf.placement_from_config(args.design)
+        args.config = p.name
+    else:
+        from . import synth
+        p = synth.make_placement(args.config, scale=args.scale)
     with DensityDescent(p) as loop:
         r = loop.run(args.steps, graph=not args.no_graph)
     every = max(1, args.steps // 10)

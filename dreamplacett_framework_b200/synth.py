@@ -196,7 +196,11 @@ def make_placement(config: str = "c1", scale: float = 1.0, grid: Optional[int] =
     bsx, bsy = p.bin_size_x, p.bin_size_y
     p.size_x_clamped, p.size_y_clamped, p.offset_x, p.offset_y, p.ratio = stretch(p.size_x, p.size_y, bsx, bsy)
     if len(mx):
-        p.initial_density_map = rasterise(mx, my, mw, mh, p.xl, p.yl, bsx, bsy, M, N)
+        # from the fp32 node arrays the engine is given, so every consumer sees one geometry
+        t = slice(n_mov, n_mov + len(mx))
+        p.initial_density_map = rasterise(p.x[t].astype(np.float64), p.y[t].astype(np.float64),
+                                          p.size_x[t].astype(np.float64), p.size_y[t].astype(np.float64),
+                                          p.xl, p.yl, bsx, bsy, M, N)
     else:
         p.initial_density_map = np.zeros((M, N), np.float64)
     return p
