@@ -142,14 +142,24 @@ unsigned cell_blocks(int64_t n) {
     return (unsigned)b;
 }
 
-// twiddles exp(-2 pi i t / L) and quarter-wave (cos, sin)(pi k / 2L), fp64 -> fp32
+// FFT twiddles in the per-pass [r][k] layout the device FFT reads (fft.cuh):
+// entry (pass NS, r, k) = exp(-2 pi i r k STEP / L), STEP = L / (NS R); and the
+// quarter-wave table (cos, sin)(pi k / 2L).  fp64 -> fp32.
 void host_tables(int L, std::vector<float2>& tw, std::vector<float2>& qw) {
-    tw.resize(L); qw.resize(L);
+    std::vector<float2> w(L);
+    qw.resize(L);
     for (int t = 0; t < L; ++t) {
         const double a = 2.0 * M_PI * (double)t / (double)L;
-        tw[t] = make_float2((float)std::cos(a), (float)(-std::sin(a)));
+        w[t] = make_float2((float)std::cos(a), (float)(-std::sin(a)));
         const double b = M_PI * (double)t / (2.0 * (double)L);
         qw[t] = make_float2((float)std::cos(b), (float)std::sin(b));
+    }
+    tw.assign(std::max(1, tw_table_size(L)), make_float2(1.0f, 0.0f));
+    for (int ns = 16; ns < L; ns *= 16) {
+        const int R = L / ns >= 16 ? 16 : L / ns;
+        const int step = L / (ns * R);
+        for (int r = 0; r < R; ++r)
+            for (int k = 0; k < ns; ++k) tw[tw_offset(L, ns) + r * ns + k] = w[(int64_t)r * k * step];
     }
 }
 
@@ -287,6 +297,13 @@ int col_width(int M) {
     }
 }
 
+// Columns per strip of the column-pass output layout: at least the column
+// kernel's width (so a CTA writes inside one strip) and kStripWidth (so the row
+// pass reads whole sectors), at most the column band.
+int strip_width(const epb_handle* h) {
+    return std::min(std::max(col_width(h->M), kStripWidth), h->NB);
+}
+
 int col_blocks(int M, int N) {
     int W = 4;
     switch (M) {
@@ -343,7 +360,7 @@ int launch_columns(epb_handle* h, const float* t1, const DstTable& g, float* ene
     ca.g = g;
     ca.ostride = (int64_t)h->RB * h->NB;
     ca.lrb = ilog2(h->RB);
-    ca.lsw = ilog2(std::min(col_width(h->M), h->NB));
+    ca.lsw = ilog2(strip_width(h));
     ca.col_base = h->col0;
     ca.ku = (float)(2.0 * M_PI / h->M);
     ca.kv = (float)(2.0 * M_PI / h->N * (double)(h->bsx / h->bsy));
@@ -363,7 +380,7 @@ int launch_rows_inverse(epb_handle* h, const float* g, float* potential, float* 
     ra.qstride = kColOutputs * (int64_t)h->RB * h->NB;
     ra.kv = (float)(2.0 * M_PI / h->N * (double)(h->bsx / h->bsy));
     ra.lnb = ilog2(h->NB);
-    ra.lsw = ilog2(std::min(col_width(h->M), h->NB));
+    ra.lsw = ilog2(strip_width(h));
     ra.lrb = ilog2(h->RB);
     ra.fx = field_x; ra.fy = field_y; ra.phi = want_phi ? potential : nullptr; ra.fxy = fxy;
     ra.halo_dst = halo_dst; ra.halo_rows = halo_dst ? halo_rows : 0;
@@ -461,9 +478,9 @@ int create_handle(const epb_config* cfg, int P, int p, epb_handle** out) {
         if (!rc) rc = dev_alloc(h, &h->g, kColOutputs * MN);
         if (!rc) rc = dev_alloc(h, &h->fxy, MN);
     }
-    if (!rc) rc = dev_alloc(h, &h->twM, (size_t)h->M);
+    if (!rc) rc = dev_alloc(h, &h->twM, (size_t)std::max(1, tw_table_size(h->M)));
     if (!rc) rc = dev_alloc(h, &h->qwM, (size_t)h->M);
-    if (!rc) rc = dev_alloc(h, &h->twN, (size_t)h->N);
+    if (!rc) rc = dev_alloc(h, &h->twN, (size_t)std::max(1, tw_table_size(h->N)));
     if (!rc) rc = dev_alloc(h, &h->qwN, (size_t)h->N);
     if (!rc) rc = dev_alloc(h, &h->partials, (size_t)ncolb);
     if (!rc) rc = dev_alloc(h, &h->counter, 1);

@@ -52,6 +52,13 @@ constexpr int kMaxShards = 8;
 // transform: wv depends on the column only, so it equals wv * IDCT_M(b), and the
 // row pass applies wv when it loads the potential form.
 constexpr int kColOutputs = 2;
+// Minimum strip width (columns) of the exchanged column-pass layout.  The row
+// pass reads a row as one run of kStripWidth floats per strip; the column pass
+// writes its W columns of a strip row as one 16-byte piece.
+#ifndef EPB_STRIP_WIDTH
+#define EPB_STRIP_WIDTH 8
+#endif
+constexpr int kStripWidth = EPB_STRIP_WIDTH;
 
 // Destination of each column block / row band of an exchanged buffer: this
 // GPU's send buffer (NCCL transport) or the peer's receive buffer mapped over
@@ -141,9 +148,59 @@ k_row_fwd(long long* __restrict__ qgrid,            // FROM_FIXED: [M][L] int64 
     unsigned sat = 0;
     // element m of row (row0 + 2s + p) goes to sequence s at makhoul_pos(m), real (p=0) or imag (p=1);
     // with GS each group loads only its own sequence
+    if constexpr (GS) {
+        // a batch of U elements per thread: every load of the batch is issued
+        // before any of them is used (no branch or store between them)
+        constexpr int U = 4;
+        static_assert((L / P) % U == 0, "whole batches");
+        const int ra = row0 + 2 * grp;
+        const bool ok0 = ra < M, ok1 = ra + 1 < M;
+        const int64_t off0 = (int64_t)(ok0 ? ra : 0) * L, off1 = (int64_t)(ok1 ? ra + 1 : 0) * L;
+        for (int m0 = lane; m0 < L; m0 += U * P) {
+            float va[U], vb[U];
+            if constexpr (FROM_FIXED) {
+                long long qa[U], qb[U];
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    qa[u] = qgrid[off0 + m0 + u * P];
+                    qb[u] = qgrid[off1 + m0 + u * P];
+                }
+                float ia[U], ib[U];
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    ia[u] = init ? __ldg(init + off0 + m0 + u * P) : 0.0f;
+                    ib[u] = init ? __ldg(init + off1 + m0 + u * P) : 0.0f;
+                }
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    if (qa[u] < 0 || qa[u] >= (1ll << 62) || qb[u] < 0 || qb[u] >= (1ll << 62)) sat = 1;
+                    va[u] = __double2float_rn(__dmul_rn(__ll2double_rn(qa[u]), dscale));
+                    vb[u] = __double2float_rn(__dmul_rn(__ll2double_rn(qb[u]), dscale));
+                    if (init) { va[u] = __fadd_rn(va[u], ia[u]); vb[u] = __fadd_rn(vb[u], ib[u]); }
+                }
+            } else {
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    va[u] = __ldg(rho_in + off0 + m0 + u * P);
+                    vb[u] = __ldg(rho_in + off1 + m0 + u * P);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int m = m0 + u * P;
+                if (!ok0) va[u] = 0.0f;
+                if (!ok1) vb[u] = 0.0f;
+                if (rho_out) {
+                    if (ok0) rho_out[off0 + m] = va[u];
+                    if (ok1) rho_out[off1 + m] = vb[u];
+                }
+                buf[grp * LP + pidx(makhoul_pos(m, L))] = make_float2(va[u], vb[u]);
+            }
+        }
+    } else {
 #pragma unroll 4
-    for (int e = GS ? lane : threadIdx.x; e < (GS ? L : S * L); e += (GS ? P : T)) {
-        const int s = GS ? grp : e / L, m = GS ? e : e % L;
+    for (int e = threadIdx.x; e < S * L; e += T) {
+        const int s = e / L, m = e % L;
         float vals[2];
 #pragma unroll
         for (int p = 0; p < 2; ++p) {
@@ -166,6 +223,7 @@ k_row_fwd(long long* __restrict__ qgrid,            // FROM_FIXED: [M][L] int64 
             vals[p] = v;
         }
         buf[s * LP + pidx(makhoul_pos(m, L))] = make_float2(vals[0], vals[1]);
+    }
     }
     if (FROM_FIXED && sat) atomicOr(flags, kFlagSaturated);
     seq_sync<P, GS>(grp);
@@ -220,7 +278,7 @@ struct ColArgs {
     int col_base;           // global index of local column 0
     float ku;               // wu = u * ku,  ku = 2 pi / M
     float kv;               // wv = v * kv,  kv = 2 pi / N * bsx / bsy
-    const float2* tw;       // FFT twiddles, length M
+    const float2* tw;       // per-pass FFT twiddle table of length-M transforms (fft.cuh)
     const float2* qw;       // quarter-wave table, length M
     double* partials;       // [gridDim.x] energy partial sums
     unsigned* counter;      // last-block counter (wraps to 0)
@@ -286,30 +344,50 @@ k_col(const __grid_constant__ ColArgs a) {
     fft_seq<L, false, GS>(myseq, lane, a.tw, true, grp);
 
     // ---- auv + energy ----
+    // One iteration handles the index pair (u, L-u) of one sequence (u = 0 handles
+    // the self-paired 0 and L/2): for two real columns packed as one FFT Z,
+    //   Va_u = (Z_u + conj(Z_{L-u}))/2,  Vb_u = -i (Z_u - conj(Z_{L-u}))/2,
+    // Va_{L-u} = conj(Va_u), Vb_{L-u} = conj(Vb_u), and the quarter-wave factor of
+    // L-u is that of u with cos and sin swapped.
     const float scale = 2.0f / (float)L;
     double esum = 0.0;
-    for (int e = GS ? lane : threadIdx.x; e < (GS ? L : S * L); e += (GS ? P : T)) {
-        const int s = GS ? grp : e / L, u = GS ? e : e % L;
+    for (int e = GS ? lane : threadIdx.x; e < (GS ? L / 2 : S * (L / 2)); e += (GS ? P : T)) {
+        const int s = GS ? grp : e / (L / 2), u = GS ? e : e % (L / 2);
+        const int u2 = u == 0 ? L / 2 : L - u;   // the second index of this iteration
         const float2 Z = buf[s * LP + pidx(u)];
-        const float2 Zr = buf[s * LP + pidx((L - u) & (L - 1))];
+        const float2 Zr = buf[s * LP + pidx(u == 0 ? 0 : L - u)];
+        const float2 Zh = u == 0 ? buf[s * LP + pidx(L / 2)] : make_float2(0.0f, 0.0f);
         const float2 Va = make_float2(0.5f * (Z.x + Zr.x), 0.5f * (Z.y - Zr.y));
         const float2 Vb = make_float2(0.5f * (Z.y + Zr.y), -0.5f * (Z.x - Zr.x));
         const float2 q = __ldg(a.qw + u);
-        const float xa = scale * (Va.x * q.x + Va.y * q.y);
-        const float xb = scale * (Vb.x * q.x + Vb.y * q.y);
-        const float wu = (float)u * a.ku;
-        const double cu = u == 0 ? 1.0 : 2.0;
+        float x1[2], x2[2];  // [column p]: values at u and at u2
+        x1[0] = scale * (Va.x * q.x + Va.y * q.y);
+        x1[1] = scale * (Vb.x * q.x + Vb.y * q.y);
+        if (u != 0) {
+            x2[0] = scale * (Va.x * q.y - Va.y * q.x);
+            x2[1] = scale * (Vb.x * q.y - Vb.y * q.x);
+        } else {
+            // index L/2 pairs with itself: Va = (Zh.x, 0), Vb = (Zh.y, 0)
+            const float2 qh = __ldg(a.qw + L / 2);
+            x2[0] = scale * (Zh.x * qh.x);
+            x2[1] = scale * (Zh.y * qh.x);
+        }
+        const float wu1 = (float)u * a.ku, wu2 = (float)u2 * a.ku;
+        const float cu1 = u == 0 ? 1.0f : 2.0f;
 #pragma unroll
         for (int p = 0; p < 2; ++p) {
             const int col = c0 + 2 * s + p;
             const int gcol = a.col_base + col;
             const float wv = (float)gcol * a.kv;
-            const float d = wu * wu + wv * wv;
-            const float inv = d == 0.0f ? 0.0f : __frcp_rn(d);
-            const float x = p ? xb : xa;
-            const float b = x * inv;
-            bsp[(2 * s + p) * L + u] = b;
-            if (col < N) esum += cu * (gcol == 0 ? 1.0 : 2.0) * (double)x * (double)b;
+            const float wv2 = wv * wv;
+            const float d1 = wu1 * wu1 + wv2, d2 = wu2 * wu2 + wv2;
+            const float b1 = d1 == 0.0f ? 0.0f : __fdividef(x1[p], d1);
+            const float b2 = __fdividef(x2[p], d2);
+            bsp[(2 * s + p) * L + u] = b1;
+            bsp[(2 * s + p) * L + u2] = b2;
+            // energy terms c_u c_v auv^2 / (wu^2 + wv^2), accumulated in fp64
+            const float cv = gcol == 0 ? 1.0f : 2.0f;
+            if (col < N) esum += (double)(cu1 * cv * (x1[p] * b1)) + (double)(2.0f * cv * (x2[p] * b2));
         }
     }
     // ---- deterministic energy reduction, done before the inverse rounds so the
@@ -433,7 +511,7 @@ struct RowInvArgs {
     float2* fxy;                                        // interleaved fields [M][N] of this band
     float2* halo_dst;        // nullable: the previous band's field halo (its rows RB..), peer memory
     int halo_rows;           // rows of this band that also go to halo_dst
-    const float2* tw; const float2* qw;                 // length N
+    const float2* tw; const float2* qw;                 // per-pass FFT twiddles, quarter-wave table (N)
     int M;                   // rows in this band
     int want_phi;
 };
@@ -457,6 +535,68 @@ k_row_inv(RowInvArgs a) {
     const int grp = threadIdx.x / P, lane = threadIdx.x % P;
     // one thread builds V_n and V_{L-n} from the same four loads; with GS each
     // group fills only its own sequence
+    if constexpr (GS) {
+        // group grp < ROWS: fx + i fy of band row row0 + grp (field_x form, wv * potential form);
+        // group ROWS + j: potential rows row0 + 2j, row0 + 2j + 1 (potential form).
+        // A batch of U indices per thread issues all its loads first; the partner index
+        // L - n wraps to 0 for n = 0 (a valid address) and the select below drops it.
+        const bool fxy_grp = grp < ROWS;
+        const int rA = fxy_grp ? row0 + grp : row0 + 2 * (grp - ROWS);
+        const int rB = fxy_grp ? rA : rA + 1;
+        const bool okA = rA < a.M && (fxy_grp || a.want_phi), okB = rB < a.M && (fxy_grp || a.want_phi);
+        const int oA = fxy_grp ? 0 : 1;                       // output read for the real part
+        const int lA = okA ? rA : 0, lB = okB ? rB : 0;
+        const float hkv = 0.5f * a.kv;
+        float2* sq = buf + grp * LP;
+        constexpr int H = L / 2;
+        if (lane == 0 && (fxy_grp || a.want_phi)) {
+            // V_{L/2} = (A_{L/2} - i A_{L/2}) e^{i pi / 4}
+            float hA = rowinv_load(a, oA, lA, H), hB = rowinv_load(a, 1, lB, H);
+            if (fxy_grp) hB *= (float)H * hkv;
+            if (!okA) hA = 0.0f;
+            if (!okB) hB = 0.0f;
+            sq[pidx(H)] = idct_pre(hA, hA, hB, hB, __ldg(a.qw + H));
+        }
+        constexpr int U = 4;
+        static_assert((H / P) % U == 0, "whole batches");
+        // a potential group with no potential wanted loads nothing (its transform is not stored)
+        const int n_end = fxy_grp || a.want_phi ? H : 0;
+        for (int n0 = lane; n0 < n_end; n0 += U * P) {
+            float an[U], am[U], bn[U], bm[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int n = n0 + u * P, nm = (L - n) & (L - 1);
+                an[u] = rowinv_load(a, oA, lA, n);
+                am[u] = rowinv_load(a, oA, lA, nm);
+                bn[u] = rowinv_load(a, 1, lB, n);
+                bm[u] = rowinv_load(a, 1, lB, nm);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int n = n0 + u * P, nm = L - n;
+                float An0, Am0, An1, Am1;
+                if (fxy_grp) {
+                    // fx: IDCT of the Gx row; fy: IDXST of the Gy row = IDCT of b (b_0 = 0,
+                    // b_m = a_{L-m}) with the 1/2 folded in, Gy_l = wv_l * Gp_l
+                    An0 = an[u];
+                    Am0 = am[u];
+                    An1 = bm[u] * ((float)nm * hkv);
+                    Am1 = bn[u] * ((float)n * hkv);
+                    if (n == 0) { Am0 = 0.0f; An1 = 0.0f; Am1 = 0.0f; }
+                } else {
+                    An0 = an[u];
+                    Am0 = am[u];
+                    An1 = bn[u];
+                    Am1 = bm[u];
+                    if (n == 0) { Am0 = 0.0f; Am1 = 0.0f; }
+                }
+                if (!okA) { An0 = 0.0f; Am0 = 0.0f; }
+                if (!okB) { An1 = 0.0f; Am1 = 0.0f; }
+                sq[pidx(n)] = idct_pre(An0, Am0, An1, Am1, __ldg(a.qw + n));
+                if (n != 0) sq[pidx(nm)] = idct_pre(Am0, An0, Am1, An1, __ldg(a.qw + nm));
+            }
+        }
+    } else {
 #pragma unroll 2
     for (int e = GS ? lane : threadIdx.x; e < (GS ? L / 2 : S * (L / 2)); e += (GS ? P : T)) {
         const int s = GS ? grp : e / (L / 2), n = GS ? e : e % (L / 2);
@@ -490,6 +630,7 @@ k_row_inv(RowInvArgs a) {
         sq[pidx(n)] = idct_pre(An[0], Am[0], An[1], Am[1], __ldg(a.qw + n));
         if (n != 0) sq[pidx(nm)] = idct_pre(Am[0], An[0], Am[1], An[1], __ldg(a.qw + nm));
         else sq[pidx(h)] = idct_pre(Ah[0], Ah[0], Ah[1], Ah[1], __ldg(a.qw + h));
+    }
     }
     seq_sync<P, GS>(grp);
     fft_seq<L, true, GS>(buf + grp * LP, lane, a.tw, true, grp);

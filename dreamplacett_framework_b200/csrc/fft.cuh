@@ -18,9 +18,12 @@
 // p + p/16 (one float2 of padding per 16), so the stride-16 writes of the
 // first pass and the stride-R reads of later passes spread over all banks.
 //
-// Twiddles come from a table tw[t] = exp(-2 pi i t / L), t < L, computed in
-// float64 on the host and rounded once to fp32 (no device sincosf).  INV
-// selects exp(+...) (unnormalised inverse DFT).
+// Twiddles: pass (R, NS) multiplies element r of butterfly b by w^(r*k*STEP),
+// k = b mod NS, STEP = L/(NS*R), w = exp(-2 pi i / L).  They are read from a
+// table laid out per pass as [r][k] (k fastest) so the lanes of a warp, which
+// hold consecutive k, read consecutive entries; the entries are the fp32
+// roundings of the float64 values computed on the host (no device sincosf).
+// INV selects exp(+...) (unnormalised inverse DFT) by conjugation.
 #pragma once
 #include <cstdint>
 
@@ -39,6 +42,16 @@ template <bool INV>
 __device__ __forceinline__ float2 mul_mi(float2 a) {
     return INV ? make_float2(-a.y, a.x) : make_float2(a.y, -a.x);
 }
+
+// Offset of pass NS's twiddle block in the per-pass table of length-L
+// transforms (passes NS = 16, 256, ... carry twiddles; block size R*NS).
+__host__ __device__ constexpr int tw_offset(int L, int NS) {
+    int off = 0;
+    for (int ns = 16; ns < NS; ns *= 16) off += (L / ns >= 16 ? 16 : L / ns) * ns;
+    return off;
+}
+// Entries of the whole per-pass twiddle table of a length-L transform.
+__host__ __device__ constexpr int tw_table_size(int L) { return tw_offset(L, L); }
 
 template <int L>
 struct Log2 { static constexpr int value = 1 + Log2<L / 2>::value; };
@@ -165,10 +178,10 @@ __device__ __forceinline__ void fft_pass(float2* seq, int lane, const float2* __
         const int b = lane + bb * P;
         const int k = b & (NS - 1);
         if (NS > 1) {
-            constexpr int STEP = L / (NS * R);
+            const float2* __restrict__ twp = tw + tw_offset(L, NS) + k;
 #pragma unroll
             for (int r = 1; r < R; ++r) {
-                const float2 w = __ldg(tw + r * k * STEP);
+                const float2 w = __ldg(twp + r * NS);
                 v[bb][r] = INV ? cmulc(v[bb][r], w) : cmul(v[bb][r], w);
             }
         }

@@ -25,8 +25,9 @@ def _idxst(a, axis):
 
 def strip_width(M, NB):
     """Strip width SW of the exchanged column-pass layout: the column kernel's
-    columns per CTA (ColCfg<M>::W = 2 * max(2, 4096 / M)), at most NB."""
-    return min(2 * max(2, 4096 // M), NB)
+    columns per CTA (ColCfg<M>::W = 2 * max(2, 4096 / M)) or 32 (kStripWidth),
+    whichever is larger, at most NB."""
+    return min(max(2 * max(2, 4096 // M), 32), NB)
 
 
 def to_strips(a, SW):
