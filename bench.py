@@ -59,11 +59,11 @@ STAGE_BYTES = {
 # build (profiles/c3_step_kernels_full.md); ncu flushes caches per launch, so
 # these are cold-cache figures.
 NCU_TRAFFIC_C3 = {
-    "scatter": 72.8e6,
-    "row_fwd": 61.6e6,
-    "column": 17.9e6,
-    "row_inv": 88.5e6,
-    "gather": 79.9e6,
+    "scatter": 72.7e6,
+    "row_fwd": 60.5e6,
+    "column": 16.8e6,
+    "row_inv": 60.4e6,
+    "gather": 79.8e6,
 }
 
 
