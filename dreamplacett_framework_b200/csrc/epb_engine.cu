@@ -48,6 +48,10 @@ struct epb_handle {
     double* ovf_partials = nullptr;   // [2 * kOvfMaxBlocks]
     unsigned* ovf_counter = nullptr;
     unsigned* linf_bits = nullptr;
+    // band selection of a shard's scatter / gather (k_band_select)
+    int* sel_list = nullptr;
+    int* sel_count = nullptr;
+    int64_t sel_cap = 0;
     // peer transport (epb_shard_peer_buffers / epb_shard_connect)
     float* p_t1 = nullptr;      // t1_recv [M*NB]
     float* p_g = nullptr;       // g_recv [kColOutputs*M*NB]
@@ -132,6 +136,7 @@ int make_view(epb_handle* h, const epb_cells* c, CellView& v) {
     v.x = c->x; v.y = c->y; v.sx = c->size_x; v.sy = c->size_y;
     v.ox = c->offset_x; v.oy = c->offset_y; v.ratio = c->ratio;
     v.b0 = c->begin0; v.n0 = n0; v.b1 = c->begin1; v.n = n0 + n1;
+    v.sel = nullptr; v.sel_n = nullptr;
     return EPB_OK;
 }
 
@@ -173,7 +178,7 @@ int dev_alloc(epb_handle* h, T** p, size_t count) {
 void free_all(epb_handle* h) {
     void* ptrs[] = {h->grid, h->init, h->t1, h->g, h->fxy, h->twM, h->qwM,
                     h->twN, h->qwN, h->partials, h->counter, h->energy_d, h->flags,
-                    h->ovf_partials, h->ovf_counter, h->linf_bits};
+                    h->ovf_partials, h->ovf_counter, h->linf_bits, h->sel_list, h->sel_count};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     for (int q = 0; q < kMaxShards; ++q) {
@@ -400,12 +405,59 @@ int solve_from_t1(epb_handle* h, cudaStream_t st, float* potential, float* field
     return EPB_OK;
 }
 
-int scatter_into(epb_handle* h, const CellView& v, cudaStream_t st, long long* grid) {
-    if (v.n == 0) return EPB_OK;
+// On a shard (P > 1): list the cells this band's scatter (mode 0) or gather
+// (mode 1) visits and point v at the list.  The list buffer grows with the cell
+// count (that call synchronises and allocates).
+int band_selection(epb_handle* h, CellView& v, int mode, cudaStream_t st) {
+    const int64_t nseg = (v.n + kSelChunk - 1) / kSelChunk;
+    if (v.n > h->sel_cap) {
+        EPB_CUDA(h, cudaStreamSynchronize(st));
+        if (h->sel_list) cudaFree(h->sel_list);
+        if (h->sel_count) cudaFree(h->sel_count);
+        h->sel_list = nullptr;
+        h->sel_count = nullptr;
+        h->sel_cap = 0;
+        if (int rc = dev_alloc(h, &h->sel_list, (size_t)(nseg * kSelChunk))) return rc;
+        if (int rc = dev_alloc(h, &h->sel_count, (size_t)nseg)) return rc;
+        h->sel_cap = v.n;
+    }
+    k_band_select<<<(unsigned)nseg, 256, 0, st>>>(v, geom(h), h->row0, h->row0 + h->RB, mode, h->sel_list,
+                                                  h->sel_count, h->flags);
+    EPB_LAUNCHED(h, "k_band_select launch");
+    v.sel = h->sel_list;
+    v.sel_n = h->sel_count;
+    return EPB_OK;
+}
+
+int scatter_into(epb_handle* h, const CellView& v0, cudaStream_t st, long long* grid) {
+    if (v0.n == 0) return EPB_OK;
+    if (v0.n >= ((int64_t)1 << 31)) return fail(h, EPB_EINVAL, "at most 2^31 - 1 cells");
     const float qscale = ldexpf(1.0f, h->S);
-    k_scatter<<<cell_blocks(v.n), 256, 0, st>>>(v, geom(h), qscale, (unsigned long long*)grid, h->row0,
-                                                h->row0 + h->RB, h->flags);
+    CellView v = v0;
+    unsigned blocks = cell_blocks(v.n);
+    if (h->P > 1) {
+        if (int rc = band_selection(h, v, 0, st)) return rc;
+        blocks = (unsigned)((v.n + kSelChunk - 1) / kSelChunk);   // one CTA per segment
+    }
+    k_scatter<<<blocks, 256, 0, st>>>(v, geom(h), qscale, (unsigned long long*)grid, h->row0, h->row0 + h->RB,
+                                      h->flags);
     EPB_LAUNCHED(h, "k_scatter launch");
+    return EPB_OK;
+}
+
+// Gather of a shard's own cells (first bin row in the band) from fields holding
+// rows [row0, row0 + RB + halo).
+int shard_gather(epb_handle* h, const CellView& v0, const float2* fxy, int halo, const float* grad_out,
+                 float* grad_x, float* grad_y, cudaStream_t st) {
+    CellView v = v0;
+    unsigned blocks = cell_blocks(v.n);
+    if (h->P > 1) {
+        if (int rc = band_selection(h, v, 1, st)) return rc;
+        blocks = (unsigned)((v.n + kSelChunk - 1) / kSelChunk);   // one CTA per segment
+    }
+    k_gather<<<blocks, 256, 0, st>>>(v, geom(h), fxy, nullptr, nullptr, h->row0, h->row0 + h->RB, halo, 1, grad_out,
+                                     grad_x, grad_y, h->flags);
+    EPB_LAUNCHED(h, "k_gather launch");
     return EPB_OK;
 }
 
@@ -789,10 +841,8 @@ int epb_shard_gather(epb_handle* h, const epb_cells* cells, const float* fxy_ext
     cudaStream_t st = (cudaStream_t)stream;
     ProfCall pc(h, st);
     pc.begin();
-    k_gather<<<cell_blocks(v.n), 256, 0, st>>>(v, geom(h), reinterpret_cast<const float2*>(fxy_ext), nullptr, nullptr,
-                                                h->row0, h->row0 + h->RB, halo_rows, 1, grad_out, grad_x, grad_y,
-                                                h->flags);
-    EPB_LAUNCHED(h, "k_gather launch");
+    if (int rc = shard_gather(h, v, reinterpret_cast<const float2*>(fxy_ext), halo_rows, grad_out, grad_x, grad_y, st))
+        return rc;
     pc.end_stage(EPB_STAGE_GATHER);
     return EPB_OK;
 }
@@ -955,9 +1005,7 @@ int epb_shard_backward_peer(epb_handle* h, const epb_cells* cells, const float* 
     cudaStream_t st = (cudaStream_t)stream;
     ProfCall pc(h, st);
     pc.begin();
-    k_gather<<<cell_blocks(v.n), 256, 0, st>>>(v, geom(h), h->p_fxy, nullptr, nullptr, h->row0, h->row0 + h->RB,
-                                                h->p_halo, 1, grad_out, grad_x, grad_y, h->flags);
-    EPB_LAUNCHED(h, "k_gather launch");
+    if (int rc = shard_gather(h, v, h->p_fxy, h->p_halo, grad_out, grad_x, grad_y, st)) return rc;
     pc.end_stage(EPB_STAGE_GATHER);
     return EPB_OK;
 }

@@ -73,13 +73,14 @@ struct DstTable {
 __global__ void __launch_bounds__(256)
 k_scatter(CellView c, GridGeom g, float qscale, unsigned long long* __restrict__ grid,
           int row0, int row1, unsigned* __restrict__ flags) {
-    // grid holds rows [row0, row1) of the density grid; footprints are clipped to them
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < c.n; i += stride) {
+    // grid holds rows [row0, row1) of the density grid; footprints are clipped to them.
+    // Cells of a selection are known to meet the band: they skip the band test.
+    const int blo = c.sel ? 0 : row0, bhi = c.sel ? g.M : row1;
+    for_each_cell(c, [&](int64_t node) {
         Footprint f;
-        const int st = cell_footprint(c, g, cell_node(c, i), f, row0, row1, false);
-        if (st < 0) { atomicOr(flags, kFlagNonFinite); continue; }
-        if (st != 1) continue;
+        const int st = cell_footprint(c, g, node, f, blo, bhi, false);
+        if (st < 0) { atomicOr(flags, kFlagNonFinite); return; }
+        if (st != 1) return;
         const int kxa = max(f.kx0, row0), kxb = min(f.kx1, row1 - 1);
         for (int kx = kxa; kx <= kxb; ++kx) {
             const float oxr = __fmul_rn(bin_overlap(f.x, f.ex, g.xl, g.bsx, kx), f.r);
@@ -91,7 +92,7 @@ k_scatter(CellView c, GridGeom g, float qscale, unsigned long long* __restrict__
                 if (q != 0) atomicAdd(row + ky, (unsigned long long)q);
             }
         }
-    }
+    });
 }
 
 // ---------------------------------------------------------------------------
@@ -658,6 +659,61 @@ k_row_inv(RowInvArgs a) {
 }
 
 // ---------------------------------------------------------------------------
+// Band selection (sharded grids): the cells a row band's scatter or gather
+// visits, listed so those kernels run full warps instead of testing every cell.
+// Only the x data is read.  mode 0: cells whose rows meet [row0, row1) (the
+// scatter; cells that contribute nothing go to the list of the band holding
+// row 0, which then reports their non-finite data); mode 1: cells whose first
+// row is in [row0, row1) (the gather).  Cells with non-finite x data are
+// flagged here.  Each CTA compacts a fixed segment of kSelChunk cells (no
+// global atomics); the consumers run one CTA per segment.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+k_band_select(CellView c, GridGeom g, int row0, int row1, int mode, int* __restrict__ list,
+              int* __restrict__ counts, unsigned* __restrict__ flags) {
+    // CTA s compacts cells [s * kSelChunk, (s + 1) * kSelChunk) into list[s * kSelChunk ...]
+    // in increasing order and writes their number to counts[s]
+    __shared__ int wtot[8];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t seg0 = (int64_t)blockIdx.x * kSelChunk;
+    int run = 0;
+    unsigned bad = 0;
+    for (int r = 0; r < kSelChunk / 256; ++r) {
+        const int64_t i = seg0 + r * 256 + threadIdx.x;
+        bool in = false;
+        if (i < c.n) {
+            const int64_t node = cell_node(c, i);
+            float x = __ldg(c.x + node);
+            if (c.ox) x = __fadd_rn(x, __ldg(c.ox + node));
+            const float sx = __ldg(c.sx + node);
+            if (!isfinite(x) || !isfinite(sx)) {
+                bad = 1;
+            } else {
+                const int kx0 = bin_floor(x, g.xl, g.bsx, g.ibsx, g.M);
+                const int kx1 = min(bin_floor(__fadd_rn(x, sx), g.xl, g.bsx, g.ibsx, g.M), g.M - 1);
+                const bool empty = !(sx > 0.0f) || kx0 > kx1;
+                if (mode == 0) in = empty ? row0 == 0 : !(kx1 < row0 || kx0 >= row1);
+                else in = !empty && kx0 >= row0 && kx0 < row1;
+            }
+        }
+        const unsigned m = __ballot_sync(0xffffffffu, in);
+        if (lane == 0) wtot[warp] = __popc(m);
+        __syncthreads();
+        int before = 0, total = 0;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+            before += w < warp ? wtot[w] : 0;
+            total += wtot[w];
+        }
+        if (in) list[seg0 + run + before + __popc(m & ((1u << lane) - 1u))] = (int)i;
+        run += total;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) counts[blockIdx.x] = run;
+    if (bad) atomicOr(flags, kFlagNonFinite);
+}
+
+// ---------------------------------------------------------------------------
 // Gather: grad[node] = -g * ratio * sum (ox*oy) * field
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256)
@@ -670,14 +726,14 @@ k_gather(CellView c, GridGeom g, const float2* __restrict__ fxy,
     // whose first bin row lies in [row0, row1) are computed and written; other
     // entries of grad_x / grad_y are left as they are.
     const float gscale = grad_out ? -__ldg(grad_out) : -1.0f;
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < c.n; i += stride) {
-        const int64_t node = cell_node(c, i);
+    // cells of a selection are the band's own cells: no band test
+    const int blo = c.sel ? 0 : row0, bhi = c.sel ? g.M : row1;
+    for_each_cell(c, [&](int64_t node) {
         Footprint f;
-        const int st = cell_footprint(c, g, node, f, row0, row1, owned_only != 0);
+        const int st = cell_footprint(c, g, node, f, blo, bhi, owned_only != 0);
         float ax = 0.0f, ay = 0.0f, r = 0.0f;
         if (st < 0) atomicOr(flags, kFlagNonFinite);
-        if (owned_only && st != 1) continue;
+        if (owned_only && st != 1) return;
         if (st == 1) {
             r = f.r;
             int kxb = f.kx1;
@@ -701,7 +757,7 @@ k_gather(CellView c, GridGeom g, const float2* __restrict__ fxy,
         const float s = gscale * r;
         grad_x[node] = s * ax;
         grad_y[node] = s * ay;
-    }
+    });
 }
 
 // ---------------------------------------------------------------------------

@@ -32,10 +32,33 @@ struct CellView {
     int64_t b0, n0;  // first range: nodes b0 .. b0+n0-1
     int64_t b1;      // second range starts at node b1
     int64_t n;       // total cells (n0 + second range length)
+    // optional selection: when sel is set, the cells visited are, for each
+    // segment s < ceil(n / kSelChunk), sel[s * kSelChunk + j] for j < sel_n[s]
+    // (cell indices in [0, n), increasing within a segment)
+    const int* __restrict__ sel;
+    const int* __restrict__ sel_n;
 };
+
+constexpr int kSelChunk = 2048;   // cells per selection segment
 
 __device__ __forceinline__ int64_t cell_node(const CellView& c, int64_t i) {
     return i < c.n0 ? c.b0 + i : c.b1 + (i - c.n0);
+}
+
+// Visit every cell of v (all cells, or the selected ones) with body(node), the
+// work spread over the grid: a grid-stride loop, or one segment per CTA.
+template <typename F>
+__device__ __forceinline__ void for_each_cell(const CellView& c, F&& body) {
+    if (c.sel) {
+        const int64_t nseg = (c.n + kSelChunk - 1) / kSelChunk;
+        for (int64_t s = blockIdx.x; s < nseg; s += gridDim.x) {
+            const int cnt = c.sel_n[s];
+            for (int j = threadIdx.x; j < cnt; j += blockDim.x) body(cell_node(c, c.sel[s * kSelChunk + j]));
+        }
+    } else {
+        const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+        for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < c.n; i += stride) body(cell_node(c, i));
+    }
 }
 
 __device__ __forceinline__ int bin_floor(float v, float origin, float bs, float ibs, int nb) {
