@@ -61,7 +61,7 @@ struct epb_handle {
     int p_halo = 0;             // halo rows this band receives (0 for the last band)
     int p_halo_max = 0;
     bool connected = false;
-    unsigned epoch = 0;
+    unsigned* epoch_dev = nullptr;  // step epoch of the peer signals (device: captured steps replay)
     float* peer_t1[kMaxShards] = {nullptr};
     float* peer_g[kMaxShards] = {nullptr};
     float2* peer_fxy[kMaxShards] = {nullptr};
@@ -188,7 +188,7 @@ void free_all(epb_handle* h) {
         if (h->peer_fxy[q]) cudaIpcCloseMemHandle(h->peer_fxy[q]);
         if (h->peer_sig[q]) cudaIpcCloseMemHandle(h->peer_sig[q]);
     }
-    void* own[] = {h->p_t1, h->p_g, h->p_gsend, h->p_fxy, h->p_sig, h->energy_total};
+    void* own[] = {h->p_t1, h->p_g, h->p_gsend, h->p_fxy, h->p_sig, h->energy_total, h->epoch_dev};
     for (void* p : own)
         if (p) cudaFree(p);
     for (cudaEvent_t e : h->prof_events) cudaEventDestroy(e);
@@ -866,8 +866,10 @@ int epb_shard_peer_buffers(epb_handle* h, int32_t halo_rows, void* handles_out) 
     if (!rc) rc = dev_alloc(h, &h->p_fxy, (size_t)(h->RB + halo_rows) * h->N);
     if (!rc) rc = dev_alloc(h, &h->p_sig, sig_bytes);
     if (!rc) rc = dev_alloc(h, &h->energy_total, 1);
+    if (!rc) rc = dev_alloc(h, &h->epoch_dev, 1);
     if (rc) return rc;
     EPB_CUDA(h, cudaMemset(h->p_sig, 0, sig_bytes));
+    EPB_CUDA(h, cudaMemset(h->epoch_dev, 0, sizeof(unsigned)));
     EPB_CUDA(h, cudaMemset(h->p_fxy, 0, (size_t)(h->RB + halo_rows) * h->N * sizeof(float2)));
     cudaIpcMemHandle_t* out = static_cast<cudaIpcMemHandle_t*>(handles_out);
     EPB_CUDA(h, cudaIpcGetMemHandle(&out[0], h->p_t1));
@@ -922,11 +924,11 @@ PeerSignals peer_signals(epb_handle* h) {
 
 int signal_and_wait(epb_handle* h, int stage, cudaStream_t st, const double* energy = nullptr,
                     float* energy_out = nullptr) {
-    k_signal<<<1, 32, 0, st>>>(peer_signals(h), h->P, h->p, stage, h->epoch, energy);
+    k_signal<<<1, 32, 0, st>>>(peer_signals(h), h->P, h->p, stage, h->epoch_dev, stage == 0 ? 1 : 0, energy);
     EPB_LAUNCHED(h, "k_signal launch");
     const double* my_energy = reinterpret_cast<const double*>(h->p_sig + 3 * kMaxShards * sizeof(unsigned));
-    k_wait<<<1, 32, 0, st>>>(reinterpret_cast<const unsigned*>(h->p_sig), h->P, stage, h->epoch, h->max_polls,
-                             my_energy, energy ? h->energy_total : nullptr, energy_out, 1.0, h->flags);
+    k_wait<<<1, 32, 0, st>>>(reinterpret_cast<const unsigned*>(h->p_sig), h->P, stage, h->epoch_dev, 0u,
+                             h->max_polls, my_energy, energy ? h->energy_total : nullptr, energy_out, 1.0, h->flags);
     EPB_LAUNCHED(h, "k_wait launch");
     return EPB_OK;
 }
@@ -941,7 +943,6 @@ int epb_shard_forward_peer(epb_handle* h, const epb_cells* cells, epb_stream str
     if (int rc = make_view(h, cells, v)) return rc;
     DeviceGuard guard(h->dev);
     cudaStream_t st = (cudaStream_t)stream;
-    h->epoch += 1;
     if (h->grid_dirty) {
         EPB_CUDA(h, cudaMemsetAsync(h->grid, 0, (size_t)h->RB * h->N * sizeof(long long), st));
         h->grid_dirty = false;
@@ -1015,9 +1016,9 @@ int epb_shard_wait_test(epb_handle* h, epb_stream stream, int64_t max_polls) {
     if (!h->p_sig) return fail(h, EPB_ENOSTATE, "epb_shard_peer_buffers first");
     DeviceGuard guard(h->dev);
     // an epoch no shard has published: the wait must run out and flag a timeout
-    k_wait<<<1, 32, 0, (cudaStream_t)stream>>>(reinterpret_cast<const unsigned*>(h->p_sig), h->P, 0,
-                                                h->epoch + 0x40000000u, (long long)max_polls, nullptr, nullptr,
-                                                nullptr, 1.0, h->flags);
+    k_wait<<<1, 32, 0, (cudaStream_t)stream>>>(reinterpret_cast<const unsigned*>(h->p_sig), h->P, 0, h->epoch_dev,
+                                                0x40000000u, (long long)max_polls, nullptr, nullptr, nullptr, 1.0,
+                                                h->flags);
     EPB_LAUNCHED(h, "k_wait launch");
     return EPB_OK;
 }

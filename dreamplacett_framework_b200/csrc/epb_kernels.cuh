@@ -794,8 +794,14 @@ struct PeerSignals {
     double* energy[kMaxShards];    // peer q's energy partials: [shard]
 };
 
-__global__ void k_signal(PeerSignals peers, int P, int p, int stage, unsigned epoch, const double* energy) {
+// The epoch lives in device memory (*epoch_dev) so that a captured step replays
+// with a fresh epoch: the stage-0 signal of a step (bump = 1) advances it, the
+// later signals and waits of the step read it.
+__global__ void k_signal(PeerSignals peers, int P, int p, int stage, unsigned* epoch_dev, int bump,
+                         const double* energy) {
     if (threadIdx.x != 0) return;
+    unsigned epoch = *epoch_dev;
+    if (bump) *epoch_dev = ++epoch;
     __threadfence_system();
     for (int q = 0; q < P; ++q) {
         if (energy) peers.energy[q][p] = *energy;
@@ -808,10 +814,11 @@ __global__ void k_signal(PeerSignals peers, int P, int p, int stage, unsigned ep
     __threadfence_system();
 }
 
-__global__ void k_wait(const unsigned* sig, int P, int stage, unsigned epoch, long long max_polls,
-                       const double* energy_in, double* energy_sum, float* energy_out, double energy_scale,
-                       unsigned* flags) {
+__global__ void k_wait(const unsigned* sig, int P, int stage, const unsigned* epoch_dev, unsigned epoch_add,
+                       long long max_polls, const double* energy_in, double* energy_sum, float* energy_out,
+                       double energy_scale, unsigned* flags) {
     if (threadIdx.x != 0) return;
+    const unsigned epoch = *epoch_dev + epoch_add;
     const volatile unsigned* row = sig + stage * kMaxShards;
     for (int q = 0; q < P; ++q) {
         long long polls = 0;
