@@ -56,7 +56,7 @@ STAGE_BYTES = {
 
 # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of each
 # engine kernel on the c3 workload, from one ncu --set full capture of this
-# build (profiles/c3_step_kernels_full.md); ncu flushes caches per launch, so
+# build (the kernel summary under profiles/); ncu flushes caches per launch, so
 # these are cold-cache figures.
 NCU_TRAFFIC_C3 = {
     "scatter": 72.7e6,
@@ -65,6 +65,31 @@ NCU_TRAFFIC_C3 = {
     "row_inv": 60.4e6,
     "gather": 79.8e6,
 }
+
+
+# 64-bit atomic adds per second on this pool's B200 for scatter-like footprints
+# (2x2, 2x3, 3x3 adds at hashed positions of a 2048 x 2048 int64 grid: 194-212 G/s),
+# measured by dreamplacett_framework_b200/csrc/probe_atomics.cu.  The scatter
+# issues one such add per (cell, bin) pair, so count / rate is its floor.
+ATOMIC_RATE_GOPS = 205.0
+
+
+def scatter_atomics(p):
+    """(cell, bin) pairs the scatter adds for placement p: footprint rows x
+    columns per scattered cell (bin indices as the kernel computes them, up to
+    exact-edge cases where an overlap is zero and no add is issued)."""
+    import numpy as np
+    (b0, e0), (b1, e1) = p.ranges
+    idx = np.concatenate([np.arange(b0, e0), np.arange(b1, e1)])
+    f = np.float32
+    x = (p.x[idx] + p.offset_x[idx]).astype(f)
+    y = (p.y[idx] + p.offset_y[idx]).astype(f)
+    bsx, bsy = f(p.bin_size_x), f(p.bin_size_y)
+    kx0 = np.clip(np.floor((x - f(p.xl)) / bsx), 0, p.num_bins_x - 1)
+    ky0 = np.clip(np.floor((y - f(p.yl)) / bsy), 0, p.num_bins_y - 1)
+    kx1 = np.clip(np.floor((x + p.size_x_clamped[idx] - f(p.xl)) / bsx), 0, p.num_bins_x - 1)
+    ky1 = np.clip(np.floor((y + p.size_y_clamped[idx] - f(p.yl)) / bsy), 0, p.num_bins_y - 1)
+    return int(np.sum((kx1 - kx0 + 1) * (ky1 - ky0 + 1)))
 
 
 def algorithmic_bytes(stage, n_cells, bins):
@@ -577,6 +602,14 @@ def main():
         roof = {"bound": "hbm", "kernel": dom, "achieved": kern[dom]["gbs"], "peak": peak, "unit": "GB/s",
                 "frac": kern[dom]["frac"],
                 "traffic": NCU_TRAFFIC_C3.get(dom) if args.config == "c3" else None, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"}
+        if "scatter" in kern:
+            # the scatter's own ceiling: one 64-bit atomic add per (cell, bin) at the probed rate
+            na = scatter_atomics(p)
+            floor_us = na / (ATOMIC_RATE_GOPS * 1e3)
+            kern["scatter"]["atomic_bound"] = {
+                "atomics": na, "rate_gops": ATOMIC_RATE_GOPS, "floor_us": floor_us,
+                "frac": floor_us / kern["scatter"]["avg_us"],
+                "rate_source": "dreamplacett_framework_b200/csrc/probe_atomics.cu on this pool's B200"}
         step_bytes = sum(algorithmic_bytes(k, p.num_cells, bins) for k in STAGE_BYTES)
         value = world * K / (total_ms / 1000.0)
         line = {
