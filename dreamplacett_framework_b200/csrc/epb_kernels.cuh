@@ -67,10 +67,27 @@ struct DstTable {
     float* p[kMaxShards];
 };
 
+// Register caps of the cell kernels (0 = no bound).
+#ifndef EPB_SCATTER_MINB
+#define EPB_SCATTER_MINB 0
+#endif
+#ifndef EPB_GATHER_MINB
+#define EPB_GATHER_MINB 6
+#endif
+#if EPB_SCATTER_MINB > 0
+#define EPB_SCATTER_BOUNDS __launch_bounds__(256, EPB_SCATTER_MINB)
+#else
+#define EPB_SCATTER_BOUNDS __launch_bounds__(256)
+#endif
+#if EPB_GATHER_MINB > 0
+#define EPB_GATHER_BOUNDS __launch_bounds__(256, EPB_GATHER_MINB)
+#else
+#define EPB_GATHER_BOUNDS __launch_bounds__(256)
+#endif
 // ---------------------------------------------------------------------------
 // Scatter
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256)
+__global__ void EPB_SCATTER_BOUNDS
 k_scatter(CellView c, GridGeom g, float qscale, unsigned long long* __restrict__ grid,
           int row0, int row1, unsigned* __restrict__ flags) {
     // grid holds rows [row0, row1) of the density grid; footprints are clipped to them.
@@ -716,7 +733,7 @@ k_band_select(CellView c, GridGeom g, int row0, int row1, int mode, int* __restr
 // ---------------------------------------------------------------------------
 // Gather: grad[node] = -g * ratio * sum (ox*oy) * field
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256)
+__global__ void EPB_GATHER_BOUNDS
 k_gather(CellView c, GridGeom g, const float2* __restrict__ fxy,
          const float* __restrict__ fx, const float* __restrict__ fy,  // planar alternative when fxy == nullptr
          int row0, int row1, int halo, int owned_only,
