@@ -4,8 +4,8 @@
 //   k_row_fwd<L>   grid (or fp32 density) -> normalised density rho (+ initial
 //                  density), then DCT-II along y of every row       -> T1
 //   k_col<L>       DCT-II along x of T1 columns -> auv; spectral energy;
-//                  weights wu/wv/inv; inverse transforms along x     -> Gx, Gy, Gp
-//   k_row_inv<L>   inverse transforms along y of Gx, Gy, Gp rows     -> field_x,
+//                  weights wu/wv/inv; inverse transforms along x     -> Gx, Gp
+//   k_row_inv<L>   inverse transforms along y of Gx, wv * Gp, Gp rows -> field_x,
 //                  field_y, potential (+ interleaved field map for the gather)
 //   k_gather       cells + interleaved fields -> per-node gradient
 //

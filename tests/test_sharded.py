@@ -95,6 +95,7 @@ def test_gloo_ranks_match_oracle(oracle, tmp_path, world):
 @pytest.mark.gpu
 def test_single_shard_stages_match_forward(cuda_device):
     """P = 1: the shard stages run the same kernels as epb_forward/epb_backward."""
+    from dreamplacett_framework_b200 import _lib
     from dreamplacett_framework_b200.engine import ElectricPotentialEngine
     from dreamplacett_framework_b200.sharded import EngineShard
     p = synth.make_placement("c3", scale=0.1, grid=1024)
@@ -113,7 +114,7 @@ def test_single_shard_stages_match_forward(cuda_device):
         f = lambda *s: torch.empty(*s, dtype=torch.float32, device=cuda_device)
         dens, phi, fx, fy = f(M, N), f(M, N), f(M, N), f(M, N)
         t1 = f(M * N)
-        g = f(3 * M * N)
+        g = f(_lib.COL_OUTPUTS * M * N)
         fxy = f(M * N * 2)
         e = torch.zeros(1, dtype=torch.float64, device=cuda_device)
         be.rows_forward(cells, dens, t1)
