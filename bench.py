@@ -638,8 +638,8 @@ def main():
                 r5 = loop.run(200, graph=True)
             line["placement_loop"] = {
                 "workload": f"C5: {p5.num_cells} cells, {p5.num_bins_x}x{p5.num_bins_y} bins, 200 normalised "
-                            "density-descent steps (overflow + forward + backward + step per iteration, one "
-                            "CUDA graph per step, no host reads inside the loop)",
+                            "density-descent steps (fused overflow + forward with one scatter, backward, step "
+                            "per iteration; one CUDA graph per step, no host reads inside the loop)",
                 "ms_per_step": r5["ms"] / 200, "steps_per_s": 200 * 1000.0 / r5["ms"],
                 "overflow_first": float(r5["overflow"][0]), "overflow_final": float(r5["overflow"][-1]),
                 "max_density_final": float(r5["max_density"][-1]), "error_flags": r5["flags"]}

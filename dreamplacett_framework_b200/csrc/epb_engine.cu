@@ -32,6 +32,7 @@ struct epb_handle {
     int S = 0;
     double dscale = 0;          // 2^-S / bin_area
     long long* grid = nullptr;  // int64 [RB*N] (this band), kept zeroed between forwards
+    long long* grid2 = nullptr; // int64 [M*N] first-range grid of epb_forward_overflow (lazy)
     bool grid_dirty = false;
     float* init = nullptr;      // normalised initial density of this band [RB*N]
     bool has_init = false;
@@ -176,7 +177,7 @@ int dev_alloc(epb_handle* h, T** p, size_t count) {
 }
 
 void free_all(epb_handle* h) {
-    void* ptrs[] = {h->grid, h->init, h->t1, h->g, h->fxy, h->twM, h->qwM,
+    void* ptrs[] = {h->grid, h->grid2, h->init, h->t1, h->g, h->fxy, h->twM, h->qwM,
                     h->twN, h->qwN, h->partials, h->counter, h->energy_d, h->flags,
                     h->ovf_partials, h->ovf_counter, h->linf_bits, h->sel_list, h->sel_count};
     for (void* p : ptrs)
@@ -715,10 +716,54 @@ int epb_overflow(epb_handle* h, const epb_cells* cells, float target_density, ep
     if (int rc = scatter_into(h, v, st, h->grid)) return rc;
     k_overflow<<<ovf_blocks(nbins), kOvfThreads, 0, st>>>(h->grid, h->has_init ? h->init : nullptr, h->dscale, nbins,
                                                           target_density, (double)h->bsx * (double)h->bsy,
-                                                          h->ovf_partials, h->ovf_counter, out, h->flags);
+                                                          h->ovf_partials, h->ovf_counter, out, nullptr, h->flags);
     EPB_LAUNCHED(h, "k_overflow launch");
     h->grid_dirty = false;
     return EPB_OK;
+}
+
+int epb_forward_overflow(epb_handle* h, const epb_cells* cells, float target_density, epb_stream stream,
+                         double* overflow, float* density, float* potential, float* field_x, float* field_y,
+                         float* energy) {
+    if (!h) return EPB_EINVAL;
+    if (int rc = whole_grid_only(h)) return rc;
+    if (!overflow) return fail(h, EPB_EINVAL, "overflow is NULL");
+    if (!std::isfinite(target_density)) return fail(h, EPB_EINVAL, "target_density must be finite");
+    CellView v;
+    if (int rc = make_view(h, cells, v)) return rc;
+    DeviceGuard guard(h->dev);
+    cudaStream_t st = (cudaStream_t)stream;
+    const int64_t nbins = (int64_t)h->M * h->N;
+    if (!h->grid2) {
+        // second grid for the first range (allocated once; the first call synchronises)
+        EPB_CUDA(h, cudaStreamSynchronize(st));
+        if (int rc = dev_alloc(h, &h->grid2, (size_t)nbins)) return rc;
+        EPB_CUDA(h, cudaMemset(h->grid2, 0, (size_t)nbins * sizeof(long long)));
+    }
+    if (h->grid_dirty) {
+        EPB_CUDA(h, cudaMemsetAsync(h->grid, 0, (size_t)nbins * sizeof(long long), st));
+        EPB_CUDA(h, cudaMemsetAsync(h->grid2, 0, (size_t)nbins * sizeof(long long), st));
+        h->grid_dirty = false;
+    }
+    h->grid_dirty = true;  // until the row pass has consumed and re-zeroed the grids
+    // first range -> grid2 (its overflow), second range -> grid; then grid += grid2
+    CellView v0 = v, v1 = v;
+    v0.n = v.n0;
+    v1.b0 = v.b1; v1.n0 = v.n - v.n0; v1.n = v.n - v.n0;
+    ProfCall pc(h, st);
+    pc.begin();
+    if (int rc = scatter_into(h, v0, st, h->grid2)) return rc;
+    if (int rc = scatter_into(h, v1, st, h->grid)) return rc;
+    k_overflow<<<ovf_blocks(nbins), kOvfThreads, 0, st>>>(h->grid2, h->has_init ? h->init : nullptr, h->dscale, nbins,
+                                                          target_density, (double)h->bsx * (double)h->bsy,
+                                                          h->ovf_partials, h->ovf_counter, overflow, h->grid,
+                                                          h->flags);
+    EPB_LAUNCHED(h, "k_overflow launch");
+    pc.end_stage(EPB_STAGE_SCATTER);
+    if (int rc = launch_row_fwd(h, true, nullptr, density, blocked(h->t1, 0, 1), 0, st)) return rc;
+    pc.end_stage(EPB_STAGE_ROW_FWD);
+    h->grid_dirty = false;
+    return solve_from_t1(h, st, potential, field_x, field_y, energy, pc);
 }
 
 int epb_descent_step(epb_handle* h, const epb_cells* cells, float* x, float* y, const float* grad_x,

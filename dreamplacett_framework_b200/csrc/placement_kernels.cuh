@@ -29,11 +29,13 @@ inline int ovf_blocks(int64_t nbins) {
 
 // Per bin: rho = fp32(q * dscale) + init (the density-map value epb_forward
 // writes), excess = max(rho - target, 0) in fp64.  out[0] = bin_area * sum of
-// excess, out[1] = max rho.  The grid is left zeroed for the next scatter.
+// excess, out[1] = max rho.  With `merge`, each bin's q is then added to
+// merge[bin] (another grid of the same layout, e.g. the one the forward converts).
+// The grid is left zeroed for the next scatter.
 __global__ void __launch_bounds__(kOvfThreads)
 k_overflow(long long* __restrict__ qgrid, const float* __restrict__ init, double dscale, int64_t nbins,
            float target, double bin_area, double* __restrict__ partials, unsigned* __restrict__ counter,
-           double* __restrict__ out, unsigned* __restrict__ flags) {
+           double* __restrict__ out, long long* __restrict__ merge, unsigned* __restrict__ flags) {
     __shared__ double s_sum[kOvfThreads];
     __shared__ double s_max[kOvfThreads];
     __shared__ bool is_last;
@@ -53,8 +55,14 @@ k_overflow(long long* __restrict__ qgrid, const float* __restrict__ init, double
         if (ex > 0.0) sum += ex;
         mx = fmaxf(mx, v);
     }
-    // re-zero after every load of this thread has been issued
-    for (int64_t i = lo + threadIdx.x; i < hi; i += kOvfThreads) qgrid[i] = 0;
+    // merge and re-zero after every load of this thread has been issued
+    for (int64_t i = lo + threadIdx.x; i < hi; i += kOvfThreads) {
+        if (merge) {
+            const long long q = qgrid[i];
+            if (q != 0) merge[i] += q;
+        }
+        qgrid[i] = 0;
+    }
     if (sat) atomicOr(flags, kFlagSaturated);
     s_sum[threadIdx.x] = sum;
     s_max[threadIdx.x] = (double)mx;

@@ -141,19 +141,7 @@ class ElectricPotentialEngine:
     def _grid(self, dtype=torch.float32):
         return torch.empty((self.M, self.N), dtype=dtype, device=self.device)
 
-    # -- API --------------------------------------------------------------
-    def set_initial_density(self, init_norm: Optional[torch.Tensor], stream=None):
-        """Normalised fixed-cell density (initial_density_map / bin_area)."""
-        if init_norm is not None:
-            _check_f32("init_norm", init_norm, self.device, self.M * self.N)
-        _lib.check(self._h, self.lib.epb_set_initial_density(
-            self._h, _ptr(init_norm), _stream_ptr(stream, self.device)))
-
-    def forward(self, cells: CellTensors, want_density=True, want_potential=True, want_fields=True,
-                want_energy=True, out=None, stream=None):
-        """Returns dict with density, potential, field_x, field_y (M x N fp32)
-        and energy (1-element fp32 tensor); entries are None when not wanted.
-        `out` may supply preallocated tensors under the same keys."""
+    def _outputs(self, want_density, want_potential, want_fields, want_energy, out):
         out = dict(out or {})
         res = {}
         for key, want, shape in (("density", want_density, (self.M, self.N)),
@@ -170,6 +158,22 @@ class ElectricPotentialEngine:
             else:
                 _check_f32(key, t, self.device, math.prod(shape))
             res[key] = t
+        return res
+
+    # -- API --------------------------------------------------------------
+    def set_initial_density(self, init_norm: Optional[torch.Tensor], stream=None):
+        """Normalised fixed-cell density (initial_density_map / bin_area)."""
+        if init_norm is not None:
+            _check_f32("init_norm", init_norm, self.device, self.M * self.N)
+        _lib.check(self._h, self.lib.epb_set_initial_density(
+            self._h, _ptr(init_norm), _stream_ptr(stream, self.device)))
+
+    def forward(self, cells: CellTensors, want_density=True, want_potential=True, want_fields=True,
+                want_energy=True, out=None, stream=None):
+        """Returns dict with density, potential, field_x, field_y (M x N fp32)
+        and energy (1-element fp32 tensor); entries are None when not wanted.
+        `out` may supply preallocated tensors under the same keys."""
+        res = self._outputs(want_density, want_potential, want_fields, want_energy, out)
         st = self.lib.epb_forward(self._h, self._cells(cells), _stream_ptr(stream, self.device),
                                   _ptr(res["density"]), _ptr(res["potential"]), _ptr(res["field_x"]),
                                   _ptr(res["field_y"]), _ptr(res["energy"]))
@@ -238,6 +242,25 @@ class ElectricPotentialEngine:
                                    _stream_ptr(stream, self.device), _ptr(out))
         _lib.check(self._h, st)
         return out
+
+    def forward_overflow(self, cells: CellTensors, target_density: float = 1.0,
+                         overflow: Optional[torch.Tensor] = None, want_density=True, want_potential=True,
+                         want_fields=True, want_energy=True, out=None, stream=None):
+        """forward() of both cell ranges plus the first range's overflow (as
+        overflow() of that range alone) with one scatter (epb_forward_overflow).
+        Returns (forward outputs, device float64[2] overflow)."""
+        if overflow is None:
+            overflow = torch.empty(2, dtype=torch.float64, device=self.device)
+        if (overflow.dtype != torch.float64 or overflow.device != self.device or overflow.numel() < 2
+                or not overflow.is_contiguous()):
+            raise ValueError("overflow must be a contiguous float64 tensor of 2 elements on the engine's device")
+        res = self._outputs(want_density, want_potential, want_fields, want_energy, out)
+        st = self.lib.epb_forward_overflow(self._h, self._cells(cells), float(target_density),
+                                           _stream_ptr(stream, self.device), _ptr(overflow), _ptr(res["density"]),
+                                           _ptr(res["potential"]), _ptr(res["field_x"]), _ptr(res["field_y"]),
+                                           _ptr(res["energy"]))
+        _lib.check(self._h, st)
+        return res, overflow
 
     def descent_step(self, cells: CellTensors, grad_x: torch.Tensor, grad_y: torch.Tensor, width: torch.Tensor,
                      height: torch.Tensor, step_bins: float = 0.5, x: Optional[torch.Tensor] = None,

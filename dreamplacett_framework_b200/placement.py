@@ -6,8 +6,9 @@ and reads the per-iteration overflow back through EvalMetrics on the host
 (run_dreamplace.py:333-370).  Here the whole iteration stays on the device:
 
     per step t (lambda_t = lam0 * 2^(t // lam_every)):
-      overflow_t  = epb_overflow(movable cells) / total movable area
-      energy_t    = epb_forward(movable + filler cells)      (fields kept inside)
+      overflow_t, energy_t = epb_forward_overflow(movable | filler cells)
+                             (overflow of the movable cells / total movable area;
+                              forward of both ranges, fields kept inside)
       grad        = epb_backward(movable + filler cells)
       objective_t = lambda_t * energy_t
       epb_descent_step: x <- clamp(x - step_bins * bin_w * grad / max|grad|)
@@ -83,9 +84,10 @@ class DensityDescent:
 
     def _step(self, traj_ovf, traj_energy, traj_linf):
         eng = self.engine
-        eng.overflow(self.movable, self.target, out=self._ovf)
-        eng.forward(self.cells, want_density=False, want_potential=False, want_fields=False, want_energy=True,
-                    out={"energy": self._energy})
+        # one scatter: movable cells (first range) give the overflow, fillers join for the forward
+        eng.forward_overflow(self.cells, self.target, overflow=self._ovf, want_density=False,
+                             want_potential=False, want_fields=False, want_energy=True,
+                             out={"energy": self._energy})
         eng.backward(self.cells, grad_x=self.gx, grad_y=self.gy)
         eng.descent_step(self.cells, self.gx, self.gy, self.width, self.height, self.step_bins,
                          grad_linf=self._linf)

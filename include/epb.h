@@ -241,6 +241,20 @@ int epb_shard_wait_test(epb_handle* h, epb_stream stream, int64_t max_polls);
  * not overlap with its forward. */
 int epb_overflow(epb_handle* h, const epb_cells* cells, float target_density, epb_stream stream, double* out);
 
+/* epb_forward with the overflow of the first cell range folded in: the cells
+ * of the first range (DREAMPlace's movable nodes) are scattered into a second
+ * fixed-point grid, those of the second range (fillers) into the forward's
+ * grid; out[0..1] receive the first range's overflow exactly as epb_overflow
+ * reports it for that range alone; the second grid is then added into the
+ * first (integer sums: the density is bit-for-bit epb_forward's for both
+ * ranges) and the forward continues as epb_forward.  One scatter of every
+ * cell per placement iteration instead of two.  The first call allocates the
+ * second grid (M*N int64) and synchronises: make it before stream capture.
+ * Whole-grid handles only. */
+int epb_forward_overflow(epb_handle* h, const epb_cells* cells, float target_density, epb_stream stream,
+                         double* overflow, float* density, float* potential, float* field_x, float* field_y,
+                         float* energy);
+
 /* One normalised density-descent step of every node in the cells' ranges:
  *   linf = max over those nodes of max(|grad_x|, |grad_y|)
  *   x <- max(min(x - (step_bins * bin_size_x / linf) * grad_x, xh - width), xl)

@@ -177,3 +177,26 @@ def test_c5_loop_graph_equals_eager(cuda_device):
         np.testing.assert_array_equal(a[k], b[k])
     np.testing.assert_array_equal(ax, bx)
     np.testing.assert_array_equal(ay, by)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("config,scale,grid", [("c5", 1.0, None), ("c3", 0.25, None), ("c1", 0.05, 64)])
+def test_forward_overflow_equals_separate_calls(cuda_device, config, scale, grid):
+    """epb_forward_overflow: the movable range's overflow exactly as epb_overflow
+    reports it, and the forward of both ranges exactly as epb_forward (twice in
+    a row, so both grids are left zeroed)."""
+    p = synth.make_placement(config, scale=scale, grid=grid)
+    arrs, ranges = placement_cells(p)
+    with engine_for(p, cuda_device) as eng:
+        eng.set_initial_density(torch.from_numpy(p.initial_density_norm()).to(cuda_device))
+        cells = to_device(arrs, ranges, cuda_device)
+        movable = to_device(arrs, (ranges[0], (0, 0)), cuda_device)
+        ref_ovf = eng.overflow(movable, 1.0).clone()
+        ref = {k: v.clone() for k, v in eng.forward(cells).items()}
+        for _ in range(2):
+            out, ovf = eng.forward_overflow(cells, 1.0)
+            assert torch.equal(ovf, ref_ovf)
+            for k in ("density", "potential", "field_x", "field_y", "energy"):
+                assert torch.equal(out[k], ref[k]), k
+        rgx, rgy = eng.backward(cells)
+        assert eng.error_flags() == 0
