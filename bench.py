@@ -560,9 +560,9 @@ def main():
     energy_host = torch.empty(1, dtype=torch.float32).pin_memory()
 
     def e2e_step():
-        pos.copy_(pos_host, non_blocking=True)
-        step()
-        grad_host.copy_(grad, non_blocking=True)
+        # host positions in and host gradients out, each copy pipelined with the cell kernels
+        eng.forward_host(cells, pos_host[:n], pos_host[n:], out=outs)
+        eng.backward_host(cells, grad_host[:n], grad_host[n:], grad_x=grad[:n], grad_y=grad[n:])
         energy_host.copy_(outs["energy"], non_blocking=True)
 
     K_e2e = max(10, min(K, 200))
@@ -623,7 +623,9 @@ def main():
             "step_gbs": step_bytes / (total_ms / K / 1000.0) / 1e9,
             "e2e": {"value": world * K_e2e / (e2e_ms / 1000.0), "unit": UNIT, "steps": K_e2e,
                     "h2d_bytes_per_step": 2 * n * 4, "d2h_bytes_per_step": 2 * n * 4 + 4,
-                    "path": "engine API: pinned pos[2n] H2D, forward+backward, grad[2n] + energy D2H"},
+                    "path": "engine API with host buffers: epb_forward_host (pinned pos[2n], H2D in 8 node chunks "
+                            "overlapped with the scatter), epb_backward_host (grad[2n] D2H in 8 chunks overlapped "
+                            "with the gather), energy D2H"},
             "gpu_launches": 5 * K,
             "cuda_graph": "timed steps replay one captured graph of forward+backward; per-kernel "
                           f"times from {K_prof} eager profiled steps; e2e is eager API calls",

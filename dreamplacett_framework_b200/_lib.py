@@ -37,6 +37,7 @@ EXPORTS = (
     "epb_shard_peer_buffers", "epb_shard_connect", "epb_shard_set_timeout", "epb_shard_forward_peer",
     "epb_shard_backward_peer", "epb_shard_wait_test",
     "epb_overflow", "epb_descent_step", "epb_forward_overflow",
+    "epb_forward_host", "epb_backward_host",
 )
 
 # Largest grid (M*N bins) epb_density_noalloc accepts (EPB_NOALLOC_MAX_BINS).
@@ -122,6 +123,8 @@ def load():
     L.epb_overflow.argtypes = [vp, cp, ctypes.c_float, vp, vp]
     L.epb_descent_step.argtypes = [vp, cp, vp, vp, vp, vp, vp, vp, ctypes.c_float, vp, vp]
     L.epb_forward_overflow.argtypes = [vp, cp, ctypes.c_float, vp, vp, vp, vp, vp, vp, vp]
+    L.epb_forward_host.argtypes = [vp, cp, vp, vp, i32, vp, vp, vp, vp, vp, vp]
+    L.epb_backward_host.argtypes = [vp, cp, vp, i32, vp, vp, vp, vp, vp]
     for name in EXPORTS:
         if name not in ("epb_version", "epb_status_string", "epb_last_error"):
             getattr(L, name).restype = ctypes.c_int

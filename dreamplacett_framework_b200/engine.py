@@ -243,6 +243,53 @@ class ElectricPotentialEngine:
         _lib.check(self._h, st)
         return out
 
+    # -- host buffers -------------------------------------------------------
+    @staticmethod
+    def _check_host(name, t, n):
+        if t.is_cuda or t.dtype != torch.float32 or not t.is_contiguous() or t.numel() < n:
+            raise ValueError(f"{name} must be a contiguous float32 host tensor of at least {n} elements")
+        if not t.is_pinned():
+            raise ValueError(f"{name} must be in pinned memory (tensor.pin_memory())")
+
+    def forward_host(self, cells: CellTensors, host_x: torch.Tensor, host_y: torch.Tensor, chunks: int = 8,
+                     want_density=True, want_potential=True, want_fields=True, want_energy=True, out=None,
+                     stream=None):
+        """forward() with the positions taken from pinned host tensors: they
+        are copied into cells.x / cells.y in `chunks` node ranges, each range's
+        scatter overlapping the next range's copy (epb_forward_host)."""
+        n = cells.num_nodes
+        self._check_host("host_x", host_x, n)
+        self._check_host("host_y", host_y, n)
+        res = self._outputs(want_density, want_potential, want_fields, want_energy, out)
+        st = self.lib.epb_forward_host(self._h, self._cells(cells), _ptr(host_x), _ptr(host_y), int(chunks),
+                                       _stream_ptr(stream, self.device), _ptr(res["density"]),
+                                       _ptr(res["potential"]), _ptr(res["field_x"]), _ptr(res["field_y"]),
+                                       _ptr(res["energy"]))
+        _lib.check(self._h, st)
+        return res
+
+    def backward_host(self, cells: CellTensors, host_grad_x: torch.Tensor, host_grad_y: torch.Tensor,
+                      grad_out: Optional[torch.Tensor] = None, grad_x: Optional[torch.Tensor] = None,
+                      grad_y: Optional[torch.Tensor] = None, chunks: int = 8, stream=None):
+        """backward() whose gradients also land in pinned host tensors, each
+        chunk's copy overlapping the next chunk's gather (epb_backward_host).
+        The host tensors are complete once `stream` has been synchronised."""
+        n = cells.num_nodes
+        self._check_host("host_grad_x", host_grad_x, n)
+        self._check_host("host_grad_y", host_grad_y, n)
+        if grad_x is None:
+            grad_x = torch.zeros(n, dtype=torch.float32, device=self.device)
+        if grad_y is None:
+            grad_y = torch.zeros(n, dtype=torch.float32, device=self.device)
+        _check_f32("grad_x", grad_x, self.device, n)
+        _check_f32("grad_y", grad_y, self.device, n)
+        _check_f32("grad_out", grad_out, self.device, 1)
+        st = self.lib.epb_backward_host(self._h, self._cells(cells), _ptr(grad_out), int(chunks),
+                                        _stream_ptr(stream, self.device), _ptr(grad_x), _ptr(grad_y),
+                                        _ptr(host_grad_x), _ptr(host_grad_y))
+        _lib.check(self._h, st)
+        return grad_x, grad_y
+
     def forward_overflow(self, cells: CellTensors, target_density: float = 1.0,
                          overflow: Optional[torch.Tensor] = None, want_density=True, want_potential=True,
                          want_fields=True, want_energy=True, out=None, stream=None):

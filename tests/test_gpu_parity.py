@@ -264,3 +264,33 @@ def test_multiple_engines_and_streams(cuda_device):
         s.synchronize()
         assert torch.equal(ra["density"], rb["density"])
         assert torch.equal(ra["field_x"], rb["field_x"])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("chunks", [1, 3, 8])
+def test_host_buffer_entry_points(cuda_device, chunks):
+    """epb_forward_host / epb_backward_host: positions from pinned host memory,
+    gradients back to it, results identical to the device entry points."""
+    p = synth.make_placement("c3", scale=0.1, grid=512)
+    arrs, ranges = placement_cells(p)
+    with engine_for(p, cuda_device) as eng:
+        eng.set_initial_density(torch.from_numpy(p.initial_density_norm()).to(cuda_device))
+        cells = to_device(arrs, ranges, cuda_device)
+        ref = {k: v.clone() for k, v in eng.forward(cells).items()}
+        rgx, rgy = (t.clone() for t in eng.backward(cells))
+        hx = torch.from_numpy(p.x.copy()).pin_memory()
+        hy = torch.from_numpy(p.y.copy()).pin_memory()
+        cells.x.zero_()
+        cells.y.zero_()
+        out = eng.forward_host(cells, hx, hy, chunks=chunks)
+        hgx = torch.zeros(p.num_nodes).pin_memory()
+        hgy = torch.zeros(p.num_nodes).pin_memory()
+        gx, gy = eng.backward_host(cells, hgx, hgy, chunks=chunks)
+        torch.cuda.synchronize(cuda_device)
+        assert torch.equal(cells.x.cpu(), hx) and torch.equal(cells.y.cpu(), hy)
+        for k in ("density", "potential", "field_x", "field_y", "energy"):
+            assert torch.equal(out[k], ref[k]), k
+        assert torch.equal(gx, rgx) and torch.equal(gy, rgy)
+        assert torch.equal(hgx, rgx.cpu()) and torch.equal(hgy, rgy.cpu())
+        with pytest.raises(ValueError):
+            eng.forward_host(cells, torch.zeros(p.num_nodes), hy)  # not pinned
