@@ -623,9 +623,9 @@ def main():
             "step_gbs": step_bytes / (total_ms / K / 1000.0) / 1e9,
             "e2e": {"value": world * K_e2e / (e2e_ms / 1000.0), "unit": UNIT, "steps": K_e2e,
                     "h2d_bytes_per_step": 2 * n * 4, "d2h_bytes_per_step": 2 * n * 4 + 4,
-                    "path": "engine API with host buffers: epb_forward_host (pinned pos[2n], H2D in 8 node chunks "
-                            "overlapped with the scatter), epb_backward_host (grad[2n] D2H in 8 chunks overlapped "
-                            "with the gather), energy D2H"},
+                    "path": "engine API with host buffers: epb_forward_host (the scatter reads pinned pos[2n] "
+                            "over PCIe), epb_backward_host (the gather stores grad[2n] to pinned host memory), "
+                            "energy D2H"},
             "gpu_launches": 5 * K,
             "cuda_graph": "timed steps replay one captured graph of forward+backward; per-kernel "
                           f"times from {K_prof} eager profiled steps; e2e is eager API calls",

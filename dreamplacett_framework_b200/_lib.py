@@ -123,8 +123,8 @@ def load():
     L.epb_overflow.argtypes = [vp, cp, ctypes.c_float, vp, vp]
     L.epb_descent_step.argtypes = [vp, cp, vp, vp, vp, vp, vp, vp, ctypes.c_float, vp, vp]
     L.epb_forward_overflow.argtypes = [vp, cp, ctypes.c_float, vp, vp, vp, vp, vp, vp, vp]
-    L.epb_forward_host.argtypes = [vp, cp, vp, vp, i32, vp, vp, vp, vp, vp, vp]
-    L.epb_backward_host.argtypes = [vp, cp, vp, i32, vp, vp, vp, vp, vp]
+    L.epb_forward_host.argtypes = [vp, cp, vp, vp, vp, vp, vp, vp, vp, vp]
+    L.epb_backward_host.argtypes = [vp, cp, vp, vp, vp, vp, vp, vp]
     for name in EXPORTS:
         if name not in ("epb_version", "epb_status_string", "epb_last_error"):
             getattr(L, name).restype = ctypes.c_int

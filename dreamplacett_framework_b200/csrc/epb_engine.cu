@@ -76,9 +76,6 @@ struct epb_handle {
     std::vector<cudaEvent_t> prof_events;
     int prof_used = 0;
     std::vector<Span> prof_spans;
-    // host-buffer entry points: copy stream and per-chunk events (created on first use)
-    cudaStream_t copy_st = nullptr;
-    std::vector<cudaEvent_t> chunk_ev;
     std::string err;
 };
 
@@ -197,10 +194,6 @@ void free_all(epb_handle* h) {
         if (p) cudaFree(p);
     for (cudaEvent_t e : h->prof_events) cudaEventDestroy(e);
     h->prof_events.clear();
-    for (cudaEvent_t e : h->chunk_ev) cudaEventDestroy(e);
-    h->chunk_ev.clear();
-    if (h->copy_st) cudaStreamDestroy(h->copy_st);
-    h->copy_st = nullptr;
 }
 
 // ----- kernel dispatch on the transform length -----
@@ -447,7 +440,7 @@ int scatter_into(epb_handle* h, const CellView& v0, cudaStream_t st, long long* 
         if (int rc = band_selection(h, v, 0, st)) return rc;
         blocks = (unsigned)((v.n + kSelChunk - 1) / kSelChunk);   // one CTA per segment
     }
-    k_scatter<<<blocks, 256, 0, st>>>(v, geom(h), qscale, (unsigned long long*)grid, h->row0, h->row0 + h->RB,
+    k_scatter<false><<<blocks, 256, 0, st>>>(v, geom(h), qscale, (unsigned long long*)grid, h->row0, h->row0 + h->RB,
                                       h->flags);
     EPB_LAUNCHED(h, "k_scatter launch");
     return EPB_OK;
@@ -463,7 +456,7 @@ int shard_gather(epb_handle* h, const CellView& v0, const float2* fxy, int halo,
         if (int rc = band_selection(h, v, 1, st)) return rc;
         blocks = (unsigned)((v.n + kSelChunk - 1) / kSelChunk);   // one CTA per segment
     }
-    k_gather<<<blocks, 256, 0, st>>>(v, geom(h), fxy, nullptr, nullptr, h->row0, h->row0 + h->RB, halo, 1, grad_out,
+    k_gather<false><<<blocks, 256, 0, st>>>(v, geom(h), fxy, nullptr, nullptr, h->row0, h->row0 + h->RB, halo, 1, grad_out,
                                      grad_x, grad_y, h->flags);
     EPB_LAUNCHED(h, "k_gather launch");
     return EPB_OK;
@@ -653,7 +646,7 @@ int epb_backward(epb_handle* h, const epb_cells* cells, const float* grad_out, e
     DeviceGuard guard(h->dev);
     ProfCall pc(h, (cudaStream_t)stream);
     pc.begin();
-    k_gather<<<cell_blocks(v.n), 256, 0, (cudaStream_t)stream>>>(v, geom(h), h->fxy, nullptr, nullptr, 0, h->M, 0, 0,
+    k_gather<false><<<cell_blocks(v.n), 256, 0, (cudaStream_t)stream>>>(v, geom(h), h->fxy, nullptr, nullptr, 0, h->M, 0, 0,
                                                                grad_out, grad_x, grad_y, h->flags);
     EPB_LAUNCHED(h, "k_gather launch");
     pc.end_stage(EPB_STAGE_GATHER);
@@ -700,7 +693,7 @@ int epb_gather(epb_handle* h, const epb_cells* cells, const float* field_x, cons
     if (v.n > 0 && (!grad_x || !grad_y)) return fail(h, EPB_EINVAL, "grad_x/grad_y must be non-NULL");
     if (v.n == 0) return EPB_OK;
     DeviceGuard guard(h->dev);
-    k_gather<<<cell_blocks(v.n), 256, 0, (cudaStream_t)stream>>>(v, geom(h), nullptr, field_x, field_y, 0, h->M, 0, 0,
+    k_gather<false><<<cell_blocks(v.n), 256, 0, (cudaStream_t)stream>>>(v, geom(h), nullptr, field_x, field_y, 0, h->M, 0, 0,
                                                                grad_out, grad_x, grad_y, h->flags);
     EPB_LAUNCHED(h, "k_gather launch");
     return EPB_OK;
@@ -708,66 +701,32 @@ int epb_gather(epb_handle* h, const epb_cells* cells, const float* field_x, cons
 
 namespace {
 
-// The cells of v whose node lies in [lo, hi).
-CellView chunk_view(const CellView& v, int64_t lo, int64_t hi) {
-    CellView c = v;
-    const int64_t a0 = std::max(v.b0, lo), e0 = std::min(v.b0 + v.n0, hi);
-    const int64_t a1 = std::max(v.b1, lo), e1 = std::min(v.b1 + (v.n - v.n0), hi);
-    c.b0 = a0;
-    c.n0 = std::max<int64_t>(0, e0 - a0);
-    c.b1 = a1;
-    c.n = c.n0 + std::max<int64_t>(0, e1 - a1);
-    return c;
-}
-
-// Copy stream and at least n events of the host-buffer entry points.
-int host_io_setup(epb_handle* h, int n) {
-    if (!h->copy_st) EPB_CUDA(h, cudaStreamCreateWithFlags(&h->copy_st, cudaStreamNonBlocking));
-    while ((int)h->chunk_ev.size() < n) {
-        cudaEvent_t e;
-        EPB_CUDA(h, cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
-        h->chunk_ev.push_back(e);
+// Device address of a pinned host buffer (EINVAL when it is not pinned).
+int host_device_ptr(epb_handle* h, const void* host, void** dev) {
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, host) != cudaSuccess || at.type != cudaMemoryTypeHost || !at.devicePointer) {
+        cudaGetLastError();  // clear the sticky-free error of a failed query
+        return fail(h, EPB_EINVAL, "host buffers must be pinned (page-locked) host memory");
     }
-    return EPB_OK;
-}
-
-int host_io_args(epb_handle* h, const epb_cells* cells, const void* a, const void* b, int chunks) {
-    if (!cells) return fail(h, EPB_EINVAL, "cells is NULL");
-    if (!a || !b) return fail(h, EPB_EINVAL, "host arrays must be non-NULL");
-    if (chunks < 1 || chunks > 64) return fail(h, EPB_EINVAL, "chunks must be in [1, 64]");
+    *dev = at.devicePointer;
     return EPB_OK;
 }
 
 }  // namespace
 
-int epb_forward_host(epb_handle* h, const epb_cells* cells, const float* host_x, const float* host_y, int32_t chunks,
+int epb_forward_host(epb_handle* h, const epb_cells* cells, const float* host_x, const float* host_y,
                      epb_stream stream, float* density, float* potential, float* field_x, float* field_y,
                      float* energy) {
     if (!h) return EPB_EINVAL;
     if (int rc = whole_grid_only(h)) return rc;
-    if (int rc = host_io_args(h, cells, host_x, host_y, chunks)) return rc;
+    if (!host_x || !host_y) return fail(h, EPB_EINVAL, "host_x and host_y must be non-NULL");
     CellView v;
     if (int rc = make_view(h, cells, v)) return rc;
     DeviceGuard guard(h->dev);
     cudaStream_t st = (cudaStream_t)stream;
-    if (int rc = host_io_setup(h, chunks + 1)) return rc;
-    // nodes [0, nn) hold every scattered cell; chunk k covers nodes [k*nn/chunks, (k+1)*nn/chunks)
-    const int64_t nn = std::max(cells->end0, cells->end1);
-    float* dx = const_cast<float*>(cells->x);
-    float* dy = const_cast<float*>(cells->y);
-    // the copies start after the caller's earlier work on its stream
-    EPB_CUDA(h, cudaEventRecord(h->chunk_ev[chunks], st));
-    EPB_CUDA(h, cudaStreamWaitEvent(h->copy_st, h->chunk_ev[chunks], 0));
-    for (int k = 0; k < chunks; ++k) {
-        const int64_t lo = nn * k / chunks, hi = nn * (k + 1) / chunks;
-        if (hi > lo) {
-            EPB_CUDA(h, cudaMemcpyAsync(dx + lo, host_x + lo, (size_t)(hi - lo) * sizeof(float),
-                                        cudaMemcpyHostToDevice, h->copy_st));
-            EPB_CUDA(h, cudaMemcpyAsync(dy + lo, host_y + lo, (size_t)(hi - lo) * sizeof(float),
-                                        cudaMemcpyHostToDevice, h->copy_st));
-        }
-        EPB_CUDA(h, cudaEventRecord(h->chunk_ev[k], h->copy_st));
-    }
+    void *hx = nullptr, *hy = nullptr;
+    if (int rc = host_device_ptr(h, host_x, &hx)) return rc;
+    if (int rc = host_device_ptr(h, host_y, &hy)) return rc;
     if (h->grid_dirty) {
         EPB_CUDA(h, cudaMemsetAsync(h->grid, 0, (size_t)h->M * h->N * sizeof(long long), st));
         h->grid_dirty = false;
@@ -775,11 +734,15 @@ int epb_forward_host(epb_handle* h, const epb_cells* cells, const float* host_x,
     h->grid_dirty = true;
     ProfCall pc(h, st);
     pc.begin();
-    // the scatter of chunk k runs while chunk k+1 is still on the bus
-    for (int k = 0; k < chunks; ++k) {
-        const int64_t lo = nn * k / chunks, hi = nn * (k + 1) / chunks;
-        EPB_CUDA(h, cudaStreamWaitEvent(st, h->chunk_ev[k], 0));
-        if (int rc = scatter_into(h, chunk_view(v, lo, hi), st, h->grid)) return rc;
+    if (v.n > 0) {
+        // positions read straight from host memory over PCIe and kept in cells->x / cells->y
+        CellView vh = v;
+        vh.x = static_cast<const float*>(hx);
+        vh.y = static_cast<const float*>(hy);
+        k_scatter<true><<<cell_blocks(v.n), 256, 0, st>>>(vh, geom(h), ldexpf(1.0f, h->S),
+                                                          (unsigned long long*)h->grid, 0, h->M, h->flags,
+                                                          const_cast<float*>(cells->x), const_cast<float*>(cells->y));
+        EPB_LAUNCHED(h, "k_scatter launch");
     }
     pc.end_stage(EPB_STAGE_SCATTER);
     if (int rc = launch_row_fwd(h, true, nullptr, density, blocked(h->t1, 0, 1), 0, st)) return rc;
@@ -788,43 +751,28 @@ int epb_forward_host(epb_handle* h, const epb_cells* cells, const float* host_x,
     return solve_from_t1(h, st, potential, field_x, field_y, energy, pc);
 }
 
-int epb_backward_host(epb_handle* h, const epb_cells* cells, const float* grad_out, int32_t chunks, epb_stream stream,
+int epb_backward_host(epb_handle* h, const epb_cells* cells, const float* grad_out, epb_stream stream,
                       float* grad_x, float* grad_y, float* host_grad_x, float* host_grad_y) {
     if (!h) return EPB_EINVAL;
     if (int rc = whole_grid_only(h)) return rc;
     if (!h->have_fields) return fail(h, EPB_ENOSTATE, "epb_backward_host before a forward");
-    if (int rc = host_io_args(h, cells, host_grad_x, host_grad_y, chunks)) return rc;
-    if (!grad_x || !grad_y) return fail(h, EPB_EINVAL, "grad_x/grad_y must be non-NULL");
+    if (!grad_x || !grad_y || !host_grad_x || !host_grad_y)
+        return fail(h, EPB_EINVAL, "grad_x, grad_y, host_grad_x and host_grad_y must be non-NULL");
     CellView v;
     if (int rc = make_view(h, cells, v)) return rc;
     DeviceGuard guard(h->dev);
     cudaStream_t st = (cudaStream_t)stream;
-    if (int rc = host_io_setup(h, chunks + 1)) return rc;
-    const int64_t nn = std::max(cells->end0, cells->end1);
+    void *hgx = nullptr, *hgy = nullptr;
+    if (int rc = host_device_ptr(h, host_grad_x, &hgx)) return rc;
+    if (int rc = host_device_ptr(h, host_grad_y, &hgy)) return rc;
+    if (v.n == 0) return EPB_OK;
     ProfCall pc(h, st);
     pc.begin();
-    // chunk k's gradients go to the host while chunk k+1 is gathered
-    for (int k = 0; k < chunks; ++k) {
-        const int64_t lo = nn * k / chunks, hi = nn * (k + 1) / chunks;
-        const CellView c = chunk_view(v, lo, hi);
-        if (c.n > 0) {
-            k_gather<<<cell_blocks(c.n), 256, 0, st>>>(c, geom(h), h->fxy, nullptr, nullptr, 0, h->M, 0, 0, grad_out,
-                                                       grad_x, grad_y, h->flags);
-            EPB_LAUNCHED(h, "k_gather launch");
-        }
-        EPB_CUDA(h, cudaEventRecord(h->chunk_ev[k], st));
-        EPB_CUDA(h, cudaStreamWaitEvent(h->copy_st, h->chunk_ev[k], 0));
-        if (hi > lo) {
-            EPB_CUDA(h, cudaMemcpyAsync(host_grad_x + lo, grad_x + lo, (size_t)(hi - lo) * sizeof(float),
-                                        cudaMemcpyDeviceToHost, h->copy_st));
-            EPB_CUDA(h, cudaMemcpyAsync(host_grad_y + lo, grad_y + lo, (size_t)(hi - lo) * sizeof(float),
-                                        cudaMemcpyDeviceToHost, h->copy_st));
-        }
-    }
+    k_gather<true><<<cell_blocks(v.n), 256, 0, st>>>(v, geom(h), h->fxy, nullptr, nullptr, 0, h->M, 0, 0, grad_out,
+                                                     grad_x, grad_y, h->flags, static_cast<float*>(hgx),
+                                                     static_cast<float*>(hgy));
+    EPB_LAUNCHED(h, "k_gather launch");
     pc.end_stage(EPB_STAGE_GATHER);
-    // the caller's stream resumes after the last copy
-    EPB_CUDA(h, cudaEventRecord(h->chunk_ev[chunks], h->copy_st));
-    EPB_CUDA(h, cudaStreamWaitEvent(st, h->chunk_ev[chunks], 0));
     return EPB_OK;
 }
 
@@ -1345,7 +1293,7 @@ extern "C" int epb_density_noalloc(const epb_config* cfg, const epb_cells* cells
     cudaError_t e = cudaMemsetAsync(grid, 0, (size_t)(nbins + 32) * sizeof(long long), st);
     if (e != cudaSuccess) return noalloc_fail(err, err_len, EPB_ECUDA, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
     if (v.n > 0) {
-        k_scatter<<<cell_blocks(v.n), 256, 0, st>>>(v, geom(&g), ldexpf(1.0f, g.S), (unsigned long long*)grid, 0, g.M,
+        k_scatter<false><<<cell_blocks(v.n), 256, 0, st>>>(v, geom(&g), ldexpf(1.0f, g.S), (unsigned long long*)grid, 0, g.M,
                                                     flags);
         e = cudaGetLastError();
         if (e != cudaSuccess) return noalloc_fail(err, err_len, EPB_ECUDA, std::string("k_scatter: ") + cudaGetErrorString(e));

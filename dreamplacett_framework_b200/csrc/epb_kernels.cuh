@@ -87,13 +87,21 @@ struct DstTable {
 // ---------------------------------------------------------------------------
 // Scatter
 // ---------------------------------------------------------------------------
+// IO: c.x / c.y point into pinned host memory (read over PCIe) and every
+// visited node's position is also stored to xcopy / ycopy in device memory.
+template <bool IO = false>
 __global__ void EPB_SCATTER_BOUNDS
 k_scatter(CellView c, GridGeom g, float qscale, unsigned long long* __restrict__ grid,
-          int row0, int row1, unsigned* __restrict__ flags) {
+          int row0, int row1, unsigned* __restrict__ flags, float* __restrict__ xcopy = nullptr,
+          float* __restrict__ ycopy = nullptr) {
     // grid holds rows [row0, row1) of the density grid; footprints are clipped to them.
     // Cells of a selection are known to meet the band: they skip the band test.
     const int blo = c.sel ? 0 : row0, bhi = c.sel ? g.M : row1;
     for_each_cell(c, [&](int64_t node) {
+        if constexpr (IO) {
+            xcopy[node] = __ldg(c.x + node);
+            ycopy[node] = __ldg(c.y + node);
+        }
         Footprint f;
         const int st = cell_footprint(c, g, node, f, blo, bhi, false);
         if (st < 0) { atomicOr(flags, kFlagNonFinite); return; }
@@ -733,12 +741,15 @@ k_band_select(CellView c, GridGeom g, int row0, int row1, int mode, int* __restr
 // ---------------------------------------------------------------------------
 // Gather: grad[node] = -g * ratio * sum (ox*oy) * field
 // ---------------------------------------------------------------------------
+// IO: the gradients are also stored to host_gx / host_gy in pinned host memory
+// (written over PCIe).
+template <bool IO = false>
 __global__ void EPB_GATHER_BOUNDS
 k_gather(CellView c, GridGeom g, const float2* __restrict__ fxy,
          const float* __restrict__ fx, const float* __restrict__ fy,  // planar alternative when fxy == nullptr
          int row0, int row1, int halo, int owned_only,
          const float* __restrict__ grad_out, float* __restrict__ grad_x, float* __restrict__ grad_y,
-         unsigned* __restrict__ flags) {
+         unsigned* __restrict__ flags, float* __restrict__ host_gx = nullptr, float* __restrict__ host_gy = nullptr) {
     // The field maps hold rows [row0, row1 + halo).  With owned_only, only cells
     // whose first bin row lies in [row0, row1) are computed and written; other
     // entries of grad_x / grad_y are left as they are.
@@ -774,6 +785,10 @@ k_gather(CellView c, GridGeom g, const float2* __restrict__ fxy,
         const float s = gscale * r;
         grad_x[node] = s * ax;
         grad_y[node] = s * ay;
+        if constexpr (IO) {
+            host_gx[node] = s * ax;
+            host_gy[node] = s * ay;
+        }
     });
 }
 

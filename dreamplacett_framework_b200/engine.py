@@ -251,17 +251,17 @@ class ElectricPotentialEngine:
         if not t.is_pinned():
             raise ValueError(f"{name} must be in pinned memory (tensor.pin_memory())")
 
-    def forward_host(self, cells: CellTensors, host_x: torch.Tensor, host_y: torch.Tensor, chunks: int = 8,
+    def forward_host(self, cells: CellTensors, host_x: torch.Tensor, host_y: torch.Tensor,
                      want_density=True, want_potential=True, want_fields=True, want_energy=True, out=None,
                      stream=None):
-        """forward() with the positions taken from pinned host tensors: they
-        are copied into cells.x / cells.y in `chunks` node ranges, each range's
-        scatter overlapping the next range's copy (epb_forward_host)."""
+        """forward() with the positions read from pinned host tensors by the
+        scatter itself (over PCIe); the positions of the nodes in the cell
+        ranges are kept in cells.x / cells.y (epb_forward_host)."""
         n = cells.num_nodes
         self._check_host("host_x", host_x, n)
         self._check_host("host_y", host_y, n)
         res = self._outputs(want_density, want_potential, want_fields, want_energy, out)
-        st = self.lib.epb_forward_host(self._h, self._cells(cells), _ptr(host_x), _ptr(host_y), int(chunks),
+        st = self.lib.epb_forward_host(self._h, self._cells(cells), _ptr(host_x), _ptr(host_y),
                                        _stream_ptr(stream, self.device), _ptr(res["density"]),
                                        _ptr(res["potential"]), _ptr(res["field_x"]), _ptr(res["field_y"]),
                                        _ptr(res["energy"]))
@@ -270,10 +270,10 @@ class ElectricPotentialEngine:
 
     def backward_host(self, cells: CellTensors, host_grad_x: torch.Tensor, host_grad_y: torch.Tensor,
                       grad_out: Optional[torch.Tensor] = None, grad_x: Optional[torch.Tensor] = None,
-                      grad_y: Optional[torch.Tensor] = None, chunks: int = 8, stream=None):
-        """backward() whose gradients also land in pinned host tensors, each
-        chunk's copy overlapping the next chunk's gather (epb_backward_host).
-        The host tensors are complete once `stream` has been synchronised."""
+                      grad_y: Optional[torch.Tensor] = None, stream=None):
+        """backward() whose gradients the gather also stores to pinned host
+        tensors over PCIe (epb_backward_host).  The host tensors are complete
+        once `stream` has been synchronised."""
         n = cells.num_nodes
         self._check_host("host_grad_x", host_grad_x, n)
         self._check_host("host_grad_y", host_grad_y, n)
@@ -284,7 +284,7 @@ class ElectricPotentialEngine:
         _check_f32("grad_x", grad_x, self.device, n)
         _check_f32("grad_y", grad_y, self.device, n)
         _check_f32("grad_out", grad_out, self.device, 1)
-        st = self.lib.epb_backward_host(self._h, self._cells(cells), _ptr(grad_out), int(chunks),
+        st = self.lib.epb_backward_host(self._h, self._cells(cells), _ptr(grad_out),
                                         _stream_ptr(stream, self.device), _ptr(grad_x), _ptr(grad_y),
                                         _ptr(host_grad_x), _ptr(host_grad_y))
         _lib.check(self._h, st)

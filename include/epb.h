@@ -225,24 +225,22 @@ int epb_shard_wait_test(epb_handle* h, epb_stream stream, int64_t max_polls);
 /* ---- Host buffers ------------------------------------------------------
  * The reference's client hands the server host arrays every iteration
  * (integration/scatter_ttnn_client.py:411-509: px, py, sx, sy written to shared
- * memory, field maps read back).  These two entry points take and return host
- * buffers and overlap the PCIe copies with the cell kernels: the nodes
- * [0, max(end0, end1)) are split into `chunks` ranges (1..64), and
- *   epb_forward_host copies host_x / host_y (pinned, node-indexed) into the
- *     device arrays cells->x / cells->y chunk by chunk on the handle's copy
- *     stream while the scatter of the chunks already copied runs on `stream`;
- *     then it continues exactly as epb_forward (same results);
- *   epb_backward_host gathers chunk by chunk into the device arrays grad_x /
- *     grad_y (as epb_backward) and copies each finished chunk of both to
- *     host_grad_x / host_grad_y (pinned) while the next one is gathered.
- * `stream` waits for the last copy before its later work; synchronise on it
- * before reading the host gradients.  The first call creates the copy stream
- * and its events.  Whole-grid handles only.  No reference counterpart as
- * entry points (the reference's server copies through shared memory). */
-int epb_forward_host(epb_handle* h, const epb_cells* cells, const float* host_x, const float* host_y, int32_t chunks,
+ * memory, field maps read back).  These two entry points take and return
+ * pinned (page-locked) host buffers with no separate copy: the kernels access
+ * host memory over PCIe themselves, so the transfer and the cell work overlap.
+ *   epb_forward_host: the scatter reads the node positions from host_x /
+ *     host_y and stores those of the nodes in the cell ranges into the device
+ *     arrays cells->x / cells->y (for the backward); then it continues exactly
+ *     as epb_forward (same results).
+ *   epb_backward_host: as epb_backward into grad_x / grad_y (device), each
+ *     gradient also stored to host_grad_x / host_grad_y; they are complete once
+ *     `stream` has been synchronised.
+ * Non-pinned host buffers are rejected with EPB_EINVAL.  Whole-grid handles
+ * only.  No reference counterpart as entry points. */
+int epb_forward_host(epb_handle* h, const epb_cells* cells, const float* host_x, const float* host_y,
                      epb_stream stream, float* density, float* potential, float* field_x, float* field_y,
                      float* energy);
-int epb_backward_host(epb_handle* h, const epb_cells* cells, const float* grad_out, int32_t chunks, epb_stream stream,
+int epb_backward_host(epb_handle* h, const epb_cells* cells, const float* grad_out, epb_stream stream,
                       float* grad_x, float* grad_y, float* host_grad_x, float* host_grad_y);
 
 /* ---- Global-placement loop pieces (the operator's callers) -------------
