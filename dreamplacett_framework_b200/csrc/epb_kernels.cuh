@@ -67,6 +67,13 @@ struct DstTable {
     float* p[kMaxShards];
 };
 
+// Cell kernels: footprints at most kOyCache bins wide compute their column
+// overlaps once per cell (compile-time knob EPB_OY_CACHE).
+constexpr int kOyCache = 4;
+#ifndef EPB_OY_CACHE
+#define EPB_OY_CACHE 1
+#endif
+
 // Register caps of the cell kernels (0 = no bound).
 #ifndef EPB_SCATTER_MINB
 #define EPB_SCATTER_MINB 0
@@ -107,6 +114,25 @@ k_scatter(CellView c, GridGeom g, float qscale, unsigned long long* __restrict__
         if (st < 0) { atomicOr(flags, kFlagNonFinite); return; }
         if (st != 1) return;
         const int kxa = max(f.kx0, row0), kxb = min(f.kx1, row1 - 1);
+        if (EPB_OY_CACHE && f.ky1 - f.ky0 < kOyCache) {
+            // the column overlaps are the same for every row: computed once
+            float oy[kOyCache];
+#pragma unroll
+            for (int j = 0; j < kOyCache; ++j)
+                oy[j] = f.ky0 + j <= f.ky1 ? bin_overlap(f.y, f.ey, g.yl, g.bsy, f.ky0 + j) : 0.0f;
+            for (int kx = kxa; kx <= kxb; ++kx) {
+                const float oxr = __fmul_rn(bin_overlap(f.x, f.ex, g.xl, g.bsx, kx), f.r);
+                if (oxr == 0.0f) continue;
+                unsigned long long* row = grid + (int64_t)(kx - row0) * g.N + f.ky0;
+#pragma unroll
+                for (int j = 0; j < kOyCache; ++j) {
+                    if (f.ky0 + j > f.ky1) break;
+                    const long long q = __float2ll_rn(__fmul_rn(__fmul_rn(oxr, oy[j]), qscale));
+                    if (q != 0) atomicAdd(row + j, (unsigned long long)q);
+                }
+            }
+            return;
+        }
         for (int kx = kxa; kx <= kxb; ++kx) {
             const float oxr = __fmul_rn(bin_overlap(f.x, f.ex, g.xl, g.bsx, kx), f.r);
             if (oxr == 0.0f) continue;
@@ -769,6 +795,25 @@ k_gather(CellView c, GridGeom g, const float2* __restrict__ fxy,
                 atomicOr(flags, kFlagHalo);
                 kxb = row1 + halo - 1;
             }
+            if (EPB_OY_CACHE && fxy && f.ky1 - f.ky0 < kOyCache) {
+                // column overlaps computed once per cell; the same products in the same order
+                float oy[kOyCache];
+#pragma unroll
+                for (int j = 0; j < kOyCache; ++j)
+                    oy[j] = f.ky0 + j <= f.ky1 ? bin_overlap(f.y, f.ey, g.yl, g.bsy, f.ky0 + j) : 0.0f;
+                for (int kx = f.kx0; kx <= kxb; ++kx) {
+                    const float ox = bin_overlap(f.x, f.ex, g.xl, g.bsx, kx);
+                    const float2* rowp = fxy + (int64_t)(kx - row0) * g.N + f.ky0;
+#pragma unroll
+                    for (int j = 0; j < kOyCache; ++j) {
+                        if (f.ky0 + j > f.ky1) break;
+                        const float w = ox * oy[j];
+                        const float2 fv = __ldg(rowp + j);
+                        ax = fmaf(w, fv.x, ax);
+                        ay = fmaf(w, fv.y, ay);
+                    }
+                }
+            } else
             for (int kx = f.kx0; kx <= kxb; ++kx) {
                 const float ox = bin_overlap(f.x, f.ex, g.xl, g.bsx, kx);
                 const int64_t rowoff = (int64_t)(kx - row0) * g.N;
