@@ -59,11 +59,11 @@ STAGE_BYTES = {
 # build (the kernel summary under profiles/); ncu flushes caches per launch, so
 # these are cold-cache figures.
 NCU_TRAFFIC_C3 = {
-    "scatter": 72.7e6,
-    "row_fwd": 60.5e6,
-    "column": 16.8e6,
-    "row_inv": 60.4e6,
-    "gather": 79.8e6,
+    "scatter": 72.9e6,
+    "row_fwd": 60.8e6,
+    "column": 16.9e6,
+    "row_inv": 60.1e6,
+    "gather": 79.5e6,
 }
 
 
