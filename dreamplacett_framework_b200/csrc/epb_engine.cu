@@ -49,10 +49,16 @@ struct epb_handle {
     double* ovf_partials = nullptr;   // [2 * kOvfMaxBlocks]
     unsigned* ovf_counter = nullptr;
     unsigned* linf_bits = nullptr;
-    // band selection of a shard's scatter / gather (k_band_select)
+    // band selection of a shard's scatter / gather (k_band_select): the cells
+    // meeting the band and the cells owned by it, with the cell view the own
+    // list was made from (the gather reuses it for the same cell arrays)
     int* sel_list = nullptr;
     int* sel_count = nullptr;
+    int* own_list = nullptr;
+    int* own_count = nullptr;
     int64_t sel_cap = 0;
+    bool own_valid = false;
+    CellView own_key{};
     // peer transport (epb_shard_peer_buffers / epb_shard_connect)
     float* p_t1 = nullptr;      // t1_recv [M*NB]
     float* p_g = nullptr;       // g_recv [kColOutputs*M*NB]
@@ -179,7 +185,8 @@ int dev_alloc(epb_handle* h, T** p, size_t count) {
 void free_all(epb_handle* h) {
     void* ptrs[] = {h->grid, h->grid2, h->init, h->t1, h->g, h->fxy, h->twM, h->qwM,
                     h->twN, h->qwN, h->partials, h->counter, h->energy_d, h->flags,
-                    h->ovf_partials, h->ovf_counter, h->linf_bits, h->sel_list, h->sel_count};
+                    h->ovf_partials, h->ovf_counter, h->linf_bits, h->sel_list, h->sel_count,
+                    h->own_list, h->own_count};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     for (int q = 0; q < kMaxShards; ++q) {
@@ -406,27 +413,40 @@ int solve_from_t1(epb_handle* h, cudaStream_t st, float* potential, float* field
     return EPB_OK;
 }
 
-// On a shard (P > 1): list the cells this band's scatter (mode 0) or gather
-// (mode 1) visits and point v at the list.  The list buffer grows with the cell
-// count (that call synchronises and allocates).
-int band_selection(epb_handle* h, CellView& v, int mode, cudaStream_t st) {
+// Same cell arrays and ranges: the lists made from one view serve the other.
+bool same_cells(const CellView& a, const CellView& b) {
+    return a.x == b.x && a.ox == b.ox && a.sx == b.sx && a.b0 == b.b0 && a.n0 == b.n0 && a.b1 == b.b1 && a.n == b.n;
+}
+
+// On a shard (P > 1): list the cells meeting this band (the scatter's list,
+// when `meet`) and the cells owned by it (the gather's list, always); v then
+// points at the first list made.  The buffers grow with the cell count (that
+// call synchronises and allocates).
+int band_selection(epb_handle* h, CellView& v, bool meet, cudaStream_t st) {
     const int64_t nseg = (v.n + kSelChunk - 1) / kSelChunk;
     if (v.n > h->sel_cap) {
         EPB_CUDA(h, cudaStreamSynchronize(st));
-        if (h->sel_list) cudaFree(h->sel_list);
-        if (h->sel_count) cudaFree(h->sel_count);
-        h->sel_list = nullptr;
-        h->sel_count = nullptr;
+        int** bufs[] = {&h->sel_list, &h->sel_count, &h->own_list, &h->own_count};
+        for (int** b : bufs) {
+            if (*b) cudaFree(*b);
+            *b = nullptr;
+        }
         h->sel_cap = 0;
+        h->own_valid = false;
         if (int rc = dev_alloc(h, &h->sel_list, (size_t)(nseg * kSelChunk))) return rc;
         if (int rc = dev_alloc(h, &h->sel_count, (size_t)nseg)) return rc;
+        if (int rc = dev_alloc(h, &h->own_list, (size_t)(nseg * kSelChunk))) return rc;
+        if (int rc = dev_alloc(h, &h->own_count, (size_t)nseg)) return rc;
         h->sel_cap = v.n;
     }
-    k_band_select<<<(unsigned)nseg, 256, 0, st>>>(v, geom(h), h->row0, h->row0 + h->RB, mode, h->sel_list,
-                                                  h->sel_count, h->flags);
+    k_band_select<<<(unsigned)nseg, 256, 0, st>>>(v, geom(h), h->row0, h->row0 + h->RB,
+                                                  meet ? h->sel_list : nullptr, meet ? h->sel_count : nullptr,
+                                                  h->own_list, h->own_count, h->flags);
     EPB_LAUNCHED(h, "k_band_select launch");
-    v.sel = h->sel_list;
-    v.sel_n = h->sel_count;
+    h->own_key = v;
+    h->own_valid = true;
+    v.sel = meet ? h->sel_list : h->own_list;
+    v.sel_n = meet ? h->sel_count : h->own_count;
     return EPB_OK;
 }
 
@@ -437,7 +457,7 @@ int scatter_into(epb_handle* h, const CellView& v0, cudaStream_t st, long long* 
     CellView v = v0;
     unsigned blocks = cell_blocks(v.n);
     if (h->P > 1) {
-        if (int rc = band_selection(h, v, 0, st)) return rc;
+        if (int rc = band_selection(h, v, true, st)) return rc;
         blocks = (unsigned)((v.n + kSelChunk - 1) / kSelChunk);   // one CTA per segment
     }
     k_scatter<false><<<blocks, 256, 0, st>>>(v, geom(h), qscale, (unsigned long long*)grid, h->row0, h->row0 + h->RB,
@@ -453,7 +473,13 @@ int shard_gather(epb_handle* h, const CellView& v0, const float2* fxy, int halo,
     CellView v = v0;
     unsigned blocks = cell_blocks(v.n);
     if (h->P > 1) {
-        if (int rc = band_selection(h, v, 1, st)) return rc;
+        if (h->own_valid && same_cells(h->own_key, v)) {
+            // the forward's selection of the same cells (positions are the forward's)
+            v.sel = h->own_list;
+            v.sel_n = h->own_count;
+        } else if (int rc = band_selection(h, v, false, st)) {
+            return rc;
+        }
         blocks = (unsigned)((v.n + kSelChunk - 1) / kSelChunk);   // one CTA per segment
     }
     k_gather<false><<<blocks, 256, 0, st>>>(v, geom(h), fxy, nullptr, nullptr, h->row0, h->row0 + h->RB, halo, 1, grad_out,
@@ -855,6 +881,7 @@ int epb_descent_step(epb_handle* h, const epb_cells* cells, float* x, float* y, 
     DeviceGuard guard(h->dev);
     cudaStream_t st = (cudaStream_t)stream;
     EPB_CUDA(h, cudaMemsetAsync(h->linf_bits, 0, sizeof(unsigned), st));
+    h->own_valid = false;  // positions move: no selection made before this step stays valid
     if (v.n > 0) {
         k_grad_linf<<<cell_blocks(v.n), 256, 0, st>>>(v, grad_x, grad_y, h->linf_bits, h->flags);
         EPB_LAUNCHED(h, "k_grad_linf launch");

@@ -712,26 +712,26 @@ k_row_inv(RowInvArgs a) {
 // ---------------------------------------------------------------------------
 // Band selection (sharded grids): the cells a row band's scatter or gather
 // visits, listed so those kernels run full warps instead of testing every cell.
-// Only the x data is read.  mode 0: cells whose rows meet [row0, row1) (the
-// scatter; cells that contribute nothing go to the list of the band holding
-// row 0, which then reports their non-finite data); mode 1: cells whose first
-// row is in [row0, row1) (the gather).  Cells with non-finite x data are
-// flagged here.  Each CTA compacts a fixed segment of kSelChunk cells (no
-// global atomics); the consumers run one CTA per segment.
+// Only the x data is read.  Two lists, each optional: `meet`, the cells whose
+// rows meet [row0, row1) (the scatter; cells that contribute nothing go to the
+// list of the band holding row 0, which then reports their non-finite data),
+// and `own`, the cells whose first row is in [row0, row1) (the gather).  Cells
+// with non-finite x data are flagged here.  Each CTA compacts a fixed segment
+// of kSelChunk cells (no global atomics); the consumers run one CTA per segment.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256)
-k_band_select(CellView c, GridGeom g, int row0, int row1, int mode, int* __restrict__ list,
-              int* __restrict__ counts, unsigned* __restrict__ flags) {
+k_band_select(CellView c, GridGeom g, int row0, int row1, int* __restrict__ meet, int* __restrict__ meet_n,
+              int* __restrict__ own, int* __restrict__ own_n, unsigned* __restrict__ flags) {
     // CTA s compacts cells [s * kSelChunk, (s + 1) * kSelChunk) into list[s * kSelChunk ...]
-    // in increasing order and writes their number to counts[s]
-    __shared__ int wtot[8];
+    // in increasing order and writes their number to list_n[s], for each list given
+    __shared__ int wtot[2][8];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t seg0 = (int64_t)blockIdx.x * kSelChunk;
-    int run = 0;
+    int run_m = 0, run_o = 0;
     unsigned bad = 0;
     for (int r = 0; r < kSelChunk / 256; ++r) {
         const int64_t i = seg0 + r * 256 + threadIdx.x;
-        bool in = false;
+        bool in_m = false, in_o = false;
         if (i < c.n) {
             const int64_t node = cell_node(c, i);
             float x = __ldg(c.x + node);
@@ -743,24 +743,35 @@ k_band_select(CellView c, GridGeom g, int row0, int row1, int mode, int* __restr
                 const int kx0 = bin_floor(x, g.xl, g.bsx, g.ibsx, g.M);
                 const int kx1 = min(bin_floor(__fadd_rn(x, sx), g.xl, g.bsx, g.ibsx, g.M), g.M - 1);
                 const bool empty = !(sx > 0.0f) || kx0 > kx1;
-                if (mode == 0) in = empty ? row0 == 0 : !(kx1 < row0 || kx0 >= row1);
-                else in = !empty && kx0 >= row0 && kx0 < row1;
+                in_m = empty ? row0 == 0 : !(kx1 < row0 || kx0 >= row1);
+                in_o = !empty && kx0 >= row0 && kx0 < row1;
             }
         }
-        const unsigned m = __ballot_sync(0xffffffffu, in);
-        if (lane == 0) wtot[warp] = __popc(m);
+        const unsigned mm = __ballot_sync(0xffffffffu, in_m), mo = __ballot_sync(0xffffffffu, in_o);
+        if (lane == 0) {
+            wtot[0][warp] = __popc(mm);
+            wtot[1][warp] = __popc(mo);
+        }
         __syncthreads();
-        int before = 0, total = 0;
+        int bm = 0, tm = 0, bo = 0, to = 0;
 #pragma unroll
         for (int w = 0; w < 8; ++w) {
-            before += w < warp ? wtot[w] : 0;
-            total += wtot[w];
+            bm += w < warp ? wtot[0][w] : 0;
+            tm += wtot[0][w];
+            bo += w < warp ? wtot[1][w] : 0;
+            to += wtot[1][w];
         }
-        if (in) list[seg0 + run + before + __popc(m & ((1u << lane) - 1u))] = (int)i;
-        run += total;
+        const unsigned below = (1u << lane) - 1u;
+        if (meet && in_m) meet[seg0 + run_m + bm + __popc(mm & below)] = (int)i;
+        if (own && in_o) own[seg0 + run_o + bo + __popc(mo & below)] = (int)i;
+        run_m += tm;
+        run_o += to;
         __syncthreads();
     }
-    if (threadIdx.x == 0) counts[blockIdx.x] = run;
+    if (threadIdx.x == 0) {
+        if (meet_n) meet_n[blockIdx.x] = run_m;
+        if (own_n) own_n[blockIdx.x] = run_o;
+    }
     if (bad) atomicOr(flags, kFlagNonFinite);
 }
 

@@ -190,7 +190,12 @@ int epb_shard_columns(epb_handle* h, const float* t1_recv, epb_stream stream, fl
  * match the epb_shard_columns call (non-NULL potential_band) */
 int epb_shard_rows_inverse(epb_handle* h, const float* g_recv, epb_stream stream, float* potential_band,
                            float* field_x_band, float* field_y_band, float* fxy_band);
-/* gradient of the cells whose first bin row lies in this band */
+/* gradient of the cells whose first bin row lies in this band.  Given the
+ * same cell arrays and ranges as the shard's last forward (and no
+ * epb_descent_step since), the gather reuses that forward's list of the band's
+ * cells.  The positions must be the ones the forward saw, as in the
+ * reference, whose backward reads the pos the forward saved
+ * (integration/scatter_ttnn_client.py:833). */
 int epb_shard_gather(epb_handle* h, const epb_cells* cells, const float* fxy_ext, int32_t halo_rows,
                      const float* grad_out, epb_stream stream, float* grad_x, float* grad_y);
 
