@@ -315,7 +315,8 @@ struct ColCfg {
     static constexpr int T = P * S;
     static constexpr int W = 2 * S;
     static constexpr int LP = Padded<L>::value;
-    static constexpr size_t SMEM = (size_t)S * LP * sizeof(float2) + (size_t)W * L * sizeof(float);
+    // S forward sequences (column pairs), then W = 2S inverse sequences (one per column)
+    static constexpr size_t SMEM = (size_t)W * LP * sizeof(float2);
     // the register cap applies to the 256-thread configurations (L <= 2048)
     static constexpr int MINB = T <= 256 ? EPB_COL_MINB : 1;
 };
@@ -369,14 +370,15 @@ k_col(const __grid_constant__ ColArgs a) {
     // CTA-wide phases: the strip's float4 loads and stores span both sequences of a CTA
     constexpr bool GS = false;
     extern __shared__ float2 sm_col[];
-    float2* buf = sm_col;                                   // S x LP complex
-    // b = auv / (wu^2 + wv^2) per column (W x L): the potential's spectrum; the field
-    // spectra are b * wu / 2 and b * wv, so no weight is evaluated twice
-    float* bsp = reinterpret_cast<float*>(sm_col + S * LP);
+    // W x LP complex.  Forward: sequence s < S holds columns (2s, 2s+1) as real and
+    // imaginary parts.  Inverse: sequence r*S + s holds output r of the same two
+    // columns (r = 0 the field_x form, r = 1 the potential form; the two forms
+    // differ in scale by up to ~1/wu, so each sequence packs one form), and
+    // output 0 takes over forward sequence s in place.
+    float2* buf = sm_col;
     const int N = a.N;
     const int c0 = blockIdx.x * W;
     const int grp = threadIdx.x / P;
-    float2* myseq = buf + grp * LP;
     const int lane = threadIdx.x % P;
 
     // ---- load T1 strip [L rows][W cols], Makhoul reorder along rows ----
@@ -393,18 +395,21 @@ k_col(const __grid_constant__ ColArgs a) {
         buf[(s0 + 1) * LP + pos] = make_float2(v.z, v.w);
     }
     seq_sync<P, GS>(grp);
-    fft_seq<L, false, GS>(myseq, lane, a.tw, true, grp);
+    fft_seq<L, false, GS>(buf + grp * LP, lane, a.tw, true, grp);
 
-    // ---- auv + energy ----
+    // ---- auv, b = auv / (wu^2 + wv^2), energy, and the inverse inputs ----
     // One iteration handles the index pair (u, L-u) of one sequence (u = 0 handles
     // the self-paired 0 and L/2): for two real columns packed as one FFT Z,
     //   Va_u = (Z_u + conj(Z_{L-u}))/2,  Vb_u = -i (Z_u - conj(Z_{L-u}))/2,
     // Va_{L-u} = conj(Va_u), Vb_{L-u} = conj(Vb_u), and the quarter-wave factor of
-    // L-u is that of u with cos and sin swapped.
+    // L-u is that of u with cos and sin swapped.  The inverse inputs at n need b at
+    // n and L-n, so the same iteration writes V_u and V_{L-u} of both outputs, at
+    // the positions it read (no other iteration touches them).
     const float scale = 2.0f / (float)L;
+    const float hku = 0.5f * a.ku;
     double esum = 0.0;
-    for (int e = GS ? lane : threadIdx.x; e < (GS ? L / 2 : S * (L / 2)); e += (GS ? P : T)) {
-        const int s = GS ? grp : e / (L / 2), u = GS ? e : e % (L / 2);
+    for (int e = threadIdx.x; e < S * (L / 2); e += T) {
+        const int s = e / (L / 2), u = e % (L / 2);
         const int u2 = u == 0 ? L / 2 : L - u;   // the second index of this iteration
         const float2 Z = buf[s * LP + pidx(u)];
         const float2 Zr = buf[s * LP + pidx(u == 0 ? 0 : L - u)];
@@ -412,6 +417,7 @@ k_col(const __grid_constant__ ColArgs a) {
         const float2 Va = make_float2(0.5f * (Z.x + Zr.x), 0.5f * (Z.y - Zr.y));
         const float2 Vb = make_float2(0.5f * (Z.y + Zr.y), -0.5f * (Z.x - Zr.x));
         const float2 q = __ldg(a.qw + u);
+        const float2 q2 = __ldg(a.qw + u2);
         float x1[2], x2[2];  // [column p]: values at u and at u2
         x1[0] = scale * (Va.x * q.x + Va.y * q.y);
         x1[1] = scale * (Vb.x * q.x + Vb.y * q.y);
@@ -420,12 +426,12 @@ k_col(const __grid_constant__ ColArgs a) {
             x2[1] = scale * (Vb.x * q.y - Vb.y * q.x);
         } else {
             // index L/2 pairs with itself: Va = (Zh.x, 0), Vb = (Zh.y, 0)
-            const float2 qh = __ldg(a.qw + L / 2);
-            x2[0] = scale * (Zh.x * qh.x);
-            x2[1] = scale * (Zh.y * qh.x);
+            x2[0] = scale * (Zh.x * q2.x);
+            x2[1] = scale * (Zh.y * q2.x);
         }
         const float wu1 = (float)u * a.ku, wu2 = (float)u2 * a.ku;
         const float cu1 = u == 0 ? 1.0f : 2.0f;
+        float b1[2], b2[2];  // [column p]: b at u and at u2
 #pragma unroll
         for (int p = 0; p < 2; ++p) {
             const int col = c0 + 2 * s + p;
@@ -433,13 +439,37 @@ k_col(const __grid_constant__ ColArgs a) {
             const float wv = (float)gcol * a.kv;
             const float wv2 = wv * wv;
             const float d1 = wu1 * wu1 + wv2, d2 = wu2 * wu2 + wv2;
-            const float b1 = d1 == 0.0f ? 0.0f : __fdividef(x1[p], d1);
-            const float b2 = __fdividef(x2[p], d2);
-            bsp[(2 * s + p) * L + u] = b1;
-            bsp[(2 * s + p) * L + u2] = b2;
+            b1[p] = d1 == 0.0f ? 0.0f : __fdividef(x1[p], d1);
+            b2[p] = __fdividef(x2[p], d2);
             // energy terms c_u c_v auv^2 / (wu^2 + wv^2), accumulated in fp64
             const float cv = gcol == 0 ? 1.0f : 2.0f;
-            if (col < N) esum += (double)(cu1 * cv * (x1[p] * b1)) + (double)(2.0f * cv * (x2[p] * b2));
+            if (col < N) esum += (double)(cu1 * cv * (x1[p] * b1[p])) + (double)(2.0f * cv * (x2[p] * b2[p]));
+        }
+        // inverse inputs (Makhoul IDCT pre-twiddle of A_n, A_{L-n}, two columns packed):
+        //   output 0, the IDXST form: IDCT of c_n = a_{L-n} with a_u = b_u * wu / 2 (c_0 = 0)
+        //   output 1, the IDCT form: A_u = b_u (A_L = 0)
+        float2* v0s = buf + s * LP;
+        float2* v1s = buf + (S + s) * LP;
+        if (u != 0) {
+            float an[2], am[2];
+#pragma unroll
+            for (int p = 0; p < 2; ++p) {
+                an[p] = b2[p] * ((float)u2 * hku);
+                am[p] = b1[p] * ((float)u * hku);
+            }
+            v0s[pidx(u)] = idct_pre(an[0], am[0], an[1], am[1], q);
+            v0s[pidx(u2)] = idct_pre(am[0], an[0], am[1], an[1], q2);
+            v1s[pidx(u)] = idct_pre(b1[0], b2[0], b1[1], b2[1], q);
+            v1s[pidx(u2)] = idct_pre(b2[0], b1[0], b2[1], b1[1], q2);
+        } else {
+            // V_{L/2} = (A_{L/2} - i A_{L/2}) e^{i pi / 4}
+            float h[2];
+#pragma unroll
+            for (int p = 0; p < 2; ++p) h[p] = b2[p] * ((float)(L / 2) * hku);
+            v0s[pidx(0)] = idct_pre(0.0f, 0.0f, 0.0f, 0.0f, q);
+            v0s[pidx(L / 2)] = idct_pre(h[0], h[0], h[1], h[1], q2);
+            v1s[pidx(0)] = idct_pre(b1[0], 0.0f, b1[1], 0.0f, q);
+            v1s[pidx(L / 2)] = idct_pre(b2[0], b2[0], b2[1], b2[1], q2);
         }
     }
     // ---- deterministic energy reduction, done before the inverse rounds so the
@@ -478,60 +508,26 @@ k_col(const __grid_constant__ ColArgs a) {
     }
     seq_sync<P, GS>(grp);
 
-    // ---- two inverse transforms along x: 0 -> gx (IDXST form), 1 -> gp ----
-    for (int r = 0; r < kColOutputs; ++r) {
-        // build V for seq s = columns (2s, 2s+1); one thread makes V_n and V_{L-n}
-        for (int e = GS ? lane : threadIdx.x; e < (GS ? L / 2 : S * (L / 2)); e += (GS ? P : T)) {
-            const int s = GS ? grp : e / (L / 2), n = GS ? e : e % (L / 2);
-            const int nm = L - n;  // partner index (L when n == 0)
-            float An[2], Am[2];    // A_n, A_{L-n} of the two packed columns (A_L = 0)
-            const float hku = 0.5f * a.ku;
-#pragma unroll
-            for (int p = 0; p < 2; ++p) {
-                const float* bc = bsp + (2 * s + p) * L;
-                const float bn = bc[n], bm = n == 0 ? 0.0f : bc[nm];
-                if (r == 0) {
-                    // IDXST via IDCT of c_n = a_{L-n} (c_0 = c_L = 0), a_u = b_u * wu / 2
-                    An[p] = n == 0 ? 0.0f : bm * ((float)nm * hku);
-                    Am[p] = n == 0 ? 0.0f : bn * ((float)n * hku);
-                } else {
-                    An[p] = bn;
-                    Am[p] = bm;
-                }
-            }
-            float2* sq = buf + s * LP;
-            sq[pidx(n)] = idct_pre(An[0], Am[0], An[1], Am[1], __ldg(a.qw + n));
-            if (n != 0) {
-                sq[pidx(nm)] = idct_pre(Am[0], An[0], Am[1], An[1], __ldg(a.qw + nm));
-            } else {
-                // V_{L/2} = (A_{L/2} - i A_{L/2}) e^{i pi / 4}
-                float h[2];
-#pragma unroll
-                for (int p = 0; p < 2; ++p) {
-                    const float bh = bsp[(2 * s + p) * L + L / 2];
-                    h[p] = r == 0 ? bh * ((float)(L / 2) * hku) : bh;
-                }
-                sq[pidx(L / 2)] = idct_pre(h[0], h[0], h[1], h[1], __ldg(a.qw + L / 2));
-            }
-        }
-        seq_sync<P, GS>(grp);
-        fft_seq<L, true, GS>(myseq, lane, a.tw, true, grp);
-        const int64_t oo = (int64_t)r * a.ostride;
-        const int rbm = (1 << a.lrb) - 1;
+    // ---- inverse transforms along x: group g takes outputs 0 and 1 of its column pair ----
+    fft_seq<L, true, GS>(buf + grp * LP, lane, a.tw, true, grp);
+    fft_seq<L, true, GS>(buf + (S + grp) * LP, lane, a.tw, true, grp);
+    const int rbm = (1 << a.lrb) - 1;
 #pragma unroll 4
-        for (int e = threadIdx.x; e < L * (W / 4); e += T) {
-            const int k = e / (W / 4), q4 = e % (W / 4);
-            const int col = c0 + 4 * q4;
-            const int src = pidx(makhoul_pos(k, L));
-            float2 v0 = buf[(2 * q4) * LP + src];
-            float2 v1 = buf[(2 * q4 + 1) * LP + src];
-            if (r == 0 && (k & 1)) { v0.x = -v0.x; v0.y = -v0.y; v1.x = -v1.x; v1.y = -v1.y; }
-            if (col < N)
-                *reinterpret_cast<float4*>(a.g.p[k >> a.lrb] + oo + ((int64_t)(col >> a.lsw) << (a.lrb + a.lsw)) +
-                                           ((int64_t)(k & rbm) << a.lsw) + (col & ((1 << a.lsw) - 1))) =
-                    make_float4(v0.x, v0.y, v1.x, v1.y);
+    for (int e = threadIdx.x; e < L * (W / 4); e += T) {
+        const int k = e / (W / 4), q4 = e % (W / 4);
+        const int col = c0 + 4 * q4;
+        const int src = pidx(makhoul_pos(k, L));
+        // columns 4q4 .. 4q4+3: pairs 2q4 and 2q4+1, outputs 0 and 1
+        float2 g0 = buf[(2 * q4) * LP + src], g1 = buf[(2 * q4 + 1) * LP + src];
+        const float2 p0 = buf[(S + 2 * q4) * LP + src], p1 = buf[(S + 2 * q4 + 1) * LP + src];
+        // output 0: the IDXST, the IDCT of the reversed input with odd outputs negated
+        if (k & 1) { g0.x = -g0.x; g0.y = -g0.y; g1.x = -g1.x; g1.y = -g1.y; }
+        if (col < N) {
+            float* dst = a.g.p[k >> a.lrb] + ((int64_t)(col >> a.lsw) << (a.lrb + a.lsw)) +
+                         ((int64_t)(k & rbm) << a.lsw) + (col & ((1 << a.lsw) - 1));
+            *reinterpret_cast<float4*>(dst) = make_float4(g0.x, g0.y, g1.x, g1.y);
+            *reinterpret_cast<float4*>(dst + a.ostride) = make_float4(p0.x, p0.y, p1.x, p1.y);
         }
-        __syncthreads();
     }
 }
 
