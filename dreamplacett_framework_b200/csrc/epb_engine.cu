@@ -727,6 +727,9 @@ int epb_gather(epb_handle* h, const epb_cells* cells, const float* field_x, cons
 
 namespace {
 
+// The column pass and the row inverse move the exchanged blocks as float4.
+bool aligned(const void* p, uintptr_t bytes) { return (reinterpret_cast<uintptr_t>(p) & (bytes - 1)) == 0; }
+
 // Device address of a pinned host buffer (EINVAL when it is not pinned).
 int host_device_ptr(epb_handle* h, const void* host, void** dev) {
     cudaPointerAttributes at;
@@ -948,6 +951,8 @@ int epb_shard_columns(epb_handle* h, const float* t1_recv, epb_stream stream, fl
                       double* energy_partial) {
     if (!h) return EPB_EINVAL;
     if (!t1_recv || !g_send) return fail(h, EPB_EINVAL, "t1_recv and g_send must be non-NULL");
+    if (!aligned(t1_recv, 16) || !aligned(g_send, 16))
+        return fail(h, EPB_EINVAL, "t1_recv and g_send must be 16-byte aligned");
     DeviceGuard guard(h->dev);
     cudaStream_t st = (cudaStream_t)stream;
     ProfCall pc(h, st);
@@ -965,6 +970,8 @@ int epb_shard_rows_inverse(epb_handle* h, const float* g_recv, epb_stream stream
                            float* field_x_band, float* field_y_band, float* fxy_band) {
     if (!h) return EPB_EINVAL;
     if (!g_recv || !fxy_band) return fail(h, EPB_EINVAL, "g_recv and fxy_band must be non-NULL");
+    if (!aligned(g_recv, 16) || !aligned(fxy_band, 8))
+        return fail(h, EPB_EINVAL, "g_recv must be 16-byte and fxy_band 8-byte aligned");
     DeviceGuard guard(h->dev);
     cudaStream_t st = (cudaStream_t)stream;
     ProfCall pc(h, st);

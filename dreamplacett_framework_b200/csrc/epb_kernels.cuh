@@ -564,13 +564,6 @@ struct RowInvArgs {
     int want_phi;
 };
 
-// element l of band row r of column-pass output o
-__device__ __forceinline__ float rowinv_load(const RowInvArgs& a, int o, int r, int l) {
-    const int c = l & ((1 << a.lnb) - 1);
-    return __ldg(a.g + (int64_t)(l >> a.lnb) * a.qstride + (int64_t)o * a.ostride +
-                 ((int64_t)(c >> a.lsw) << (a.lrb + a.lsw)) + ((int64_t)r << a.lsw) + (c & ((1 << a.lsw) - 1)));
-}
-
 template <int L>
 __global__ void __launch_bounds__(RowInvCfg<L>::T, RowInvCfg<L>::MINB)
 k_row_inv(RowInvArgs a) {
@@ -581,106 +574,98 @@ k_row_inv(RowInvArgs a) {
     float2* buf = sm_rowinv;
     const int row0 = blockIdx.x * ROWS;
     const int grp = threadIdx.x / P, lane = threadIdx.x % P;
-    // one thread builds V_n and V_{L-n} from the same four loads; with GS each
-    // group fills only its own sequence
-    if constexpr (GS) {
-        // group grp < ROWS: fx + i fy of band row row0 + grp (field_x form, wv * potential form);
-        // group ROWS + j: potential rows row0 + 2j, row0 + 2j + 1 (potential form).
-        // A batch of U indices per thread issues all its loads first; the partner index
-        // L - n wraps to 0 for n = 0 (a valid address) and the select below drops it.
-        const bool fxy_grp = grp < ROWS;
-        const int rA = fxy_grp ? row0 + grp : row0 + 2 * (grp - ROWS);
-        const int rB = fxy_grp ? rA : rA + 1;
-        const bool okA = rA < a.M && (fxy_grp || a.want_phi), okB = rB < a.M && (fxy_grp || a.want_phi);
-        const int oA = fxy_grp ? 0 : 1;                       // output read for the real part
-        const int lA = okA ? rA : 0, lB = okB ? rB : 0;
+    // ---- stage: outputs 0 and 1 of the CTA's rows, read once as float4 (strips are
+    //      at least 8 columns wide and 16-byte aligned), stored contiguously as
+    //      stage[(o * ROWS + j) * L + l] at the top of the sequence buffers ----
+    constexpr int NST = 2 * ROWS * L;                 // staged floats
+    static_assert(NST <= 2 * S * LP, "staging fits in the sequence buffers");
+    float* stage = reinterpret_cast<float*>(buf) + (2 * S * LP - NST);
+    {
+        constexpr int NV = NST / 4, IT = (NV + T - 1) / T;
+        float4 v[IT];
+#pragma unroll
+        for (int i = 0; i < IT; ++i) {
+            const int e = threadIdx.x + i * T;
+            v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (e < NV) {
+                const int l = (e % (L / 4)) * 4, oj = e / (L / 4), o = oj / ROWS, j = oj % ROWS;
+                const int row = row0 + j, c = l & ((1 << a.lnb) - 1);
+                if (row < a.M)
+                    v[i] = __ldg(reinterpret_cast<const float4*>(
+                        a.g + (int64_t)(l >> a.lnb) * a.qstride + (int64_t)o * a.ostride +
+                        ((int64_t)(c >> a.lsw) << (a.lrb + a.lsw)) + ((int64_t)row << a.lsw) +
+                        (c & ((1 << a.lsw) - 1))));
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < IT; ++i) {
+            const int e = threadIdx.x + i * T;
+            if (e < NV) reinterpret_cast<float4*>(stage)[e] = v[i];
+        }
+    }
+    __syncthreads();
+    // ---- build: item (k, n) makes V_n and V_{L-n} (n = 0: V_0 and V_{L/2}) of the
+    //      sequences of rows 2k, 2k+1 (fx + i fy each) and of their potential pair.
+    //      The staged values of all items are read first: the sequences overwrite them. ----
+    {
+        constexpr int H = L / 2, NI = (ROWS / 2) * H, IT = (NI + T - 1) / T;
         const float hkv = 0.5f * a.kv;
-        float2* sq = buf + grp * LP;
-        constexpr int H = L / 2;
-        if (lane == 0 && (fxy_grp || a.want_phi)) {
-            // V_{L/2} = (A_{L/2} - i A_{L/2}) e^{i pi / 4}
-            float hA = rowinv_load(a, oA, lA, H), hB = rowinv_load(a, 1, lB, H);
-            if (fxy_grp) hB *= (float)H * hkv;
-            if (!okA) hA = 0.0f;
-            if (!okB) hB = 0.0f;
-            sq[pidx(H)] = idct_pre(hA, hA, hB, hB, __ldg(a.qw + H));
-        }
-        constexpr int U = 4;
-        static_assert((H / P) % U == 0, "whole batches");
-        // a potential group with no potential wanted loads nothing (its transform is not stored)
-        const int n_end = fxy_grp || a.want_phi ? H : 0;
-        for (int n0 = lane; n0 < n_end; n0 += U * P) {
-            float an[U], am[U], bn[U], bm[U];
+        // [item][row p of the pair]: output 0 at n, at L-n; output 1 at n, at L-n
+        float x0n[IT][2], x0m[IT][2], x1n[IT][2], x1m[IT][2];
 #pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int n = n0 + u * P, nm = (L - n) & (L - 1);
-                an[u] = rowinv_load(a, oA, lA, n);
-                am[u] = rowinv_load(a, oA, lA, nm);
-                bn[u] = rowinv_load(a, 1, lB, n);
-                bm[u] = rowinv_load(a, 1, lB, nm);
-            }
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int n = n0 + u * P, nm = L - n;
-                float An0, Am0, An1, Am1;
-                if (fxy_grp) {
-                    // fx: IDCT of the Gx row; fy: IDXST of the Gy row = IDCT of b (b_0 = 0,
-                    // b_m = a_{L-m}) with the 1/2 folded in, Gy_l = wv_l * Gp_l
-                    An0 = an[u];
-                    Am0 = am[u];
-                    An1 = bm[u] * ((float)nm * hkv);
-                    Am1 = bn[u] * ((float)n * hkv);
-                    if (n == 0) { Am0 = 0.0f; An1 = 0.0f; Am1 = 0.0f; }
-                } else {
-                    An0 = an[u];
-                    Am0 = am[u];
-                    An1 = bn[u];
-                    Am1 = bm[u];
-                    if (n == 0) { Am0 = 0.0f; Am1 = 0.0f; }
-                }
-                if (!okA) { An0 = 0.0f; Am0 = 0.0f; }
-                if (!okB) { An1 = 0.0f; Am1 = 0.0f; }
-                sq[pidx(n)] = idct_pre(An0, Am0, An1, Am1, __ldg(a.qw + n));
-                if (n != 0) sq[pidx(nm)] = idct_pre(Am0, An0, Am1, An1, __ldg(a.qw + nm));
-            }
-        }
-    } else {
-#pragma unroll 2
-    for (int e = GS ? lane : threadIdx.x; e < (GS ? L / 2 : S * (L / 2)); e += (GS ? P : T)) {
-        const int s = GS ? grp : e / (L / 2), n = GS ? e : e % (L / 2);
-        const int nm = L - n;
-        const int h = L / 2;
-        float An[2] = {0.f, 0.f}, Am[2] = {0.f, 0.f}, Ah[2] = {0.f, 0.f};  // A_n, A_{L-n}, A_{L/2}
-        if (s < ROWS) {
-            const int row = row0 + s;
-            if (row < a.M) {
-                // fx: IDCT of the Gx row; fy: IDXST of the Gy row = IDCT of b (b_0 = 0,
-                // b_m = a_{L-m}) with the 1/2 folded in, Gy_l = wv_l * Gp_l
-                const float hkv = 0.5f * a.kv;
-                An[0] = rowinv_load(a, 0, row, n);
-                Am[0] = n == 0 ? 0.0f : rowinv_load(a, 0, row, nm);
-                An[1] = n == 0 ? 0.0f : rowinv_load(a, 1, row, nm) * ((float)nm * hkv);
-                Am[1] = n == 0 ? 0.0f : rowinv_load(a, 1, row, n) * ((float)n * hkv);
-                if (n == 0) { Ah[0] = rowinv_load(a, 0, row, h); Ah[1] = rowinv_load(a, 1, row, h) * ((float)h * hkv); }
-            }
-        } else if (a.want_phi) {
-            const int row = row0 + 2 * (s - ROWS);
+        for (int i = 0; i < IT; ++i) {
+            const int e = threadIdx.x + i * T;
+            const int k = e / H, n = e % H;
+            const int m = n == 0 ? H : L - n;   // n = 0 pairs with L/2
 #pragma unroll
             for (int p = 0; p < 2; ++p) {
-                if (row + p < a.M) {
-                    An[p] = rowinv_load(a, 1, row + p, n);
-                    Am[p] = n == 0 ? 0.0f : rowinv_load(a, 1, row + p, nm);
-                    if (n == 0) Ah[p] = rowinv_load(a, 1, row + p, h);
-                }
+                const float* s0 = stage + (2 * k + p) * L;            // output 0, row 2k + p
+                const float* s1 = stage + (ROWS + 2 * k + p) * L;     // output 1, row 2k + p
+                const bool ok = e < NI;
+                x0n[i][p] = ok ? s0[n] : 0.f;
+                x0m[i][p] = ok ? s0[m] : 0.f;
+                x1n[i][p] = ok ? s1[n] : 0.f;
+                x1m[i][p] = ok ? s1[m] : 0.f;
             }
         }
-        float2* sq = buf + s * LP;
-        sq[pidx(n)] = idct_pre(An[0], Am[0], An[1], Am[1], __ldg(a.qw + n));
-        if (n != 0) sq[pidx(nm)] = idct_pre(Am[0], An[0], Am[1], An[1], __ldg(a.qw + nm));
-        else sq[pidx(h)] = idct_pre(Ah[0], Ah[0], Ah[1], Ah[1], __ldg(a.qw + h));
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < IT; ++i) {
+            const int e = threadIdx.x + i * T;
+            if (e >= NI) break;
+            const int k = e / H, n = e % H;
+            const float2 qn = __ldg(a.qw + n);
+            float2* sp = buf + (ROWS + k) * LP;   // potential rows 2k (real), 2k + 1 (imaginary)
+            if (n != 0) {
+                const int nm = L - n;
+                const float2 qm = __ldg(a.qw + nm);
+#pragma unroll
+                for (int p = 0; p < 2; ++p) {
+                    // fx: IDCT of the Gx row; fy: IDXST of the Gy row = IDCT of b (b_0 = 0,
+                    // b_m = a_{L-m}) with the 1/2 folded in, Gy_l = wv_l * Gp_l
+                    const float an1 = x1m[i][p] * ((float)nm * hkv), am1 = x1n[i][p] * ((float)n * hkv);
+                    float2* sq = buf + (2 * k + p) * LP;
+                    sq[pidx(n)] = idct_pre(x0n[i][p], x0m[i][p], an1, am1, qn);
+                    sq[pidx(nm)] = idct_pre(x0m[i][p], x0n[i][p], am1, an1, qm);
+                }
+                sp[pidx(n)] = idct_pre(x1n[i][0], x1m[i][0], x1n[i][1], x1m[i][1], qn);
+                sp[pidx(nm)] = idct_pre(x1m[i][0], x1n[i][0], x1m[i][1], x1n[i][1], qm);
+            } else {
+                // V_0 = A_0 (A_L = 0); V_{L/2} = (A_{L/2} - i A_{L/2}) e^{i pi / 4}
+                const float2 qh = __ldg(a.qw + H);
+#pragma unroll
+                for (int p = 0; p < 2; ++p) {
+                    float2* sq = buf + (2 * k + p) * LP;
+                    sq[0] = idct_pre(x0n[i][p], 0.0f, 0.0f, 0.0f, qn);
+                    const float hb = x1m[i][p] * ((float)H * hkv);
+                    sq[pidx(H)] = idct_pre(x0m[i][p], x0m[i][p], hb, hb, qh);
+                }
+                sp[0] = idct_pre(x1n[i][0], 0.0f, x1n[i][1], 0.0f, qn);
+                sp[pidx(H)] = idct_pre(x1m[i][0], x1m[i][0], x1m[i][1], x1m[i][1], qh);
+            }
+        }
     }
-    }
-    seq_sync<P, GS>(grp);
+    __syncthreads();  // every thread wrote into every sequence
     fft_seq<L, true, GS>(buf + grp * LP, lane, a.tw, true, grp);
 #pragma unroll 2
     for (int e = GS ? lane : threadIdx.x; e < (GS ? L : S * L); e += (GS ? P : T)) {

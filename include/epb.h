@@ -166,6 +166,8 @@ int epb_error_flags(epb_handle* h, epb_stream stream, uint32_t* flags);
  *   g_recv   2*M*NB       after all-to-all(g_send): block q = [2][RB][NB] from band q
  *   fxy_ext  (RB+halo)*N*2 floats: interleaved (field_x, field_y) of this band,
  *                          then `halo` rows of the next band (point-to-point)
+ * t1_recv, g_send and g_recv are moved as float4 and must be 16-byte aligned,
+ * fxy_band 8-byte aligned (EPB_EINVAL otherwise).
  * Every cell that overlaps the band is scattered (clipped to it), so the
  * fixed-point density of every bin is the same integer as on one GPU.  The
  * gather computes the cells whose first bin row is in the band and leaves
