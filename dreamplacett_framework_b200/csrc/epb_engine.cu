@@ -49,6 +49,9 @@ struct epb_handle {
     double* ovf_partials = nullptr;   // [2 * kOvfMaxBlocks]
     unsigned* ovf_counter = nullptr;
     unsigned* linf_bits = nullptr;
+    // whole-grid gather: CTAs resident at once (k_gather<false>, k_gather<true>),
+    // the grid of its cell-striding launch
+    unsigned gather_grid[2] = {1, 1};
     // band selection of a shard's scatter / gather (k_band_select): the cells
     // meeting the band and the cells owned by it, with the cell view the own
     // list was made from (the gather reuses it for the same cell arrays)
@@ -145,6 +148,14 @@ int make_view(epb_handle* h, const epb_cells* c, CellView& v) {
     v.b0 = c->begin0; v.n0 = n0; v.b1 = c->begin1; v.n = n0 + n1;
     v.sel = nullptr; v.sel_n = nullptr;
     return EPB_OK;
+}
+
+unsigned cell_blocks(int64_t n);
+
+// Whole-grid gather: one wave of CTAs striding over the cells (fewer when
+// there are fewer cells than threads).
+unsigned gather_blocks(const epb_handle* h, int64_t n, bool io) {
+    return std::min(cell_blocks(n), h->gather_grid[io ? 1 : 0]);
 }
 
 unsigned cell_blocks(int64_t n) {
@@ -583,6 +594,12 @@ int create_handle(const epb_config* cfg, int P, int p, epb_handle** out) {
     if (e == cudaSuccess) e = cudaMemset(h->ovf_counter, 0, sizeof(unsigned));
     if (e == cudaSuccess) e = cudaMemset(h->flags, 0, sizeof(unsigned));
     if (e == cudaSuccess) e = cudaMemset(h->energy_d, 0, sizeof(double));
+    int sms = 0, occ0 = 0, occ1 = 0;
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, h->dev);
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ0, k_gather<false>, 256, 0);
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ1, k_gather<true>, 256, 0);
+    h->gather_grid[0] = (unsigned)std::max(1, sms * occ0 * EPB_GATHER_WAVES);
+    h->gather_grid[1] = (unsigned)std::max(1, sms * occ1 * EPB_GATHER_WAVES);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) { free_all(h); delete h; return EPB_ECUDA; }
     *out = h;
@@ -672,7 +689,7 @@ int epb_backward(epb_handle* h, const epb_cells* cells, const float* grad_out, e
     DeviceGuard guard(h->dev);
     ProfCall pc(h, (cudaStream_t)stream);
     pc.begin();
-    k_gather<false><<<cell_blocks(v.n), 256, 0, (cudaStream_t)stream>>>(v, geom(h), h->fxy, nullptr, nullptr, 0, h->M, 0, 0,
+    k_gather<false><<<gather_blocks(h, v.n, false), 256, 0, (cudaStream_t)stream>>>(v, geom(h), h->fxy, nullptr, nullptr, 0, h->M, 0, 0,
                                                                grad_out, grad_x, grad_y, h->flags);
     EPB_LAUNCHED(h, "k_gather launch");
     pc.end_stage(EPB_STAGE_GATHER);
@@ -719,7 +736,7 @@ int epb_gather(epb_handle* h, const epb_cells* cells, const float* field_x, cons
     if (v.n > 0 && (!grad_x || !grad_y)) return fail(h, EPB_EINVAL, "grad_x/grad_y must be non-NULL");
     if (v.n == 0) return EPB_OK;
     DeviceGuard guard(h->dev);
-    k_gather<false><<<cell_blocks(v.n), 256, 0, (cudaStream_t)stream>>>(v, geom(h), nullptr, field_x, field_y, 0, h->M, 0, 0,
+    k_gather<false><<<gather_blocks(h, v.n, false), 256, 0, (cudaStream_t)stream>>>(v, geom(h), nullptr, field_x, field_y, 0, h->M, 0, 0,
                                                                grad_out, grad_x, grad_y, h->flags);
     EPB_LAUNCHED(h, "k_gather launch");
     return EPB_OK;
@@ -797,7 +814,7 @@ int epb_backward_host(epb_handle* h, const epb_cells* cells, const float* grad_o
     if (v.n == 0) return EPB_OK;
     ProfCall pc(h, st);
     pc.begin();
-    k_gather<true><<<cell_blocks(v.n), 256, 0, st>>>(v, geom(h), h->fxy, nullptr, nullptr, 0, h->M, 0, 0, grad_out,
+    k_gather<true><<<gather_blocks(h, v.n, true), 256, 0, st>>>(v, geom(h), h->fxy, nullptr, nullptr, 0, h->M, 0, 0, grad_out,
                                                      grad_x, grad_y, h->flags, static_cast<float*>(hgx),
                                                      static_cast<float*>(hgy));
     EPB_LAUNCHED(h, "k_gather launch");

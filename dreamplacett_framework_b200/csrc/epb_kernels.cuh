@@ -78,8 +78,11 @@ constexpr int kOyCache = 4;
 #ifndef EPB_SCATTER_MINB
 #define EPB_SCATTER_MINB 0
 #endif
+#ifndef EPB_GATHER_WAVES
+#define EPB_GATHER_WAVES 1   // whole-grid gather launch: waves of resident CTAs
+#endif
 #ifndef EPB_GATHER_MINB
-#define EPB_GATHER_MINB 6
+#define EPB_GATHER_MINB 5
 #endif
 #if EPB_SCATTER_MINB > 0
 #define EPB_SCATTER_BOUNDS __launch_bounds__(256, EPB_SCATTER_MINB)
@@ -772,11 +775,8 @@ k_gather(CellView c, GridGeom g, const float2* __restrict__ fxy,
     // whose first bin row lies in [row0, row1) are computed and written; other
     // entries of grad_x / grad_y are left as they are.
     const float gscale = grad_out ? -__ldg(grad_out) : -1.0f;
-    // cells of a selection are the band's own cells: no band test
-    const int blo = c.sel ? 0 : row0, bhi = c.sel ? g.M : row1;
-    for_each_cell(c, [&](int64_t node) {
-        Footprint f;
-        const int st = cell_footprint(c, g, node, f, blo, bhi, owned_only != 0);
+    // per-cell accumulation over the footprint and the gradient stores
+    auto finish = [&](int64_t node, int st, const Footprint& f) {
         float ax = 0.0f, ay = 0.0f, r = 0.0f;
         if (st < 0) atomicOr(flags, kFlagNonFinite);
         if (owned_only && st != 1) return;
@@ -826,6 +826,34 @@ k_gather(CellView c, GridGeom g, const float2* __restrict__ fxy,
             host_gx[node] = s * ax;
             host_gy[node] = s * ay;
         }
+    };
+    if (!c.sel && row0 == 0 && row1 >= g.M && !owned_only) {
+        // whole grid: each thread strides over cells with the next cell's inputs
+        // in flight while it reads the current cell's fields (one memory round
+        // trip per cell instead of two)
+        const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+        int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+        if (i >= c.n) return;
+        CellData cur = load_cell(c, cell_node(c, i));
+        for (;;) {
+            const int64_t inext = i + stride;
+            CellData nxt = cur;
+            if (inext < c.n) nxt = load_cell(c, cell_node(c, inext));
+            Footprint f;
+            const int st = footprint_of(c, g, cur, f);
+            finish(cell_node(c, i), st, f);
+            if (inext >= c.n) break;
+            cur = nxt;
+            i = inext;
+        }
+        return;
+    }
+    // cells of a selection are the band's own cells: no band test
+    const int blo = c.sel ? 0 : row0, bhi = c.sel ? g.M : row1;
+    for_each_cell(c, [&](int64_t node) {
+        Footprint f;
+        const int st = cell_footprint(c, g, node, f, blo, bhi, owned_only != 0);
+        finish(node, st, f);
     });
 }
 

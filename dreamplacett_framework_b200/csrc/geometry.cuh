@@ -96,6 +96,50 @@ struct Footprint {
 // On the whole grid every load is issued before any test (one memory round
 // trip per cell).  On a row band the x data is read first, so a cell of another
 // band costs three loads instead of seven; the test is uniform across the grid.
+// A cell's raw inputs (offsets and ratio as given; absent ones unused).  Kept
+// apart from the footprint arithmetic so a kernel can have the next cell's
+// loads in flight while it works on the current one.
+struct CellData {
+    float x, ox, y, oy, sx, sy, r;
+};
+
+__device__ __forceinline__ CellData load_cell(const CellView& c, int64_t node) {
+    CellData d;
+    d.x = __ldg(c.x + node);
+    d.ox = c.ox ? __ldg(c.ox + node) : 0.0f;
+    d.sx = __ldg(c.sx + node);
+    d.y = __ldg(c.y + node);
+    d.oy = c.oy ? __ldg(c.oy + node) : 0.0f;
+    d.sy = __ldg(c.sy + node);
+    d.r = c.ratio ? __ldg(c.ratio + node) : 1.0f;
+    return d;
+}
+
+// Footprint of a cell from its loaded inputs on the whole grid (no band), as
+// cell_footprint computes it with the band [0, M): -1 for non-finite inputs, 0
+// for an empty footprint, 2 for a footprint outside the grid's rows, else 1.
+__device__ __forceinline__ int footprint_of(const CellView& c, const GridGeom& g, const CellData& d, Footprint& f) {
+    const float x = c.ox ? __fadd_rn(d.x, d.ox) : d.x;
+    const float y = c.oy ? __fadd_rn(d.y, d.oy) : d.y;
+    if (!isfinite(x) || !isfinite(d.sx)) return -1;
+    bool empty = !(d.sx > 0.0f);
+    if (!empty) {
+        f.ex = __fadd_rn(x, d.sx);
+        f.kx0 = bin_floor(x, g.xl, g.bsx, g.ibsx, g.M);
+        f.kx1 = min(bin_floor(f.ex, g.xl, g.bsx, g.ibsx, g.M), g.M - 1);
+        empty = f.kx0 > f.kx1;
+        if (!empty && (f.kx1 < 0 || f.kx0 >= g.M)) return 2;
+    }
+    if (!isfinite(y) || !isfinite(d.sy) || !isfinite(d.r)) return -1;
+    if (empty || !(d.sy > 0.0f)) return 0;
+    f.ey = __fadd_rn(y, d.sy);
+    f.ky0 = bin_floor(y, g.yl, g.bsy, g.ibsy, g.N);
+    f.ky1 = min(bin_floor(f.ey, g.yl, g.bsy, g.ibsy, g.N), g.N - 1);
+    if (f.ky0 > f.ky1) return 0;
+    f.x = x; f.y = y; f.r = d.r;
+    return 1;
+}
+
 __device__ __forceinline__ int cell_footprint(const CellView& c, const GridGeom& g, int64_t node,
                                               Footprint& f, int row_lo, int row_hi, bool owner) {
     const bool banded = row_lo > 0 || row_hi < g.M;
