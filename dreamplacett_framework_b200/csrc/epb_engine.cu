@@ -469,7 +469,10 @@ int scatter_into(epb_handle* h, const CellView& v0, cudaStream_t st, long long* 
     unsigned blocks = cell_blocks(v.n);
     if (h->P > 1) {
         if (int rc = band_selection(h, v, true, st)) return rc;
-        blocks = (unsigned)((v.n + kSelChunk - 1) / kSelChunk);   // one CTA per segment
+        // a band holds about 1/P of a segment's cells: CTAs per segment so that a
+        // thread has about one cell, as in the whole-grid scatter
+        const int64_t split = std::max(1, EPB_SEL_SCATTER_SPLIT / h->P);
+        blocks = (unsigned)(((v.n + kSelChunk - 1) / kSelChunk) * split);
     }
     k_scatter<false><<<blocks, 256, 0, st>>>(v, geom(h), qscale, (unsigned long long*)grid, h->row0, h->row0 + h->RB,
                                       h->flags);

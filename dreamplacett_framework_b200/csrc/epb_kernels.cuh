@@ -78,6 +78,9 @@ constexpr int kOyCache = 4;
 #ifndef EPB_SCATTER_MINB
 #define EPB_SCATTER_MINB 0
 #endif
+#ifndef EPB_SEL_SCATTER_SPLIT
+#define EPB_SEL_SCATTER_SPLIT 8  // shard scatter: CTAs per selection segment times the shard count
+#endif
 #ifndef EPB_GATHER_WAVES
 #define EPB_GATHER_WAVES 1   // whole-grid gather launch: waves of resident CTAs
 #endif
@@ -701,7 +704,8 @@ k_row_inv(RowInvArgs a) {
 // list of the band holding row 0, which then reports their non-finite data),
 // and `own`, the cells whose first row is in [row0, row1) (the gather).  Cells
 // with non-finite x data are flagged here.  Each CTA compacts a fixed segment
-// of kSelChunk cells (no global atomics); the consumers run one CTA per segment.
+// of kSelChunk cells (no global atomics); the consumers run one or more CTAs
+// per segment.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256)
 k_band_select(CellView c, GridGeom g, int row0, int row1, int* __restrict__ meet, int* __restrict__ meet_n,
@@ -827,32 +831,20 @@ k_gather(CellView c, GridGeom g, const float2* __restrict__ fxy,
             host_gy[node] = s * ay;
         }
     };
-    if (!c.sel && row0 == 0 && row1 >= g.M && !owned_only) {
-        // whole grid: each thread strides over cells with the next cell's inputs
-        // in flight while it reads the current cell's fields (one memory round
-        // trip per cell instead of two)
-        const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-        int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-        if (i >= c.n) return;
-        CellData cur = load_cell(c, cell_node(c, i));
-        for (;;) {
-            const int64_t inext = i + stride;
-            CellData nxt = cur;
-            if (inext < c.n) nxt = load_cell(c, cell_node(c, inext));
+    if (c.sel || (row0 == 0 && row1 >= g.M)) {
+        // the whole grid, or a selection (the band's own cells, which need no band
+        // test): a footprint from loaded inputs, the next cell's loads in flight
+        // while the current cell's fields are read (one round trip per cell, not two)
+        for_each_cell_prefetched(c, [&](int64_t node, const CellData& d) {
             Footprint f;
-            const int st = footprint_of(c, g, cur, f);
-            finish(cell_node(c, i), st, f);
-            if (inext >= c.n) break;
-            cur = nxt;
-            i = inext;
-        }
+            finish(node, footprint_of(c, g, d, f), f);
+        });
         return;
     }
-    // cells of a selection are the band's own cells: no band test
-    const int blo = c.sel ? 0 : row0, bhi = c.sel ? g.M : row1;
+    // a band without a selection: every cell is tested against it
     for_each_cell(c, [&](int64_t node) {
         Footprint f;
-        const int st = cell_footprint(c, g, node, f, blo, bhi, owned_only != 0);
+        const int st = cell_footprint(c, g, node, f, row0, row1, owned_only != 0);
         finish(node, st, f);
     });
 }

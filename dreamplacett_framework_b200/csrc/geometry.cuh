@@ -46,14 +46,21 @@ __device__ __forceinline__ int64_t cell_node(const CellView& c, int64_t i) {
 }
 
 // Visit every cell of v (all cells, or the selected ones) with body(node), the
-// work spread over the grid: a grid-stride loop, or one segment per CTA.
+// work spread over the grid: a grid-stride loop, or G CTAs per segment when the
+// grid has G times as many CTAs as there are segments (else one).
 template <typename F>
 __device__ __forceinline__ void for_each_cell(const CellView& c, F&& body) {
     if (c.sel) {
+        // G consecutive CTAs share a segment when the grid has G CTAs per segment
         const int64_t nseg = (c.n + kSelChunk - 1) / kSelChunk;
-        for (int64_t s = blockIdx.x; s < nseg; s += gridDim.x) {
+        const int64_t G = gridDim.x >= nseg ? gridDim.x / nseg : 1;
+        const int64_t slots = gridDim.x / G;
+        if (blockIdx.x >= slots * G) return;
+        const int sub = (int)(blockIdx.x % G);
+        for (int64_t s = blockIdx.x / G; s < nseg; s += slots) {
             const int cnt = c.sel_n[s];
-            for (int j = threadIdx.x; j < cnt; j += blockDim.x) body(cell_node(c, c.sel[s * kSelChunk + j]));
+            for (int j = sub * (int)blockDim.x + threadIdx.x; j < cnt; j += (int)(G * blockDim.x))
+                body(cell_node(c, c.sel[s * kSelChunk + j]));
         }
     } else {
         const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -138,6 +145,52 @@ __device__ __forceinline__ int footprint_of(const CellView& c, const GridGeom& g
     if (f.ky0 > f.ky1) return 0;
     f.x = x; f.y = y; f.r = d.r;
     return 1;
+}
+
+// Visit the cells of v as for_each_cell does, calling body(node, data) with the
+// cell's loaded inputs; each thread loads its next cell's inputs before it
+// works on the current one, so that load overlaps the body's own reads.
+template <typename F>
+__device__ __forceinline__ void for_each_cell_prefetched(const CellView& c, F&& body) {
+    if (c.sel) {
+        const int64_t nseg = (c.n + kSelChunk - 1) / kSelChunk;
+        for (int64_t s = blockIdx.x; s < nseg; s += gridDim.x) {
+            const int cnt = c.sel_n[s];
+            const int* lst = c.sel + s * kSelChunk;
+            int j = threadIdx.x;
+            if (j >= cnt) continue;
+            int64_t node = cell_node(c, lst[j]);
+            CellData cur = load_cell(c, node);
+            for (;;) {
+                const int jn = j + (int)blockDim.x;
+                int64_t nnode = node;
+                CellData nxt = cur;
+                if (jn < cnt) {
+                    nnode = cell_node(c, lst[jn]);
+                    nxt = load_cell(c, nnode);
+                }
+                body(node, cur);
+                if (jn >= cnt) break;
+                j = jn;
+                node = nnode;
+                cur = nxt;
+            }
+        }
+    } else {
+        const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+        int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+        if (i >= c.n) return;
+        CellData cur = load_cell(c, cell_node(c, i));
+        for (;;) {
+            const int64_t inext = i + stride;
+            CellData nxt = cur;
+            if (inext < c.n) nxt = load_cell(c, cell_node(c, inext));
+            body(cell_node(c, i), cur);
+            if (inext >= c.n) break;
+            cur = nxt;
+            i = inext;
+        }
+    }
 }
 
 __device__ __forceinline__ int cell_footprint(const CellView& c, const GridGeom& g, int64_t node,
