@@ -18,6 +18,8 @@ import torch.multiprocessing as mp
 from dreamplacett_framework_b200 import synth
 from dreamplacett_framework_b200.engine import CellTensors
 
+from gpu_util import np_
+
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
@@ -194,3 +196,104 @@ def test_lost_rank_gives_error_not_hang(tmp_path):
         pr.kill()
     assert not alive, "a rank hung"
     assert (tmp_path / "rank0.txt").read_text().startswith("error")
+
+
+def _shard_inputs(p, device):
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(device)
+    return CellTensors(t(p.x), t(p.y), t(p.size_x_clamped), t(p.size_y_clamped), t(p.offset_x), t(p.offset_y),
+                       t(p.ratio), ranges=p.ranges)
+
+
+def _cloned(c):
+    return CellTensors(c.x.clone(), c.y.clone(), c.size_x.clone(), c.size_y.clone(), c.offset_x.clone(),
+                       c.offset_y.clone(), c.ratio.clone(), ranges=c.ranges)
+
+
+@pytest.mark.gpu
+def test_shard_gather_reuses_forward_selection(cuda_device):
+    """A shard's gather reuses the list of its own cells that its forward made
+    when it gets the same cell arrays, recomputes it for other arrays, and drops
+    it once epb_descent_step has moved the cells: every way gives the gradient
+    of a fresh selection."""
+    import ctypes
+    from dreamplacett_framework_b200 import _lib
+    from dreamplacett_framework_b200.sharded import EngineShard, halo_rows_for
+    p = synth.make_placement("c3", scale=0.1, grid=512)
+    M, N, P = p.num_bins_x, p.num_bins_y, 2
+    cells = _shard_inputs(p, cuda_device)
+    be = EngineShard(M, N, p.xl, p.yl, p.xh, p.yh, P, 0, cuda_device)
+    try:
+        RB = be.RB
+        halo = halo_rows_for(float(np.max(p.size_x_clamped)), be.bin_size_x)
+        gen = torch.Generator(device=cuda_device).manual_seed(5)
+        fxy = torch.randn((RB + halo) * N * 2, generator=gen, device=cuda_device)
+        dens = torch.empty(RB * N, device=cuda_device)
+        t1 = torch.empty(RB * N, device=cuda_device)
+        n = p.num_nodes
+
+        def gather(c):
+            gx = torch.zeros(n, device=cuda_device)
+            gy = torch.zeros(n, device=cuda_device)
+            be.gather(c, fxy, halo, None, gx, gy)
+            return gx, gy
+
+        be.rows_forward(cells, dens, t1)
+        reused = gather(cells)
+        fresh = gather(_cloned(cells))       # other pointers: a selection of its own
+        again = gather(cells)
+        for a, b, c in zip(reused, fresh, again):
+            assert torch.equal(a, b) and torch.equal(a, c)
+        # move the cells by up to 40 bins: some change band; the gather must see it
+        gx, gy = reused
+        first_row = lambda: np.floor((np_(cells.x) + np_(cells.offset_x) - p.xl) / be.bin_size_x)
+        row_before = first_row()
+        w, h = cells.size_x, cells.size_y
+        linf = torch.zeros(1, device=cuda_device)
+        st = be.lib.epb_descent_step(be._h, be._cells(cells), ctypes.c_void_p(cells.x.data_ptr()),
+                                     ctypes.c_void_p(cells.y.data_ptr()), ctypes.c_void_p(gx.data_ptr()),
+                                     ctypes.c_void_p(gy.data_ptr()), ctypes.c_void_p(w.data_ptr()),
+                                     ctypes.c_void_p(h.data_ptr()), 40.0, None,
+                                     ctypes.c_void_p(linf.data_ptr()))
+        assert st == _lib.EPB_OK
+        row_after = first_row()
+        assert np.count_nonzero((row_before < RB) & (row_after >= RB)) > 0  # cells left band 0
+        moved = gather(cells)
+        ref = gather(_cloned(cells))
+        for a, b in zip(moved, ref):
+            assert torch.equal(a, b)
+        assert not torch.equal(moved[0], reused[0])
+        assert be.error_flags() & ~0x4 == 0
+    finally:
+        be.close()
+
+
+@pytest.mark.gpu
+def test_shard_stages_reject_misaligned_buffers(cuda_device):
+    """The exchanged blocks move as float4 (the field map as float2): a
+    misaligned caller buffer is an EPB_EINVAL, before any kernel runs."""
+    from dreamplacett_framework_b200 import _lib
+    from dreamplacett_framework_b200.sharded import EngineShard
+    M = N = 64
+    be = EngineShard(M, N, 0.0, 0.0, 640.0, 640.0, 2, 0, cuda_device)
+    try:
+        f = lambda k: torch.zeros(k + 4, dtype=torch.float32, device=cuda_device)
+        t1, g, fxy = f(M * N // 2), f(_lib.COL_OUTPUTS * M * N // 2), f(M * N)
+        e = torch.zeros(1, dtype=torch.float64, device=cuda_device)
+        with pytest.raises(_lib.EpbError) as ex:
+            be.columns(t1[1:], g, True, e)
+        assert ex.value.status == _lib.EPB_EINVAL
+        with pytest.raises(_lib.EpbError) as ex:
+            be.columns(t1, g[2:], True, e)
+        assert ex.value.status == _lib.EPB_EINVAL
+        with pytest.raises(_lib.EpbError) as ex:
+            be.rows_inverse(g[1:], None, None, None, fxy)
+        assert ex.value.status == _lib.EPB_EINVAL
+        with pytest.raises(_lib.EpbError) as ex:
+            be.rows_inverse(g, None, None, None, fxy[1:])
+        assert ex.value.status == _lib.EPB_EINVAL
+        # aligned buffers pass the checks
+        be.columns(t1, g, True, e)
+        be.rows_inverse(g, None, None, None, fxy)
+        torch.cuda.synchronize()
+    finally:
+        be.close()
