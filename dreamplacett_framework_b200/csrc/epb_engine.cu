@@ -49,6 +49,7 @@ struct epb_handle {
     double* ovf_partials = nullptr;   // [2 * kOvfMaxBlocks]
     unsigned* ovf_counter = nullptr;
     unsigned* linf_bits = nullptr;
+    int sms = 1;  // streaming multiprocessors of the device
     // whole-grid gather: CTAs resident at once (k_gather<false>, k_gather<true>),
     // the grid of its cell-striding launch
     unsigned gather_grid[2] = {1, 1};
@@ -230,20 +231,20 @@ int ilog2(int v) {
 
 // Row pass over this handle's RB rows: t1 receives the blocked layout (block
 // width NB, RB*NB elements per block); for P == 1 that is plain [M][N].
-template <int L>
-int launch_row_fwd_t(epb_handle* h, bool from_fixed, const float* rho_in, float* rho_out, const DstTable& t1,
+template <int L, bool HALF>
+int launch_row_fwd_v(epb_handle* h, bool from_fixed, const float* rho_in, float* rho_out, const DstTable& t1,
                      int drow0, cudaStream_t st) {
-    using C = RowFwdCfg<L>;
+    using C = RowFwdCfg<L, HALF>;
     const unsigned blocks = (unsigned)((h->RB + C::ROWS - 1) / C::ROWS);
     const float* init = h->has_init && from_fixed ? h->init : nullptr;
     const int lnb = ilog2(h->NB);
     if (from_fixed) {
-        auto fn = k_row_fwd<L, true>;
+        auto fn = k_row_fwd<L, true, HALF>;
         if (int rc = set_smem<L>(h, (const void*)fn, C::SMEM)) return rc;
         fn<<<blocks, C::T, C::SMEM, st>>>(h->grid, nullptr, init, h->dscale, h->RB, rho_out, t1, lnb, drow0,
                                           h->twN, h->qwN, h->flags);
     } else {
-        auto fn = k_row_fwd<L, false>;
+        auto fn = k_row_fwd<L, false, HALF>;
         if (int rc = set_smem<L>(h, (const void*)fn, C::SMEM)) return rc;
         fn<<<blocks, C::T, C::SMEM, st>>>(nullptr, rho_in, nullptr, h->dscale, h->RB, rho_out, t1, lnb, drow0,
                                           h->twN, h->qwN, h->flags);
@@ -252,15 +253,31 @@ int launch_row_fwd_t(epb_handle* h, bool from_fixed, const float* rho_in, float*
     return EPB_OK;
 }
 
+// Half-size CTAs when the default launch has fewer CTAs than the GPU has SMs
+// (a shard's band of a few hundred rows, a strip of a few hundred columns).
 template <int L>
-int launch_col_t(epb_handle* h, const ColArgs& a, cudaStream_t st) {
-    using C = ColCfg<L>;
+int launch_row_fwd_t(epb_handle* h, bool from_fixed, const float* rho_in, float* rho_out, const DstTable& t1,
+                     int drow0, cudaStream_t st) {
+    if ((h->RB + RowFwdCfg<L>::ROWS - 1) / RowFwdCfg<L>::ROWS < h->sms)
+        return launch_row_fwd_v<L, true>(h, from_fixed, rho_in, rho_out, t1, drow0, st);
+    return launch_row_fwd_v<L, false>(h, from_fixed, rho_in, rho_out, t1, drow0, st);
+}
+
+template <int L, bool HALF>
+int launch_col_v(epb_handle* h, const ColArgs& a, cudaStream_t st) {
+    using C = ColCfg<L, HALF>;
     const unsigned blocks = (unsigned)((a.N + C::W - 1) / C::W);
-    auto fn = k_col<L>;
+    auto fn = k_col<L, HALF>;
     if (int rc = set_smem<L>(h, (const void*)fn, C::SMEM)) return rc;
     fn<<<blocks, C::T, C::SMEM, st>>>(a);
     EPB_LAUNCHED(h, "k_col launch");
     return EPB_OK;
+}
+
+template <int L>
+int launch_col_t(epb_handle* h, const ColArgs& a, cudaStream_t st) {
+    if ((a.N + ColCfg<L>::W - 1) / ColCfg<L>::W < h->sms) return launch_col_v<L, true>(h, a, st);
+    return launch_col_v<L, false>(h, a, st);
 }
 
 template <int L>
@@ -575,7 +592,7 @@ int create_handle(const epb_config* cfg, int P, int p, epb_handle** out) {
     if (!rc) rc = dev_alloc(h, &h->qwM, (size_t)h->M);
     if (!rc) rc = dev_alloc(h, &h->twN, (size_t)std::max(1, tw_table_size(h->N)));
     if (!rc) rc = dev_alloc(h, &h->qwN, (size_t)h->N);
-    if (!rc) rc = dev_alloc(h, &h->partials, (size_t)ncolb);
+    if (!rc) rc = dev_alloc(h, &h->partials, 2 * (size_t)ncolb);  // room for the half-size column CTAs
     if (!rc) rc = dev_alloc(h, &h->counter, 1);
     if (!rc) rc = dev_alloc(h, &h->energy_d, 1);
     if (!rc) rc = dev_alloc(h, &h->flags, 1);
@@ -599,6 +616,7 @@ int create_handle(const epb_config* cfg, int P, int p, epb_handle** out) {
     if (e == cudaSuccess) e = cudaMemset(h->energy_d, 0, sizeof(double));
     int sms = 0, occ0 = 0, occ1 = 0;
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, h->dev);
+    h->sms = std::max(1, sms);
     if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ0, k_gather<false>, 256, 0);
     if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ1, k_gather<true>, 256, 0);
     h->gather_grid[0] = (unsigned)std::max(1, sms * occ0 * EPB_GATHER_WAVES);

@@ -170,23 +170,26 @@ k_scatter(CellView c, GridGeom g, float qscale, unsigned long long* __restrict__
 #define EPB_ROWINV_MINB 3
 #endif
 #if EPB_ROWFWD_MINB > 0
-#define EPB_ROWFWD_BOUNDS(T) __launch_bounds__(T, EPB_ROWFWD_MINB)
+#define EPB_ROWFWD_BOUNDS(...) __launch_bounds__(__VA_ARGS__, EPB_ROWFWD_MINB)
 #else
-#define EPB_ROWFWD_BOUNDS(T) __launch_bounds__(T)
+#define EPB_ROWFWD_BOUNDS(...) __launch_bounds__(__VA_ARGS__)
 #endif
 
-template <int L>
+// HALF: half the sequences per CTA (at least one), for launches that would
+// otherwise leave SMs idle (a shard's few rows or columns).
+template <int L, bool HALF = false>
 struct RowFwdCfg {
     static constexpr int P = L / 16;
-    static constexpr int S = (4096 / L) > 0 ? 4096 / L : 1;
+    static constexpr int S0 = (4096 / L) > 0 ? 4096 / L : 1;
+    static constexpr int S = HALF ? (S0 / 2 > 0 ? S0 / 2 : 1) : S0;
     static constexpr int T = P * S;
     static constexpr int ROWS = 2 * S;
     static constexpr int LP = Padded<L>::value;
     static constexpr size_t SMEM = (size_t)S * LP * sizeof(float2);
 };
 
-template <int L, bool FROM_FIXED>
-__global__ void EPB_ROWFWD_BOUNDS(RowFwdCfg<L>::T)
+template <int L, bool FROM_FIXED, bool HALF = false>
+__global__ void EPB_ROWFWD_BOUNDS(RowFwdCfg<L, HALF>::T)
 k_row_fwd(long long* __restrict__ qgrid,            // FROM_FIXED: [M][L] int64 (zeroed after read)
           const float* __restrict__ rho_in,         // !FROM_FIXED: [M][L] fp32
           const float* __restrict__ init,           // nullable [M][L]
@@ -196,7 +199,7 @@ k_row_fwd(long long* __restrict__ qgrid,            // FROM_FIXED: [M][L] int64 
           int lnb, int drow0,                       // log2 block width nb; first row of this band there
           const float2* __restrict__ tw, const float2* __restrict__ qw,
           unsigned* __restrict__ flags) {
-    using C = RowFwdCfg<L>;
+    using C = RowFwdCfg<L, HALF>;
     constexpr int S = C::S, T = C::T, LP = C::LP, P = C::P;
     constexpr bool GS = GroupSync<L, S>::value;  // sequences run on their own barriers
     extern __shared__ float2 sm_rowfwd[];
@@ -314,10 +317,11 @@ k_row_fwd(long long* __restrict__ qgrid,            // FROM_FIXED: [M][L] int64 
 // ---------------------------------------------------------------------------
 // Pass 2: along x (columns).  S sequences of length L = M per CTA -> W = 2S columns.
 // ---------------------------------------------------------------------------
-template <int L>
+template <int L, bool HALF = false>
 struct ColCfg {
     static constexpr int P = L / 16;
-    static constexpr int S = (4096 / L) > 2 ? 4096 / L : 2;
+    static constexpr int S0 = (4096 / L) > 2 ? 4096 / L : 2;
+    static constexpr int S = HALF ? S0 / 2 : S0;
     static constexpr int T = P * S;
     static constexpr int W = 2 * S;
     static constexpr int LP = Padded<L>::value;
@@ -368,10 +372,10 @@ __device__ __forceinline__ float2 idct_pre(float an0, float am0, float an1, floa
     return make_float2(va.x - vb.y, va.y + vb.x);
 }
 
-template <int L>
-__global__ void __launch_bounds__(ColCfg<L>::T, ColCfg<L>::MINB)
+template <int L, bool HALF = false>
+__global__ void __launch_bounds__(ColCfg<L, HALF>::T, ColCfg<L, HALF>::MINB)
 k_col(const __grid_constant__ ColArgs a) {
-    using C = ColCfg<L>;
+    using C = ColCfg<L, HALF>;
     constexpr int S = C::S, W = C::W, T = C::T, LP = C::LP, P = C::P;
     // CTA-wide phases: the strip's float4 loads and stores span both sequences of a CTA
     constexpr bool GS = false;
@@ -387,18 +391,26 @@ k_col(const __grid_constant__ ColArgs a) {
     const int grp = threadIdx.x / P;
     const int lane = threadIdx.x % P;
 
-    // ---- load T1 strip [L rows][W cols], Makhoul reorder along rows ----
+    // ---- load T1 strip [L rows][W cols], Makhoul reorder along rows; four columns
+    //      (two sequences) per load, or two (one sequence) when W == 2 ----
+    constexpr int VW = W >= 4 ? 4 : 2;
 #pragma unroll 4
-    for (int e = threadIdx.x; e < L * (W / 4); e += T) {
-        const int m = e / (W / 4), q4 = e % (W / 4);
-        const int col = c0 + 4 * q4;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        // read once per launch: keep it out of L1, which serves the twiddle table
-        if (col < N) v = __ldcg(reinterpret_cast<const float4*>(a.t1 + (int64_t)m * N + col));
+    for (int e = threadIdx.x; e < L * (W / VW); e += T) {
+        const int m = e / (W / VW), qv = e % (W / VW);
+        const int col = c0 + VW * qv;
         const int pos = pidx(makhoul_pos(m, L));
-        const int s0 = 2 * q4;  // columns 4q4, 4q4+1 -> seq 2q4 ; 4q4+2, 4q4+3 -> seq 2q4+1
-        buf[s0 * LP + pos] = make_float2(v.x, v.y);
-        buf[(s0 + 1) * LP + pos] = make_float2(v.z, v.w);
+        // read once per launch: keep it out of L1, which serves the twiddle table
+        if constexpr (VW == 4) {
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (col < N) v = __ldcg(reinterpret_cast<const float4*>(a.t1 + (int64_t)m * N + col));
+            const int s0 = 2 * qv;  // columns 4qv, 4qv+1 -> seq 2qv ; 4qv+2, 4qv+3 -> seq 2qv+1
+            buf[s0 * LP + pos] = make_float2(v.x, v.y);
+            buf[(s0 + 1) * LP + pos] = make_float2(v.z, v.w);
+        } else {
+            float2 v = make_float2(0.f, 0.f);
+            if (col < N) v = __ldcg(reinterpret_cast<const float2*>(a.t1 + (int64_t)m * N + col));
+            buf[qv * LP + pos] = v;
+        }
     }
     seq_sync<P, GS>(grp);
     fft_seq<L, false, GS>(buf + grp * LP, lane, a.tw, true, grp);
@@ -519,20 +531,30 @@ k_col(const __grid_constant__ ColArgs a) {
     fft_seq<L, true, GS>(buf + (S + grp) * LP, lane, a.tw, true, grp);
     const int rbm = (1 << a.lrb) - 1;
 #pragma unroll 4
-    for (int e = threadIdx.x; e < L * (W / 4); e += T) {
-        const int k = e / (W / 4), q4 = e % (W / 4);
-        const int col = c0 + 4 * q4;
+    for (int e = threadIdx.x; e < L * (W / VW); e += T) {
+        const int k = e / (W / VW), qv = e % (W / VW);
+        const int col = c0 + VW * qv;
         const int src = pidx(makhoul_pos(k, L));
-        // columns 4q4 .. 4q4+3: pairs 2q4 and 2q4+1, outputs 0 and 1
-        float2 g0 = buf[(2 * q4) * LP + src], g1 = buf[(2 * q4 + 1) * LP + src];
-        const float2 p0 = buf[(S + 2 * q4) * LP + src], p1 = buf[(S + 2 * q4 + 1) * LP + src];
-        // output 0: the IDXST, the IDCT of the reversed input with odd outputs negated
-        if (k & 1) { g0.x = -g0.x; g0.y = -g0.y; g1.x = -g1.x; g1.y = -g1.y; }
-        if (col < N) {
-            float* dst = a.g.p[k >> a.lrb] + ((int64_t)(col >> a.lsw) << (a.lrb + a.lsw)) +
-                         ((int64_t)(k & rbm) << a.lsw) + (col & ((1 << a.lsw) - 1));
-            *reinterpret_cast<float4*>(dst) = make_float4(g0.x, g0.y, g1.x, g1.y);
-            *reinterpret_cast<float4*>(dst + a.ostride) = make_float4(p0.x, p0.y, p1.x, p1.y);
+        float* dst = a.g.p[k >> a.lrb] + ((int64_t)(col >> a.lsw) << (a.lrb + a.lsw)) +
+                     ((int64_t)(k & rbm) << a.lsw) + (col & ((1 << a.lsw) - 1));
+        if constexpr (VW == 4) {
+            // columns 4qv .. 4qv+3: pairs 2qv and 2qv+1, outputs 0 and 1
+            float2 g0 = buf[(2 * qv) * LP + src], g1 = buf[(2 * qv + 1) * LP + src];
+            const float2 p0 = buf[(S + 2 * qv) * LP + src], p1 = buf[(S + 2 * qv + 1) * LP + src];
+            // output 0: the IDXST, the IDCT of the reversed input with odd outputs negated
+            if (k & 1) { g0.x = -g0.x; g0.y = -g0.y; g1.x = -g1.x; g1.y = -g1.y; }
+            if (col < N) {
+                *reinterpret_cast<float4*>(dst) = make_float4(g0.x, g0.y, g1.x, g1.y);
+                *reinterpret_cast<float4*>(dst + a.ostride) = make_float4(p0.x, p0.y, p1.x, p1.y);
+            }
+        } else {
+            float2 g0 = buf[qv * LP + src];
+            const float2 p0 = buf[(S + qv) * LP + src];
+            if (k & 1) { g0.x = -g0.x; g0.y = -g0.y; }
+            if (col < N) {
+                *reinterpret_cast<float2*>(dst) = g0;
+                *reinterpret_cast<float2*>(dst + a.ostride) = p0;
+            }
         }
     }
 }
