@@ -97,6 +97,44 @@ def algorithmic_bytes(stage, n_cells, bins):
     return per_cell * n_cells + per_bin * bins
 
 
+def wirelength_item(p, dev, flush, peak, K=200, W=5):
+    """The WA wirelength + HPWL + gradient (epb_wirelength) on a seeded synthetic
+    netlist over the workload's movable cells (one net per movable cell,
+    ISPD-2005-like degrees), timed with CUDA events per call, L2 flushed before
+    each call."""
+    import numpy as np
+    import torch
+    from dreamplacett_framework_b200.wirelength import Netlist, WirelengthOp, synthetic_netlist
+    arr = synthetic_netlist(p.size_x, p.size_y, np.arange(p.num_movable), p.num_nodes, seed=0)
+    op = WirelengthOp(Netlist(arr, dev))
+    x = torch.from_numpy(p.x).to(dev)
+    y = torch.from_numpy(p.y).to(dev)
+    gamma = 4.0 * p.bin_size_x
+    for _ in range(W):
+        op(x, y, gamma)
+    torch.cuda.synchronize(dev)
+    st = torch.cuda.current_stream(dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    for i in range(K):
+        flush.zero_()
+        ev[i][0].record(st)
+        r = op(x, y, gamma)
+        ev[i][1].record(st)
+    torch.cuda.synchronize(dev)
+    us = 1000.0 * sum(a.elapsed_time(b) for a, b in ev) / K
+    E, P, V = arr.num_nets, arr.num_pins, arr.num_nodes
+    # per pin: net_pins, pin_node, 2 offsets, node x and y, pin gradient written and read back,
+    # node_pins; per net: net_start, weight; per node: node_pin_start, 2 gradients
+    nbytes = 40 * P + 8 * E + 12 * V
+    return {"workload": f"{E} nets, {P} pins over {p.num_movable} movable cells (seeded synthetic netlist); "
+                        "WA wirelength + HPWL (fp64 totals) and the WA gradient of every node",
+            "us_per_call": us, "calls": K, "algorithmic_bytes": nbytes, "gbs": nbytes / us / 1e3,
+            "frac": nbytes / us / 1e3 / peak,
+            "wirelength": float(r["wirelength"].item()), "hpwl": float(r["hpwl"].item()),
+            "gpu_launches_per_call": 3,
+            "error_flags": op.error_flags()}
+
+
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -645,6 +683,8 @@ def main():
                 "ms_per_step": r5["ms"] / 200, "steps_per_s": 200 * 1000.0 / r5["ms"],
                 "overflow_first": float(r5["overflow"][0]), "overflow_final": float(r5["overflow"][-1]),
                 "max_density_final": float(r5["max_density"][-1]), "error_flags": r5["flags"]}
+        if world == 1 and not args.no_loop:
+            line["wirelength"] = wirelength_item(p, dev, flush, peak)
         if world == 1 and not args.no_cpu_baseline:
             nthreads = os.cpu_count() or 1
             cstep = cpu_step_factory(p, nthreads)

@@ -38,6 +38,7 @@ EXPORTS = (
     "epb_shard_backward_peer", "epb_shard_wait_test",
     "epb_overflow", "epb_descent_step", "epb_forward_overflow",
     "epb_forward_host", "epb_backward_host",
+    "epb_wirelength_scratch_bytes", "epb_wirelength",
 )
 
 # Largest grid (M*N bins) epb_density_noalloc accepts (EPB_NOALLOC_MAX_BINS).
@@ -65,6 +66,16 @@ class EpbCells(ctypes.Structure):
         ("ratio", ctypes.c_void_p),
         ("begin0", ctypes.c_int64), ("end0", ctypes.c_int64),
         ("begin1", ctypes.c_int64), ("end1", ctypes.c_int64),
+    ]
+
+
+class EpbNetlist(ctypes.Structure):
+    _fields_ = [
+        ("net_start", ctypes.c_void_p), ("net_pins", ctypes.c_void_p), ("pin_node", ctypes.c_void_p),
+        ("pin_offset_x", ctypes.c_void_p), ("pin_offset_y", ctypes.c_void_p), ("net_weight", ctypes.c_void_p),
+        ("node_pin_start", ctypes.c_void_p), ("node_pins", ctypes.c_void_p),
+        ("num_nets", ctypes.c_int32), ("num_pins", ctypes.c_int32), ("num_nodes", ctypes.c_int32),
+        ("ignore_net_degree", ctypes.c_int32), ("device", ctypes.c_int32),
     ]
 
 
@@ -125,6 +136,10 @@ def load():
     L.epb_forward_overflow.argtypes = [vp, cp, ctypes.c_float, vp, vp, vp, vp, vp, vp, vp]
     L.epb_forward_host.argtypes = [vp, cp, vp, vp, vp, vp, vp, vp, vp, vp]
     L.epb_backward_host.argtypes = [vp, cp, vp, vp, vp, vp, vp, vp]
+    L.epb_wirelength_scratch_bytes.argtypes = [i32]
+    L.epb_wirelength_scratch_bytes.restype = ctypes.c_size_t
+    L.epb_wirelength.argtypes = [ctypes.POINTER(EpbNetlist), vp, vp, ctypes.c_float, vp, vp, ctypes.c_size_t, vp,
+                                 vp, vp, vp, ctypes.c_char_p, i32]
     for name in EXPORTS:
         if name not in ("epb_version", "epb_status_string", "epb_last_error"):
             getattr(L, name).restype = ctypes.c_int

@@ -17,6 +17,7 @@
 
 #include "../../include/epb.h"
 #include "epb_kernels.cuh"
+#include "wirelength.cuh"
 #include "placement_kernels.cuh"
 
 using namespace epb;
@@ -1375,5 +1376,66 @@ extern "C" int epb_density_noalloc(const epb_config* cfg, const epb_cells* cells
     k_fixed_to_density<<<(unsigned)blocks, 256, 0, st>>>(grid, init_norm, dscale, nbins, density);
     e = cudaGetLastError();
     if (e != cudaSuccess) return noalloc_fail(err, err_len, EPB_ECUDA, std::string("k_fixed_to_density: ") + cudaGetErrorString(e));
+    return EPB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Wirelength (allocation-free; csrc/wirelength.cuh)
+// ---------------------------------------------------------------------------
+extern "C" size_t epb_wirelength_scratch_bytes(int32_t num_pins) {
+    return kWlPinGradOffset + 2 * sizeof(float2) * (size_t)std::max<int32_t>(num_pins, 0);
+}
+
+extern "C" int epb_wirelength(const epb_netlist* nl, const float* x, const float* y, float gamma, epb_stream stream,
+                              void* scratch, size_t scratch_bytes, double* out, float* grad_x, float* grad_y,
+                              uint32_t* flags, char* err, int32_t err_len) {
+    if (!nl || !out || !scratch) return noalloc_fail(err, err_len, EPB_EINVAL, "nl, out and scratch must be non-NULL");
+    if (nl->num_nets < 0 || nl->num_pins < 0 || nl->num_nodes < 0)
+        return noalloc_fail(err, err_len, EPB_EINVAL, "netlist counts must be >= 0");
+    if (!nl->net_start || (nl->num_pins > 0 && (!nl->net_pins || !nl->pin_node || !nl->pin_offset_x ||
+                                                 !nl->pin_offset_y)))
+        return noalloc_fail(err, err_len, EPB_EINVAL, "net_start, net_pins, pin_node and pin offsets must be non-NULL");
+    const bool want_grad = grad_x || grad_y;
+    if (want_grad && (!nl->node_pin_start || (nl->num_pins > 0 && !nl->node_pins)))
+        return noalloc_fail(err, err_len, EPB_EINVAL, "a gradient needs node_pin_start and node_pins");
+    if (nl->num_nodes > 0 && nl->num_pins > 0 && (!x || !y))
+        return noalloc_fail(err, err_len, EPB_EINVAL, "x and y must be non-NULL");
+    if (!std::isfinite(gamma) || !(gamma > 0.0f)) return noalloc_fail(err, err_len, EPB_EINVAL, "gamma must be finite and > 0");
+    if (scratch_bytes < epb_wirelength_scratch_bytes(nl->num_pins) || (reinterpret_cast<uintptr_t>(scratch) & 15))
+        return noalloc_fail(err, err_len, EPB_EINVAL, "scratch must be 16-byte aligned and epb_wirelength_scratch_bytes long");
+    DeviceGuard guard(nl->device);
+    if (!guard.ok) return noalloc_fail(err, err_len, EPB_ECUDA, "cudaSetDevice failed");
+    cudaStream_t st = (cudaStream_t)stream;
+    NetlistView v;
+    v.net_start = nl->net_start; v.net_pins = nl->net_pins; v.pin_node = nl->pin_node;
+    v.pin_ox = nl->pin_offset_x; v.pin_oy = nl->pin_offset_y; v.net_weight = nl->net_weight;
+    v.node_pin_start = nl->node_pin_start; v.node_pins = nl->node_pins;
+    v.E = nl->num_nets; v.P = nl->num_pins; v.V = nl->num_nodes; v.ignore_degree = nl->ignore_net_degree;
+    char* base = static_cast<char*>(scratch);
+    unsigned* counter = reinterpret_cast<unsigned*>(base);
+    double* partials = reinterpret_cast<double*>(base + kWlPartialsOffset);
+    float2* pin_grad = reinterpret_cast<float2*>(base + kWlPinGradOffset);
+    float2* slot_pos = pin_grad + v.P;
+    cudaError_t e = cudaMemsetAsync(counter, 0, sizeof(unsigned), st);
+    if (e != cudaSuccess) return noalloc_fail(err, err_len, EPB_ECUDA, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
+    // nets of more than kWlWarpDegree pins first, a warp each (a block scans 256 nets per round);
+    // then the rest, a thread each, whose last block adds up both passes' block partials
+    const int nets_blocks = (int)std::max<int64_t>(((int64_t)v.E + kWlThreads - 1) / kWlThreads, 1);
+    const int bb = std::min(nets_blocks, kWlBigBlocks);
+    double* big_partials = partials + 2 * kWlMaxBlocks;
+    k_wa_big_nets<<<bb, kWlThreads, 0, st>>>(v, x, y, 1.0f / gamma, pin_grad, slot_pos, big_partials, flags);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return noalloc_fail(err, err_len, EPB_ECUDA, std::string("k_wa_big_nets: ") + cudaGetErrorString(e));
+    const int nb = std::min(nets_blocks, kWlMaxBlocks);
+    k_wa_nets<<<nb, kWlThreads, 0, st>>>(v, x, y, 1.0f / gamma, pin_grad, slot_pos, partials, big_partials, bb,
+                                         counter, out, flags);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return noalloc_fail(err, err_len, EPB_ECUDA, std::string("k_wa_nets: ") + cudaGetErrorString(e));
+    if (want_grad && v.V > 0) {
+        const int gb = (int)std::min<int64_t>(((int64_t)v.V + kWlThreads - 1) / kWlThreads, 4096);
+        k_wa_nodes<<<gb, kWlThreads, 0, st>>>(v, pin_grad, grad_x, grad_y, flags);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return noalloc_fail(err, err_len, EPB_ECUDA, std::string("k_wa_nodes: ") + cudaGetErrorString(e));
+    }
     return EPB_OK;
 }

@@ -49,6 +49,7 @@
 #ifndef EPB_H
 #define EPB_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -339,6 +340,63 @@ int epb_profile_stop(epb_handle* h, double* stage_ms, int32_t* stage_launches);
 #define EPB_NOALLOC_MAX_BINS (1024 * 1024)
 int epb_density_noalloc(const epb_config* cfg, const epb_cells* cells, const float* init_norm,
                         epb_stream stream, float* density, char* err, int32_t err_len);
+
+/* ---- Wirelength of the placement objective --------------------------------
+ * The other half of the objective DREAMPlace minimises around the electric
+ * potential: the weighted-average (WA) wirelength with its gradient, and the
+ * HPWL that EvalMetrics reports.  In the reference both come from DREAMPlace
+ * (absent from the reference tree): benchmarks/configs/adaptec1_2048.json
+ * selects "wirelength": "weighted_average", gamma 4.0, ignore_net_degree 100,
+ * and integration/run_dreamplace.py:315-370 reads hpwl (and overflow, see
+ * epb_overflow) every iteration.  These entry points replace those ops on the
+ * device.
+ *
+ * The netlist uses DREAMPlace's flat maps, as device int32 / fp32 arrays:
+ *   net_start[E+1], net_pins[P]   pins of net e: net_pins[net_start[e] .. net_start[e+1])
+ *                                 (netpin_start / flat_netpin); every pin listed once
+ *   pin_node[P]                   pin2node_map
+ *   pin_offset_x/y[P]             pin offset from the node's lower-left corner
+ *   net_weight[E]                 nullable (1)
+ *   node_pin_start[V+1], node_pins[P]  pins of node v, in increasing pin order
+ *                                 (flat_node2pin_start_map / flat_node2pin_map)
+ *   ignore_net_degree             nets with more pins are left out of the WA
+ *                                 wirelength and its gradient, not of the HPWL
+ * Per net and axis, with pin coordinates v (node corner + offset, fp32):
+ *   WA = sum v e^(v/g) / sum e^(v/g) - sum v e^(-v/g) / sum e^(-v/g), HPWL = max v - min v,
+ * both times the net weight; nets with fewer than 2 pins contribute nothing. */
+typedef struct {
+    const int32_t* net_start;
+    const int32_t* net_pins;
+    const int32_t* pin_node;
+    const float* pin_offset_x;
+    const float* pin_offset_y;
+    const float* net_weight;      /* nullable */
+    const int32_t* node_pin_start;
+    const int32_t* node_pins;
+    int32_t num_nets, num_pins, num_nodes;
+    int32_t ignore_net_degree;
+    int32_t device;               /* CUDA device of the arrays */
+} epb_netlist;
+
+#define EPB_FLAG_BAD_INDEX 0x10u  /* a netlist index was out of range; that entry was skipped */
+
+/* Bytes of device scratch one epb_wirelength call needs (16-byte aligned). */
+size_t epb_wirelength_scratch_bytes(int32_t num_pins);
+
+/* WA wirelength and HPWL of the netlist at node positions x[V], y[V]
+ * (lower-left corners), gamma > 0 in layout units (DREAMPlace derives it from
+ * params.gamma, the bin size and the overflow).  out: device double[2] =
+ * {WA, HPWL}; grad_x/grad_y: nullable device float[V], the WA gradient of
+ * every node (0 for nodes without pins).  Allocation-free: scratch is the
+ * caller's, at least epb_wirelength_scratch_bytes(num_pins); calls sharing
+ * one scratch must not overlap on the GPU.  flags: nullable device uint32,
+ * EPB_FLAG_BAD_INDEX / EPB_FLAG_NONFINITE_CELL are OR-ed in (a net with a bad
+ * index or a non-finite pin is skipped).  Deterministic: the same inputs give
+ * the same bits.  err[err_len] (nullable) receives the message of an
+ * EPB_EINVAL. */
+int epb_wirelength(const epb_netlist* nl, const float* x, const float* y, float gamma, epb_stream stream,
+                   void* scratch, size_t scratch_bytes, double* out, float* grad_x, float* grad_y,
+                   uint32_t* flags, char* err, int32_t err_len);
 
 #ifdef __cplusplus
 }
