@@ -14,7 +14,11 @@ files are available:
 * `.pl`    "name x y : orient [/FIXED | /FIXED_NI]"   (lower-left corners)
 * `.scl`   CoreRow blocks (Coordinate, Height, Sitewidth, Sitespacing,
            SubrowOrigin, NumSites)
-* `.nets`  NetDegree blocks; only the net and pin counts are kept.
+* `.nets`  NetDegree blocks: "NetDegree : k [name]", then k lines
+           "node I|O|B [: dx dy]" with the pin offset from the node's centre.
+           `read_aux` keeps the counts; `netlist_for_placement` reads the pins
+           into the wirelength op's input (offsets from the lower-left corner,
+           w/2 + dx and h/2 + dy, as DREAMPlace stores them).
 
 Layout follows DREAMPlace's node order [movable | terminals | terminal_NI |
 fillers]: `num_terminals` covers both fixed kinds, and only `terminal` nodes
@@ -168,6 +172,39 @@ def _read_nets(path):
     return nets, pins
 
 
+def _read_net_pins(path, index):
+    """(net_start, pin_node in file order, dx, dy from the node centre)."""
+    starts = [0]
+    nodes: List[int] = []
+    dxs: List[float] = []
+    dys: List[float] = []
+    expect = 0
+    for line in _lines(path):
+        if line.startswith("NetDegree"):
+            if expect:
+                raise ValueError(f"{path}: a net ended {expect} pins early")
+            expect = int(line.split(":", 1)[1].split()[0])
+            starts.append(starts[-1] + expect)
+            continue
+        if line.startswith("Num"):
+            continue
+        if expect <= 0:
+            raise ValueError(f"{path}: pin line outside a net: {line!r}")
+        head, _, off = line.partition(":")
+        name = head.split()[0]
+        if name not in index:
+            raise ValueError(f"{path}: unknown node {name!r}")
+        nodes.append(index[name])
+        o = off.split()
+        dxs.append(float(o[0]) if len(o) > 0 else 0.0)
+        dys.append(float(o[1]) if len(o) > 1 else 0.0)
+        expect -= 1
+    if expect:
+        raise ValueError(f"{path}: the last net ended {expect} pins early")
+    return (np.asarray(starts, np.int64), np.asarray(nodes, np.int64), np.asarray(dxs, np.float64),
+            np.asarray(dys, np.float64))
+
+
 def read_aux(aux_path: str) -> Design:
     files = _aux_files(aux_path)
     names, w, h, kind = _read_nodes(files["nodes"])
@@ -179,6 +216,32 @@ def read_aux(aux_path: str) -> Design:
         nets, pins = _read_nets(files["nets"])
     name = os.path.splitext(os.path.basename(aux_path))[0]
     return Design(name, names, w, h, kind, x, y, rows, nets, pins)
+
+
+def placement_order(d: Design) -> np.ndarray:
+    """File index of each node in DREAMPlace's order [movable | terminals | terminal_NI]."""
+    return np.concatenate([np.flatnonzero(d.kind == 0), np.flatnonzero(d.kind == 1), np.flatnonzero(d.kind == 2)])
+
+
+def netlist_for_placement(aux_path: str, p: Placement):
+    """The design's nets as a wirelength.NetlistArrays over the nodes of
+    `p = to_placement(read_aux(aux_path), ...)`: pins in file order, pin_node in
+    the placement's node order, offsets from the node's lower-left corner."""
+    from .wirelength import NetlistArrays
+    files = _aux_files(aux_path)
+    names, w, h, kind = _read_nodes(files["nodes"])
+    d = Design(os.path.splitext(os.path.basename(aux_path))[0], names, w, h, kind, np.zeros(len(names)),
+               np.zeros(len(names)), [], 0, 0)
+    order = placement_order(d)
+    to_place = np.empty(len(order), np.int64)
+    to_place[order] = np.arange(len(order))
+    starts, nodes, dx, dy = _read_net_pins(files["nets"], {n: i for i, n in enumerate(names)})
+    pin_node = to_place[nodes]
+    ox = (np.float32(0.5) * p.size_x[pin_node] + dx.astype(np.float32)).astype(np.float32)
+    oy = (np.float32(0.5) * p.size_y[pin_node] + dy.astype(np.float32)).astype(np.float32)
+    P = len(pin_node)
+    return NetlistArrays(starts.astype(np.int32), np.arange(P, dtype=np.int32), pin_node.astype(np.int32), ox, oy,
+                         p.num_nodes)
 
 
 def filler_plan(d: Design, target_density: float) -> Tuple[int, float, float]:
@@ -210,7 +273,7 @@ def to_placement(d: Design, num_bins_x: int, num_bins_y: int, target_density: fl
     at the die centre plus N(0, 0.001 * die size) noise (DREAMPlace's
     random_center_init_flag)."""
     rng = np.random.default_rng(seed)
-    order = np.concatenate([np.flatnonzero(d.kind == 0), np.flatnonzero(d.kind == 1), np.flatnonzero(d.kind == 2)])
+    order = placement_order(d)
     w, h, x, y = (a[order].astype(np.float64) for a in (d.width, d.height, d.x, d.y))
     n_mov = int(np.sum(d.kind == 0))
     n_term = int(np.sum(d.kind == 1))
@@ -276,11 +339,12 @@ def placement_from_config(path: str) -> Placement:
                         c["random_seed"], "center" if c["random_center_init"] else "pl")
 
 
-def write_bookshelf(p: Placement, directory: str, name: Optional[str] = None) -> str:
+def write_bookshelf(p: Placement, directory: str, name: Optional[str] = None, netlist=None) -> str:
     """Write a Placement's movable cells and terminals as a bookshelf design
     (fillers are not written: a reader re-creates them); rows of height
-    `row_height` = the most common movable height cover the die.  Returns the
-    .aux path."""
+    `row_height` = the most common movable height cover the die.  `netlist`
+    (a wirelength.NetlistArrays over p's nodes, optional) is written to the
+    .nets file with offsets from the node centres.  Returns the .aux path."""
     name = name or p.name
     os.makedirs(directory, exist_ok=True)
     n_real = p.num_movable + p.num_terminals
@@ -311,7 +375,20 @@ def write_bookshelf(p: Placement, directory: str, name: Optional[str] = None) ->
             f.write(f"  SubrowOrigin  :    {p.xl!r}\tNumSites  :  {int(round(p.xh - p.xl))}\n")
             f.write("End\n")
     with open(os.path.join(directory, name + ".nets"), "w") as f:
-        f.write("UCLA nets 1.0\n\nNumNets : 0\nNumPins : 0\n")
+        if netlist is None:
+            f.write("UCLA nets 1.0\n\nNumNets : 0\nNumPins : 0\n")
+        else:
+            if np.any(netlist.pin_node >= n_real):
+                raise ValueError("a pin on a filler cannot be written")
+            f.write(f"UCLA nets 1.0\n\nNumNets : {netlist.num_nets}\nNumPins : {netlist.num_pins}\n\n")
+            for e in range(netlist.num_nets):
+                pins = netlist.net_pins[netlist.net_start[e]:netlist.net_start[e + 1]]
+                f.write(f"NetDegree : {len(pins)}   n{e}\n")
+                for q in pins:
+                    v = int(netlist.pin_node[q])
+                    dx = float(netlist.pin_offset_x[q]) - 0.5 * float(p.size_x[v])
+                    dy = float(netlist.pin_offset_y[q]) - 0.5 * float(p.size_y[v])
+                    f.write(f"\t{names[v]}  B : {dx!r} {dy!r}\n")
     aux = os.path.join(directory, name + ".aux")
     with open(aux, "w") as f:
         f.write(f"RowBasedPlacement : {name}.nodes {name}.nets {name}.wts {name}.pl {name}.scl\n")

@@ -90,6 +90,49 @@ def test_tiny_design_known_answers(tmp_path):
     assert np.all(p.x[5:] >= 0) and np.all(p.x[5:] + 5.0 <= 40.0 + 1e-9)
 
 
+def test_tiny_netlist_offsets(tmp_path):
+    """Pins in file order, nodes in DREAMPlace's order, offsets from the lower-left
+    corner (w/2 + dx, h/2 + dy)."""
+    aux = _write_tiny(tmp_path)
+    (tmp_path / "t.nets").write_text(TINY["t.nets"].replace("  c I : 0 0", "  c I : 1.5 -2")
+                                     .replace("  m O : 0 0", "  m O"))
+    p = bookshelf.to_placement(bookshelf.read_aux(aux), 16, 16, enable_fillers=False)
+    nl = bookshelf.netlist_for_placement(aux, p)
+    nl.validate()
+    np.testing.assert_array_equal(nl.net_start, [0, 3, 5])
+    # order [a, b, c | m | p] -> a=0, b=1, c=2, m=3
+    np.testing.assert_array_equal(nl.pin_node, [0, 1, 2, 0, 3])
+    np.testing.assert_array_equal(nl.pin_offset_x, np.array([2, 3, 4 + 1.5, 2, 10], np.float32))
+    np.testing.assert_array_equal(nl.pin_offset_y, np.array([5, 5, 5 - 2, 5, 10], np.float32))
+    assert nl.num_nodes == p.num_nodes
+
+
+def test_netlist_round_trip(tmp_path):
+    import sys
+    from dreamplacett_framework_b200.wirelength import synthetic_netlist
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle"))
+    import wirelength as wlo
+    p = synth.make_placement("c1", scale=0.01)
+    n_real = p.num_movable + p.num_terminals
+    arr = synthetic_netlist(p.size_x, p.size_y, np.arange(n_real), p.num_nodes, seed=5)
+    aux = bookshelf.write_bookshelf(p, str(tmp_path), "nl", netlist=arr)
+    d = bookshelf.read_aux(aux)
+    assert (d.num_nets, d.num_pins) == (arr.num_nets, arr.num_pins)
+    q = bookshelf.to_placement(d, p.num_bins_x, p.num_bins_y, enable_fillers=False)
+    got = bookshelf.netlist_for_placement(aux, q)
+    got.validate()
+    np.testing.assert_array_equal(got.net_start, arr.net_start)
+    np.testing.assert_array_equal(got.pin_node, arr.pin_node[arr.net_pins])
+    np.testing.assert_allclose(got.pin_offset_x, arr.pin_offset_x[arr.net_pins], rtol=0, atol=1e-4)
+    np.testing.assert_allclose(got.pin_offset_y, arr.pin_offset_y[arr.net_pins], rtol=0, atol=1e-4)
+    # the same design: the same HPWL (unit weights on both sides)
+    a = wlo.wirelength(p.x, p.y, arr.net_start, arr.net_pins, arr.pin_node, arr.pin_offset_x, arr.pin_offset_y,
+                       4.0, p.num_nodes)
+    b = wlo.wirelength(q.x, q.y, got.net_start, got.net_pins, got.pin_node, got.pin_offset_x, got.pin_offset_y,
+                       4.0, q.num_nodes)
+    assert b[1] == pytest.approx(a[1], rel=1e-6) and b[0] == pytest.approx(a[0], rel=1e-6)
+
+
 def test_round_trip_of_synthetic_design(tmp_path):
     p = synth.make_placement("c3", scale=0.01)
     aux = bookshelf.write_bookshelf(p, str(tmp_path), "c3s")
