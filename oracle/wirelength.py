@@ -1,7 +1,7 @@
 """CPU oracle for the placement loop's wirelength terms.
 
-TEST INFRASTRUCTURE ONLY.  Imported by tests/ (as the checker) and by bench.py
-(to build inputs).  The product package never imports it.
+TEST INFRASTRUCTURE ONLY.  Imported by tests/, as the checker.  The product
+package never imports it.
 
 The reference hands these terms to DREAMPlace, which is absent from the
 reference tree (an un-vendored submodule, README.md:54-59).  What the
