@@ -63,11 +63,14 @@ class NetlistArrays:
             raise ValueError("net_weight must have num_nets entries")
 
 
-def synthetic_netlist(size_x, size_y, nodes, num_nodes, seed=0, nets_per_node=1.0, max_degree=400):
+def synthetic_netlist(size_x, size_y, nodes, num_nodes, seed=0, nets_per_node=1.0, max_degree=400,
+                      shuffle_pins=False):
     """Seeded nets over the given nodes, with degrees shaped like the ISPD-2005
     designs (mostly 2 and 3 pins, a tail past 100) and pin offsets inside each
     node's original outline.  A stand-in for the benchmark netlists, which are
-    not available here."""
+    not available here.  Pins are numbered net by net, as a bookshelf reader
+    numbers them while it reads the .nets file (net_pins is then 0..P-1);
+    shuffle_pins numbers them in a random order instead."""
     rng = np.random.default_rng(seed)
     nodes = np.asarray(nodes, np.int64)
     E = max(1, int(round(len(nodes) * nets_per_node)))
@@ -82,7 +85,7 @@ def synthetic_netlist(size_x, size_y, nodes, num_nodes, seed=0, nets_per_node=1.
     sy = np.asarray(size_y, np.float32)[pin_node]
     ox = (rng.random(P, dtype=np.float32) * sx).astype(np.float32)
     oy = (rng.random(P, dtype=np.float32) * sy).astype(np.float32)
-    net_pins = rng.permutation(P).astype(np.int32)   # pin ids in an order of their own, as in a real netlist
+    net_pins = (rng.permutation(P) if shuffle_pins else np.arange(P)).astype(np.int32)
     # pin_node / offsets are indexed by pin id
     pn = np.empty(P, np.int32)
     pn[net_pins] = pin_node

@@ -99,10 +99,12 @@ def test_degree_cap_and_weights():
     np.testing.assert_allclose(t[2], 2 * full[2], rtol=1e-12, atol=1e-15)
 
 
-def test_synthetic_netlist_shape():
+@pytest.mark.parametrize("shuffle", [False, True])
+def test_synthetic_netlist_shape(shuffle):
     p = synth.make_placement("c1", scale=0.05)
-    arr = synthetic_netlist(p.size_x, p.size_y, np.arange(p.num_movable), p.num_nodes, seed=3)
+    arr = synthetic_netlist(p.size_x, p.size_y, np.arange(p.num_movable), p.num_nodes, seed=3, shuffle_pins=shuffle)
     arr.validate()
+    assert np.array_equal(arr.net_pins, np.arange(arr.num_pins)) != shuffle
     deg = np.diff(arr.net_start)
     assert deg.min() >= 2 and (deg > 100).any() and np.mean(deg) < 6
     # offsets inside the pin's node
@@ -146,10 +148,11 @@ def _device_op(arr, device, ignore=100):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("config,scale,ignore", [("c1", 0.2, 100), ("c3", 0.05, 100), ("c1", 0.05, 4)])
-def test_wirelength_matches_oracle(cuda_device, config, scale, ignore):
+@pytest.mark.parametrize("config,scale,ignore,shuffle", [("c1", 0.2, 100, False), ("c3", 0.05, 100, True),
+                                                         ("c1", 0.05, 4, True)])
+def test_wirelength_matches_oracle(cuda_device, config, scale, ignore, shuffle):
     p = synth.make_placement(config, scale=scale)
-    arr = synthetic_netlist(p.size_x, p.size_y, np.arange(p.num_movable), p.num_nodes, seed=7)
+    arr = synthetic_netlist(p.size_x, p.size_y, np.arange(p.num_movable), p.num_nodes, seed=7, shuffle_pins=shuffle)
     gamma = 4.0 * p.bin_size_x
     wl, hp, gx, gy = _oracle(arr, p.x, p.y, gamma, ignore)
     op = _device_op(arr, cuda_device, ignore)
