@@ -159,4 +159,9 @@ class WirelengthOp:
         return {"wirelength": self.out[0], "hpwl": self.out[1], "grad_x": grad_x, "grad_y": grad_y}
 
     def error_flags(self) -> int:
+        """Flags OR-ed in by every call since the last clear_flags (synchronises):
+        EPB_FLAG_BAD_INDEX (0x10), EPB_FLAG_NONFINITE_CELL (0x1)."""
         return int(self.flags.item())
+
+    def clear_flags(self):
+        self.flags.zero_()
