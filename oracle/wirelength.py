@@ -28,6 +28,12 @@ HPWL_e = (max x - min x) + (max y - min y).  Both are weighted by the net
 weight.  Node gradients sum the gradients of the node's pins.
 
 Everything after the pin positions is float64.
+
+Parity unpinned against DREAMPlace: its wirelength op is absent here, and the
+reference holds no golden values for it.  The restatement is pinned to
+mathematics instead: the closed form of a two-pin net (L tanh(L / 2g)),
+central finite differences of the gradient, and the degree cap and weights
+(tests/test_wirelength.py).
 """
 from __future__ import annotations
 
