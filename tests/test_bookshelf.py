@@ -107,6 +107,20 @@ def test_tiny_netlist_offsets(tmp_path):
     assert nl.num_nodes == p.num_nodes
 
 
+@pytest.mark.parametrize("nets,msg", [
+    ("NetDegree : 2 n0\n  a I : 0 0\n  zz O : 0 0\n", "unknown node"),
+    ("  a I : 0 0\nNetDegree : 1 n0\n  b I\n", "outside a net"),
+    ("NetDegree : 3 n0\n  a I\n  b I\nNetDegree : 1 n1\n  c I\n", "early"),
+    ("NetDegree : 2 n0\n  a I\n", "early"),
+])
+def test_malformed_netlists_are_reported(tmp_path, nets, msg):
+    aux = _write_tiny(tmp_path)
+    (tmp_path / "t.nets").write_text("UCLA nets 1.0\n" + nets)
+    p = bookshelf.to_placement(bookshelf.read_aux(aux), 16, 16, enable_fillers=False)
+    with pytest.raises(ValueError, match=msg):
+        bookshelf.netlist_for_placement(aux, p)
+
+
 def test_netlist_round_trip(tmp_path):
     import sys
     from dreamplacett_framework_b200.wirelength import synthetic_netlist
