@@ -436,6 +436,10 @@ def run_sharded(args, p, dev, world, rank):
                           "gbs": b / avg_s / 1e9, "frac": b / avg_s / 1e9 / peak}
         dom = max(kern, key=lambda k: kern[k]["avg_us"])
         kernel_us = sum(v["avg_us"] for v in kern.values())
+        # our kernels per rank and step: k_band_select, k_scatter, k_row_fwd, k_col, k_row_inv, k_gather
+        # (the gather reuses the forward's selection); the peer transport adds k_push and a
+        # k_signal + k_wait pair after each of its three exchanges
+        launches_per_step = 13 if args.transport == "peer" else 6
         line = {
             "metric": METRIC, "value": K / (total_ms / 1000.0), "unit": UNIT, "n_gpus": world, "steps": K,
             "warmup": args.warmup, "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "strong",
@@ -449,7 +453,7 @@ def run_sharded(args, p, dev, world, rank):
             "e2e": {"value": K_e2e / (e2e_ms / 1000.0), "unit": UNIT, "steps": K_e2e,
                     "h2d_bytes_per_step": world * 2 * n * 4, "d2h_bytes_per_step": world * (2 * n * 4 + 8),
                     "path": "each rank: pinned pos[2n] H2D, sharded forward+backward, grad[2n] + energy D2H"},
-            "gpu_launches": 5 * K * world,
+            "gpu_launches": launches_per_step * K * world,
             "cuda_graph": ("timed steps replay one captured graph of forward+backward per rank; per-stage times "
                            "from eager profiled steps; e2e is eager API calls") if graph is not None else
                           "eager (NCCL collectives between the kernels)",
