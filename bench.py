@@ -60,10 +60,10 @@ STAGE_BYTES = {
 # these are cold-cache figures.
 NCU_TRAFFIC_C3 = {
     "scatter": 72.9e6,
-    "row_fwd": 60.8e6,
+    "row_fwd": 60.6e6,
     "column": 16.9e6,
-    "row_inv": 60.1e6,
-    "gather": 79.5e6,
+    "row_inv": 61.2e6,
+    "gather": 78.7e6,
 }
 
 
