@@ -69,7 +69,7 @@ NCU_TRAFFIC_C3 = {
 
 # 64-bit atomic adds per second on this pool's B200 for scatter-like footprints
 # (2x2, 2x3, 3x3 adds at hashed positions of a 2048 x 2048 int64 grid: 194-212 G/s),
-# measured by dreamplacett_framework_b200/csrc/probe_atomics.cu.  The scatter
+# measured by a standalone probe (profiles/scatter_atomic_rate.md).  The scatter
 # issues one such add per (cell, bin) pair, so count / rate is its floor.
 ATOMIC_RATE_GOPS = 205.0
 
@@ -198,6 +198,19 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def clock_soak(run_once, dev, seconds=1.0, batch=20):
+    """Untimed steps for at least `seconds` right before a timed region, so the
+    clock samples taken over this window and the timed steps cover a second or
+    more of sustained load however few steps are timed.  Returns its start."""
+    import torch
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        for _ in range(batch):
+            run_once()
+        torch.cuda.synchronize(dev)
+    return t0
+
+
 def gpu_smi_id(dev):
     import torch
     try:
@@ -263,11 +276,11 @@ def run_reference(args, p):
     nthreads = os.cpu_count() or 1
     step = cpu_step_factory(p, nthreads)
     # bounded: at most --ref-seconds of timed CPU work however large K is
-    n, el = time_cpu(step, max_seconds=args.ref_seconds, max_steps=args.steps, warmup=min(args.warmup, 2))
+    n, el = time_cpu(step, max_seconds=args.ref_seconds, max_steps=args.steps, warmup=args.warmup)
     value = n / el
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference",
-        "n_gpus": args.gpus, "steps": n, "warmup": min(args.warmup, 2), "ms_per_step": 1000.0 * el / n,
+        "n_gpus": args.gpus, "steps": n, "warmup": args.warmup, "ms_per_step": 1000.0 * el / n,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "config": workload_config(args, p),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": nthreads, "kind": "port",
@@ -338,7 +351,6 @@ def run_sharded(args, p, dev, world, rank):
     sampler = ClockSampler(gpu_smi_id(dev))
     sampler.start()
     time.sleep(0.5)
-    t_warm0 = time.perf_counter()
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize(dev)
@@ -370,6 +382,23 @@ def run_sharded(args, p, dev, world, rank):
             graph.replay()
         torch.cuda.synchronize(dev)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+
+    def soak_once():
+        flush.zero_()
+        graph.replay() if graph is not None else step()
+
+    # every rank runs the same number of soak steps (the peer transport's steps wait on one another)
+    n_soak = torch.tensor([0], dtype=torch.int64, device=dev)
+    if rank == 0:
+        ts = time.perf_counter()
+        soak_once()
+        torch.cuda.synchronize(dev)
+        n_soak[0] = max(20, int(1.0 / max(time.perf_counter() - ts, 1e-5)))
+    dist.broadcast(n_soak, 0)
+    dist.barrier()
+    t_soak0 = time.perf_counter()
+    for _ in range(int(n_soak.item())):
+        soak_once()
     if graph is None:
         sh.be.profile_start(2 * K)
     dist.barrier()
@@ -389,10 +418,8 @@ def run_sharded(args, p, dev, world, rank):
     if graph is None:
         stages = sh.be.profile_stop()
     total_ms = sum(a.elapsed_time(b) for a, b in ev)
-    clocks = sampler.summary(t0, t1)
-    if clocks["samples"] < 3:
-        clocks = sampler.summary(t_warm0, t1)
-        clocks["window"] = "warm-up and timed region"
+    clocks = sampler.summary(t_soak0, t1)
+    clocks["window"] = f"{int(n_soak.item())} untimed steps (about 1 s) right before the timed steps, and the timed steps"
     # e2e: pinned host pos in, this rank's gradient array and the energy out
     pos_host = torch.empty(2 * n, dtype=torch.float32).pin_memory()
     pos_host.copy_(pos.cpu())
@@ -543,7 +570,6 @@ def main():
     sampler.start()
     time.sleep(0.5)
 
-    t_warm0 = time.perf_counter()
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize(dev)
@@ -575,6 +601,12 @@ def main():
         graph.replay()
     torch.cuda.synchronize(dev)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+
+    def soak_once():
+        flush.zero_()
+        graph.replay()
+
+    t_soak0 = clock_soak(soak_once, dev)
     barrier()
     torch.cuda.synchronize(dev)
     t_wall0 = time.perf_counter()
@@ -588,10 +620,8 @@ def main():
     t_wall1 = time.perf_counter()
     step_ms = [a.elapsed_time(b) for a, b in ev]
     total_ms = sum(step_ms)
-    clocks = sampler.summary(t_wall0, t_wall1)
-    if clocks["samples"] < 3:  # timed region shorter than the sampling period: widen to warm-up
-        clocks = sampler.summary(t_warm0, t_wall1)
-        clocks["window"] = "warm-up and timed region"
+    clocks = sampler.summary(t_soak0, t_wall1)
+    clocks["window"] = "1 s of untimed graph replays right before the timed steps, and the timed steps"
     if eng.error_flags() != 0:
         raise SystemExit("engine flagged an error during the graph replays")
 
@@ -651,7 +681,7 @@ def main():
             kern["scatter"]["atomic_bound"] = {
                 "atomics": na, "rate_gops": ATOMIC_RATE_GOPS, "floor_us": floor_us,
                 "frac": floor_us / kern["scatter"]["avg_us"],
-                "rate_source": "dreamplacett_framework_b200/csrc/probe_atomics.cu on this pool's B200"}
+                "rate_source": "standalone probe on this pool's B200 (profiles/scatter_atomic_rate.md)"}
         step_bytes = sum(algorithmic_bytes(k, p.num_cells, bins) for k in STAGE_BYTES)
         value = world * K / (total_ms / 1000.0)
         line = {

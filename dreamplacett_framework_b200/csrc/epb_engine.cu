@@ -1280,8 +1280,8 @@ int epb_profile_stop(epb_handle* h, double* stage_ms, int32_t* stage_launches) {
 // cudaMalloc's device-wide synchronisation is not acceptable on their path.
 // The accumulation grid is this file-scope device array; its device address
 // is looked up once per device with cudaGetSymbolAddress (host code must not
-// use the symbol itself as a pointer).  The tail words after the grid hold the
-// kernel's flag word.
+// use the symbol itself as a pointer).  The word right after a call's nbins
+// map words holds the scatter's flag word; each call clears both.
 // ---------------------------------------------------------------------------
 static __device__ __align__(256) long long g_noalloc_grid[EPB_NOALLOC_MAX_BINS + 32];
 
@@ -1324,8 +1324,10 @@ extern "C" int epb_density_noalloc(const epb_config* cfg, const epb_cells* cells
                             "grid of " + std::to_string(cfg->num_bins_x) + "x" + std::to_string(cfg->num_bins_y) +
                                 " bins exceeds the allocation-free limit of " + std::to_string(EPB_NOALLOC_MAX_BINS) +
                                 " bins; use epb_create/epb_forward");
-    if (!(cfg->xh > cfg->xl) || !(cfg->yh > cfg->yl) || cfg->fixed_point_bits > 60 || cfg->flags != 0)
-        return noalloc_fail(err, err_len, EPB_EINVAL, "invalid die box, fixed_point_bits or flags");
+    if (!std::isfinite(cfg->xl) || !std::isfinite(cfg->xh) || !std::isfinite(cfg->yl) || !std::isfinite(cfg->yh) ||
+        !(cfg->xh > cfg->xl) || !(cfg->yh > cfg->yl) || cfg->fixed_point_bits > 60 || cfg->flags != 0)
+        return noalloc_fail(err, err_len, EPB_EINVAL, "invalid die box (bounds must be finite, xh > xl, yh > yl), "
+                                                      "fixed_point_bits or flags");
     if (cfg->device < 0 || cfg->device >= kMaxDevices) return noalloc_fail(err, err_len, EPB_EINVAL, "bad device");
     CellView v;
     if (int rc = make_view(nullptr, cells, v)) return noalloc_fail(err, err_len, rc, "invalid cell ranges or NULL arrays");
@@ -1345,7 +1347,7 @@ extern "C" int epb_density_noalloc(const epb_config* cfg, const epb_cells* cells
         base = g_noalloc_ptr[cfg->device];
     }
     long long* grid = static_cast<long long*>(base);
-    unsigned* flags = reinterpret_cast<unsigned*>(grid + EPB_NOALLOC_MAX_BINS);
+    unsigned* flags = reinterpret_cast<unsigned*>(grid + nbins);  // cleared with the map below
 
     // geometry exactly as epb_create resolves it
     epb_handle g;

@@ -23,6 +23,7 @@ from __future__ import annotations
 
 import math
 import threading
+import weakref
 from typing import Dict, Optional, Tuple
 
 import torch
@@ -71,17 +72,22 @@ def _on(t, dev):
 
 
 def _static(t, dev):
-    """Device copy of a per-design buffer, re-uploaded only when the tensor changes."""
+    """Device copy of a per-design buffer, re-uploaded only when the tensor changes.
+
+    An entry holds a weak reference to its source tensor and is dropped when
+    that tensor is freed, so a new tensor that reuses the old one's id (and
+    even its memory) never matches a stale copy."""
     if t is None:
         return None
     if t.is_cuda and t.device == dev and t.dtype == torch.float32 and t.is_contiguous():
         return t.detach()
-    key = (id(t), t.data_ptr(), t._version, tuple(t.shape), str(dev))
-    hit = _static_cache.get(id(t))
-    if hit is not None and hit[0] == key:
-        return hit[1]
+    slot = (id(t), str(dev))
+    key = (t.data_ptr(), t._version, tuple(t.shape))
+    hit = _static_cache.get(slot)
+    if hit is not None and hit[0]() is t and hit[1] == key:
+        return hit[2]
     d = _on(t, dev)
-    _static_cache[id(t)] = (key, d)
+    _static_cache[slot] = (weakref.ref(t, lambda _r, s=slot: _static_cache.pop(s, None)), key, d)
     return d
 
 
@@ -126,12 +132,21 @@ class ElectricPotentialFunction(torch.autograd.Function):
         r = _static(ratio, dev)
         # initial (fixed-cell) density: normalised by bin area once, as the
         # reference client uploads it (integration/scatter_ttnn_client.py:791-795)
+        # The engine is shared by every operator on this grid, so the map it holds
+        # is matched against this call's tensor by identity (a weak reference, so
+        # a later tensor reusing a freed one's id never matches), version and bin
+        # size; a call without a map clears whatever an earlier call uploaded.
         if initial_density_map is not None:
-            ikey = (id(initial_density_map), initial_density_map._version, float(bin_size_x), float(bin_size_y))
-            if eng._init_key != ikey:
+            ikey = (initial_density_map._version, initial_density_map.data_ptr(),
+                    float(bin_size_x), float(bin_size_y))
+            held = eng._init_key
+            if held is None or held[0]() is not initial_density_map or held[1] != ikey:
                 bin_area = float(bin_size_x) * float(bin_size_y)
                 eng.set_initial_density(_on(initial_density_map / bin_area, dev).reshape(-1))
-                eng._init_key = ikey
+                eng._init_key = (weakref.ref(initial_density_map), ikey)
+        elif eng._init_key is not None:
+            eng.set_initial_density(None)
+            eng._init_key = None
         cells = node_cells(pos_dev, num_nodes, sx, sy, ox, oy, r, num_movable_nodes, num_filler_nodes)
         out = eng.forward(cells, want_density=False, want_potential=False, want_fields=True, want_energy=True)
         ctx.engine = eng

@@ -81,8 +81,8 @@ class ElectricPotentialEngine:
         if not torch.cuda.is_available():
             raise RuntimeError("ElectricPotentialEngine needs a CUDA device (no CPU path)")
         self.lib = _lib.load()
-        self.device = torch.device("cuda", torch.cuda.current_device() if device is None
-                                   else torch.device(device).index or 0)
+        idx = None if device is None else torch.device(device).index
+        self.device = torch.device("cuda", torch.cuda.current_device() if idx is None else idx)
         self.M, self.N = int(num_bins_x), int(num_bins_y)
         self.xl, self.yl, self.xh, self.yh = float(xl), float(yl), float(xh), float(yh)
         cfg = _lib.EpbConfig(self.M, self.N, self.xl, self.yl, self.xh, self.yh,

@@ -46,8 +46,8 @@ class DensityDescent:
             raise RuntimeError("DensityDescent needs a CUDA device (no CPU path)")
         p = placement
         self.p = p
-        self.device = torch.device("cuda", torch.cuda.current_device() if device is None
-                                   else torch.device(device).index or 0)
+        idx = None if device is None else torch.device(device).index
+        self.device = torch.device("cuda", torch.cuda.current_device() if idx is None else idx)
         to = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(self.device)
         self.x, self.y = to(p.x), to(p.y)
         self.width, self.height = to(p.size_x), to(p.size_y)

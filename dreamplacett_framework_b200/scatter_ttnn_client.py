@@ -24,7 +24,8 @@ inputs.  The timing dict has the reference's keys.  The shared-memory keys are
 """
 from __future__ import annotations
 
-import os
+import collections
+import statistics
 import time
 from typing import Optional
 
@@ -149,59 +150,50 @@ class ScatterTTNNClient:
         return field_x, field_y, timing
 
     def timing_summary(self, n_warmup: int = 4) -> dict:
-        timings = self._timings[n_warmup:] if len(self._timings) > n_warmup else self._timings
-        if not timings:
-            timings = self._timings
-        if not timings:
+        """Aggregate of the per-call timing dicts (the reference's key contract,
+        integration/scatter_ttnn_client.py:511-531): for every numeric key K,
+        `K_mean` and `K_median`; for every other key, its most frequent value
+        under K; `n_iters` counts all recorded calls and `n_timed` those
+        aggregated.  The first `n_warmup` calls are left out when more calls
+        than that were recorded; otherwise every call is aggregated."""
+        recs = self._timings
+        if not recs:
             return {}
-        result = {}
-        for k in timings[0].keys():
-            vals = [t[k] for t in timings if k in t]
-            if not vals:
-                continue
-            if isinstance(vals[0], (int, float)):
-                result[f"{k}_mean"] = float(np.mean(vals))
-                result[f"{k}_median"] = float(np.median(vals))
+        timed = recs[n_warmup:] if len(recs) > n_warmup else recs
+        keys = list(dict.fromkeys(k for r in timed for k in r))
+        summary = {}
+        for k in keys:
+            vals = [r[k] for r in timed if k in r]
+            if all(isinstance(v, (int, float)) and not isinstance(v, bool) for v in vals):
+                summary[k + "_mean"] = statistics.fmean(vals)
+                summary[k + "_median"] = float(statistics.median(vals))
             else:
-                result[k] = max(set(vals), key=vals.count)
-        result["n_iters"] = len(self._timings)
-        result["n_timed"] = len(timings)
-        return result
+                summary[k] = collections.Counter(vals).most_common(1)[0][0]
+        summary["n_iters"] = len(recs)
+        summary["n_timed"] = len(timed)
+        return summary
 
 
 def patch_dreamplace(container: str = "", ipc_dir: str = "", num_cells: int = 0,
                      direct: bool = False) -> None:
     """Replace DREAMPlace's ElectricPotentialFunction forward/backward with the
-    B200 operator (reference client:534-870).  V13_USE_CPU_AFTER_ITER keeps the
-    reference's cut-over back to DREAMPlace's own forward after N iterations."""
+    B200 operator (reference client:534-870).  Every call runs on the engine:
+    the reference's V13_USE_CPU_AFTER_ITER diagnostic, which hands later calls
+    back to DREAMPlace's own forward, is not honoured (there is no CPU path)."""
     global _client
     _client = ScatterTTNNClient(container=container, ipc_dir=ipc_dir, nc_max=num_cells, direct=direct)
     import dreamplace.ops.electric_potential.electric_potential as ep_mod
 
     fn_cls = ep_mod.ElectricPotentialFunction
-    orig_forward = fn_cls.forward.__func__ if hasattr(fn_cls.forward, "__func__") else fn_cls.forward
-    orig_backward = fn_cls.backward.__func__ if hasattr(fn_cls.backward, "__func__") else fn_cls.backward
-    counter = [0]
 
     def _forward(ctx, pos, *args):
-        counter[0] += 1
-        try:
-            cpu_after = int(os.environ.get("V13_USE_CPU_AFTER_ITER", "0"))
-        except ValueError:
-            cpu_after = 0
-        if cpu_after > 0 and counter[0] > cpu_after:
-            ctx._epb = False
-            return orig_forward(ctx, pos, *args)
         t0 = time.perf_counter()
         energy = _ep.ElectricPotentialFunction.forward(ctx, pos, *args)
-        ctx._epb = True
         _client._timings.append({"ep_total_ms": (time.perf_counter() - t0) * 1000, "gather_mode": "epb200"})
         return energy
 
     def _backward(ctx, grad_pos):
-        if getattr(ctx, "_epb", False):
-            return _ep.ElectricPotentialFunction.backward(ctx, grad_pos)
-        return orig_backward(ctx, grad_pos)
+        return _ep.ElectricPotentialFunction.backward(ctx, grad_pos)
 
     fn_cls.forward = staticmethod(_forward)
     fn_cls.backward = staticmethod(_backward)

@@ -103,7 +103,8 @@ class Netlist:
     def __init__(self, arrays: NetlistArrays, device, ignore_net_degree: int = 100, validate: bool = True):
         if validate:
             arrays.validate()
-        self.device = torch.device(device)
+        d = torch.device(device)
+        self.device = torch.device("cuda", torch.cuda.current_device() if d.index is None else d.index)
         self.arrays = arrays
         i32 = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.int32)).to(self.device)
         f32 = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(self.device)
@@ -116,7 +117,7 @@ class Netlist:
         self.c = _lib.EpbNetlist(p(self.net_start), p(self.net_pins), p(self.pin_node), p(self.pin_offset_x),
                                  p(self.pin_offset_y), p(self.net_weight), p(self.node_pin_start), p(self.node_pins),
                                  arrays.num_nets, arrays.num_pins, arrays.num_nodes, int(ignore_net_degree),
-                                 self.device.index or 0)
+                                 self.device.index)
 
 
 class WirelengthOp:

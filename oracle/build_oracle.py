@@ -27,11 +27,26 @@ def build_oracle(verbose=False):
     return out
 
 
+def reference_root(ref_root=None):
+    """Where the reference tree is: the argument, else the REF_ROOT environment
+    variable, else BASELINE.json's `reference_path`; None when none is set."""
+    if ref_root:
+        return ref_root
+    if os.environ.get("REF_ROOT"):
+        return os.environ["REF_ROOT"]
+    cfg = os.path.join(os.path.dirname(HERE), "BASELINE.json")
+    if os.path.exists(cfg):
+        import json
+        with open(cfg) as f:
+            return json.load(f).get("reference_path") or None
+    return None
+
+
 def build_ref(ref_root=None, verbose=False):
     """Returns the ref_dct path, or None when the reference tree is absent."""
-    ref_root = ref_root or os.environ.get("REF_ROOT", "/root/reference")
+    ref_root = reference_root(ref_root)
     exe = os.path.join(HERE, "_ref", "ref_dct")
-    if not os.path.isdir(ref_root):
+    if not ref_root or not os.path.isdir(ref_root):
         return exe if os.path.exists(exe) else None
     r = subprocess.run(["bash", os.path.join(HERE, "build_ref.sh"), ref_root],
                        capture_output=not verbose, text=True)

@@ -120,4 +120,9 @@ def main(ref_root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("REF_ROOT", "/root/reference"))
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(HERE)), "oracle"))
+    import build_oracle
+    root = build_oracle.reference_root(sys.argv[1] if len(sys.argv) > 1 else None)
+    if not root:
+        raise SystemExit("make_golden: give the reference tree as an argument or in REF_ROOT")
+    main(root)

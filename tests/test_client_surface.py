@@ -39,8 +39,10 @@ def test_start_argument_rules():
 
 
 @pytest.mark.gpu
-def test_cpu_cutover_after_iterations(cuda_device, fake_dp, monkeypatch):
-    """V13_USE_CPU_AFTER_ITER=N hands calls after the N-th back to DREAMPlace's own forward."""
+def test_cpu_cutover_switch_not_honoured(cuda_device, fake_dp, monkeypatch):
+    """The reference's V13_USE_CPU_AFTER_ITER hands later calls back to
+    DREAMPlace's own forward; the B200 operator has no CPU path, so every call
+    stays on the engine whatever the variable says."""
     cls, calls = fake_dp
     stc.patch_dreamplace()
     monkeypatch.setenv("V13_USE_CPU_AFTER_ITER", "1")
@@ -48,12 +50,38 @@ def test_cpu_cutover_after_iterations(cuda_device, fake_dp, monkeypatch):
     f = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(cuda_device)
     t = {k: f(getattr(p, k)) for k in ("size_x_clamped", "size_y_clamped", "offset_x", "offset_y", "ratio")}
     t["initial_density_map"] = f(p.initial_density_map)
-    for i in range(2):
+    for i in range(3):
         pos = torch.cat([f(p.x), f(p.y)]).requires_grad_(True)
         e = cls.apply(pos, *fake_dreamplace.ep_args(p, t))
         e.backward()
-    assert calls["orig_forward"] == 1 and calls["orig_backward"] == 1
+    assert calls["orig_forward"] == 0 and calls["orig_backward"] == 0
+    assert stc.get_timing_summary()["n_iters"] == 3
     stc.teardown()
+
+
+def test_timing_summary_key_contract():
+    """timing_summary follows the reference's keys (client:511-531): K_mean and
+    K_median for numeric keys, the most frequent value for the others, n_iters
+    and n_timed; warm-up calls are dropped only when more calls were made."""
+    c = stc.ScatterTTNNClient("", "", num_bins_x=64, num_bins_y=64, nc_max=10)
+    assert c.timing_summary() == {}
+    for i in range(6):
+        c._timings.append({"scatter_ms": float(i), "h2d_ms": 2 * i, "gather_mode": "a" if i != 5 else "b"})
+    s = c.timing_summary(n_warmup=2)
+    assert set(s) == {"scatter_ms_mean", "scatter_ms_median", "h2d_ms_mean", "h2d_ms_median", "gather_mode",
+                      "n_iters", "n_timed"}
+    assert s["n_iters"] == 6 and s["n_timed"] == 4
+    assert s["scatter_ms_mean"] == pytest.approx(3.5) and s["scatter_ms_median"] == pytest.approx(3.5)
+    assert s["h2d_ms_mean"] == pytest.approx(7.0) and s["gather_mode"] == "a"
+    s_all = c.timing_summary(n_warmup=10)
+    assert s_all["n_timed"] == 6 and s_all["scatter_ms_mean"] == pytest.approx(2.5)
+    # a full per-call record gives the reference's summary keys
+    c2 = stc.ScatterTTNNClient("", "", num_bins_x=64, num_bins_y=64, nc_max=10)
+    rec = {k: 1.0 for k in REF_TIMING_KEYS if k != "gather_mode"}
+    rec["gather_mode"] = "epb200"
+    c2._timings.append(rec)
+    want = {k + sfx for k in REF_TIMING_KEYS if k != "gather_mode" for sfx in ("_mean", "_median")}
+    assert set(c2.timing_summary()) == want | {"gather_mode", "n_iters", "n_timed"}
 
 
 @pytest.mark.gpu

@@ -90,3 +90,17 @@ def test_noalloc_refuses_grids_beyond_its_limit():
     assert st == _lib.EPB_EINVAL
     assert b"exceeds the allocation-free limit" in err.value
     assert 2048 * 1024 > _lib.NOALLOC_MAX_BINS
+
+
+@pytest.mark.parametrize("box", [(0.0, 0.0, float("inf"), 1.0), (0.0, float("nan"), 1.0, 1.0),
+                                 (float("-inf"), 0.0, 1.0, 1.0), (1.0, 0.0, 1.0, 1.0)])
+def test_noalloc_refuses_bad_die_box(box):
+    """Non-finite or empty die bounds are refused before any device work, as
+    epb_create refuses them."""
+    lib = _lib.load()
+    cfg = _lib.EpbConfig(64, 64, *box, 0, 0, 0, 0)
+    z = _lib.EpbCells(None, None, None, None, None, None, None, 0, 0, 0, 0)
+    err = ctypes.create_string_buffer(256)
+    st = lib.epb_density_noalloc(ctypes.byref(cfg), ctypes.byref(z), None, None, ctypes.c_void_p(1), err, len(err))
+    assert st == _lib.EPB_EINVAL
+    assert b"invalid die box" in err.value
