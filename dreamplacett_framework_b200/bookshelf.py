@@ -329,6 +329,9 @@ def load_config(path: str) -> dict:
                 enable_fillers=bool(cfg.get("enable_fillers", 1)),
                 random_seed=int(cfg.get("random_seed", 1000)),
                 random_center_init=bool(cfg.get("random_center_init_flag", 0)),
+                gamma=float(cfg.get("gamma", 4.0)),
+                stop_overflow=float(cfg.get("stop_overflow", 0.07)),
+                ignore_net_degree=int(cfg.get("ignore_net_degree", 100)),
                 stages=stages)
 
 

@@ -97,6 +97,40 @@ class Placement:
         return (self.initial_density_map.astype(np.float32) / ba).astype(np.float32)
 
 
+    def regrid(self, num_bins_x: int, num_bins_y: int) -> "Placement":
+        """The same design on another grid (a stage of multi-stage placement):
+        stretched sizes, offsets, ratio and the fixed-cell density for those
+        bins; the node arrays are shared."""
+        import dataclasses
+        q = dataclasses.replace(self, num_bins_x=int(num_bins_x), num_bins_y=int(num_bins_y))
+        bsx, bsy = q.bin_size_x, q.bin_size_y
+        q.size_x_clamped, q.size_y_clamped, q.offset_x, q.offset_y, q.ratio = stretch(q.size_x, q.size_y, bsx, bsy)
+        t = slice(q.num_movable, q.num_movable + q.num_terminals)
+        if q.num_terminals:
+            q.initial_density_map = rasterise(q.x[t].astype(np.float64), q.y[t].astype(np.float64),
+                                              q.size_x[t].astype(np.float64), q.size_y[t].astype(np.float64),
+                                              q.xl, q.yl, bsx, bsy, q.num_bins_x, q.num_bins_y)
+        else:
+            q.initial_density_map = np.zeros((q.num_bins_x, q.num_bins_y), np.float64)
+        return q
+
+
+def center_init(p: "Placement", seed: int = 1000, spread: float = 0.001) -> "Placement":
+    """Movable cells and fillers at the die centre with Gaussian noise of
+    spread * die size (DREAMPlace's random_center_init_flag, the reference
+    configs' default), clamped to the die; terminals stay.  In place."""
+    rng = np.random.default_rng(seed)
+    n = p.num_nodes
+    mov = np.r_[0:p.num_movable, n - p.num_filler:n]
+    cx, cy = 0.5 * (p.xl + p.xh), 0.5 * (p.yl + p.yh)
+    w, h = p.size_x[mov], p.size_y[mov]
+    x = cx - 0.5 * w + spread * (p.xh - p.xl) * rng.standard_normal(len(mov))
+    y = cy - 0.5 * h + spread * (p.yh - p.yl) * rng.standard_normal(len(mov))
+    p.x[mov] = np.clip(x, p.xl, p.xh - w).astype(np.float32)
+    p.y[mov] = np.clip(y, p.yl, p.yh - h).astype(np.float32)
+    return p
+
+
 def stretch(size_x, size_y, bin_size_x, bin_size_y):
     """DREAMPlace's clamp to sqrt(2) bins with area ratio (fp32)."""
     sx = np.asarray(size_x, np.float32)
