@@ -38,20 +38,39 @@ sys.path.insert(0, ROOT)
 METRIC = "electric-potential iters/sec (scatter+DCT+gather) at 1.1M cells, 2048² grid"
 UNIT = "iters/s"
 
-# Algorithmic bytes per launch of each engine stage: every cell array and
-# every grid the stage must touch, counted once (n = scattered cells, B = bins).
-#   scatter : x,y,size_x,size_y,offset_x,offset_y,ratio (28 B/cell) + int64 grid (8 B/bin)
-#   row_fwd : int64 grid read + re-zero (16) + initial density (4) + density out (4) + row DCT out (4)
+# Algorithmic bytes per launch of each engine stage: every array the stage
+# must touch, counted once (n = scattered cells, L = tile listings, B = bins).
+# Cell-tile path (the default), steady state of a whole grid (the lists
+# persist; positions that stay inside the listing margin need no rebuild):
+#   bin     : validation of every listing: offsets/sizes + node/box/ratio read (32 B/listing),
+#             the cell's position re-read (8 B/cell), footprint + bins written (24 B/listing)
+#   scatter : footprint, bins, ratio per listing (40 B/listing) + initial density (4 B/bin) + density out (4 B/bin)
+#   row_fwd : density in (4) + row DCT out (4)
 #   column  : row DCT in (4) + two column-pass outputs (8: field_x form, potential form)
 #   row_inv : two column-pass maps in (8) + potential, field_x, field_y (12) + interleaved fields (8)
+#   gather  : owner listing records (40 B/cell) + gradient out (8 B/cell) + interleaved fields (8 B/bin)
+# Cell-order path (EPB_CONFIG_CELL_ORDER):
+#   scatter : x,y,size_x,size_y,offset_x,offset_y,ratio (28 B/cell) + int64 grid (8 B/bin)
+#   row_fwd : int64 grid read + re-zero (16) + initial density (4) + density out (4) + row DCT out (4)
 #   gather  : cell arrays (28 B/cell) + gradient out (8 B/cell) + interleaved fields (8 B/bin)
+# (per_cell, per_listing, per_bin)
 STAGE_BYTES = {
-    "scatter": (28, 8),
-    "row_fwd": (0, 28),
-    "column": (0, 12),
-    "row_inv": (0, 28),
-    "gather": (36, 8),
+    "bin": (8, 56, 0),
+    "scatter": (0, 40, 8),
+    "row_fwd": (0, 0, 8),
+    "column": (0, 0, 12),
+    "row_inv": (0, 0, 28),
+    "gather": (48, 0, 8),
 }
+STAGE_BYTES_CELL_ORDER = dict(STAGE_BYTES, scatter=(28, 0, 8), row_fwd=(0, 0, 28), gather=(36, 0, 8))
+STAGE_BYTES_CELL_ORDER.pop("bin")
+
+# The survey's scatter + convert + gather bytes (the north star's 60%-of-HBM
+# target): scatter N*20 + B*8, convert B*12, gather N*20 + B*8 + N*8.  The
+# cell-order path converts inside its row pass, so its scatter + gather figure
+# leaves the conversion out (48 N + 16 B); the tiles convert in their scatter.
+def sc_ga_bytes(n_cells, bins, with_convert=True):
+    return 48 * n_cells + (28 if with_convert else 16) * bins
 
 
 # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of each
@@ -69,15 +88,15 @@ NCU_TRAFFIC_C3 = {
 
 # 64-bit atomic adds per second on this pool's B200 for scatter-like footprints
 # (2x2, 2x3, 3x3 adds at hashed positions of a 2048 x 2048 int64 grid: 194-212 G/s),
-# measured by a standalone probe (profiles/scatter_atomic_rate.md).  The scatter
-# issues one such add per (cell, bin) pair, so count / rate is its floor.
+# measured by a standalone probe (profiles/scatter_atomic_rate.md).  The
+# cell-order scatter issues one such add per (cell, bin) pair, so count / rate
+# is its floor.
 ATOMIC_RATE_GOPS = 205.0
 
 
-def scatter_atomics(p):
-    """(cell, bin) pairs the scatter adds for placement p: footprint rows x
-    columns per scattered cell (bin indices as the kernel computes them, up to
-    exact-edge cases where an overlap is zero and no add is issued)."""
+def footprints(p):
+    """Bin ranges (kx0, kx1, ky0, ky1) of the scattered cells of placement p,
+    as the kernels compute them up to exact-edge cases."""
     import numpy as np
     (b0, e0), (b1, e1) = p.ranges
     idx = np.concatenate([np.arange(b0, e0), np.arange(b1, e1)])
@@ -85,16 +104,37 @@ def scatter_atomics(p):
     x = (p.x[idx] + p.offset_x[idx]).astype(f)
     y = (p.y[idx] + p.offset_y[idx]).astype(f)
     bsx, bsy = f(p.bin_size_x), f(p.bin_size_y)
-    kx0 = np.clip(np.floor((x - f(p.xl)) / bsx), 0, p.num_bins_x - 1)
-    ky0 = np.clip(np.floor((y - f(p.yl)) / bsy), 0, p.num_bins_y - 1)
-    kx1 = np.clip(np.floor((x + p.size_x_clamped[idx] - f(p.xl)) / bsx), 0, p.num_bins_x - 1)
-    ky1 = np.clip(np.floor((y + p.size_y_clamped[idx] - f(p.yl)) / bsy), 0, p.num_bins_y - 1)
+    kx0 = np.clip(np.floor((x - f(p.xl)) / bsx), 0, p.num_bins_x - 1).astype(np.int64)
+    ky0 = np.clip(np.floor((y - f(p.yl)) / bsy), 0, p.num_bins_y - 1).astype(np.int64)
+    kx1 = np.clip(np.floor((x + p.size_x_clamped[idx] - f(p.xl)) / bsx), 0, p.num_bins_x - 1).astype(np.int64)
+    ky1 = np.clip(np.floor((y + p.size_y_clamped[idx] - f(p.yl)) / bsy), 0, p.num_bins_y - 1).astype(np.int64)
+    return kx0, kx1, ky0, ky1
+
+
+def scatter_atomics(p):
+    """(cell, bin) pairs the cell-order scatter adds for placement p."""
+    import numpy as np
+    kx0, kx1, ky0, ky1 = footprints(p)
     return int(np.sum((kx1 - kx0 + 1) * (ky1 - ky0 + 1)))
 
 
-def algorithmic_bytes(stage, n_cells, bins):
-    per_cell, per_bin = STAGE_BYTES[stage]
-    return per_cell * n_cells + per_bin * bins
+def tile_listings(p, tile=32, margin=2):
+    """Listings of the cell tiles for placement p: the tiles each cell's
+    footprint, widened by the listing margin, meets (cells meeting more than
+    four take the escape path)."""
+    import numpy as np
+    kx0, kx1, ky0, ky1 = footprints(p)
+    tx = min(tile, p.num_bins_x)
+    ty = min(tile, p.num_bins_y)
+    kx0 = np.maximum(kx0 - margin, 0); ky0 = np.maximum(ky0 - margin, 0)
+    kx1 = np.minimum(kx1 + margin, p.num_bins_x - 1); ky1 = np.minimum(ky1 + margin, p.num_bins_y - 1)
+    nt = (kx1 // tx - kx0 // tx + 1) * (ky1 // ty - ky0 // ty + 1)
+    return int(np.sum(nt[nt <= 4]))
+
+
+def algorithmic_bytes(stage, n_cells, bins, listings=0, cell_order=False):
+    per_cell, per_listing, per_bin = (STAGE_BYTES_CELL_ORDER if cell_order else STAGE_BYTES)[stage]
+    return per_cell * n_cells + per_listing * listings + per_bin * bins
 
 
 def wirelength_item(p, dev, flush, peak, K=200, W=5):
@@ -308,31 +348,202 @@ def workload_config(args, p):
     }
 
 
-def sharded_bytes(stage, n_cells, bins, P):
+def sharded_bytes(stage, n_cells, bins, P, listings):
     """Algorithmic bytes one rank moves per launch when the grid is split in P
-    row bands: every rank reads all cells for its band filter (scatter, gather),
-    grids are 1/P per rank."""
-    per_cell, per_bin = STAGE_BYTES[stage]
-    if stage == "gather":
-        return 28 * n_cells + 8 * n_cells // P + per_bin * bins // P
-    return per_cell * n_cells + per_bin * bins // P
+    row bands.  A band rebuilds its tile lists every call: the x data of every
+    cell (offset, size: 12 B) is read twice (count, fill), the y data, ratio and
+    records only for the band's cells (about 1/P of them); the tile stages and
+    the grids are 1/P per rank."""
+    nb, lb, bb = n_cells // P, listings // P, bins // P
+    if stage == "bin":
+        # count + fill: x data of all cells twice, y data + ratio of the band's twice,
+        # records written (32 B/listing); validation as on a whole grid
+        return 24 * n_cells + 32 * nb + 32 * lb + 8 * nb + 56 * lb
+    per_cell, per_listing, per_bin = STAGE_BYTES[stage]
+    return per_cell * nb + per_listing * lb + per_bin * bb
 
 
-def run_sharded(args, p, dev, world, rank):
-    """One grid over `world` GPUs (strong scaling of the same workload)."""
+def _cells_on(p, dev):
     import numpy as np
     import torch
-    import torch.distributed as dist
     from dreamplacett_framework_b200.engine import CellTensors
-    from dreamplacett_framework_b200.sharded import ShardedElectricPotential
-
     to = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dev)
     n = p.num_nodes
     pos = torch.empty(2 * n, dtype=torch.float32, device=dev)
     pos[:n].copy_(to(p.x))
     pos[n:].copy_(to(p.y))
     sx, sy, ox, oy, ratio = (to(a) for a in (p.size_x_clamped, p.size_y_clamped, p.offset_x, p.offset_y, p.ratio))
-    cells = CellTensors(pos[:n], pos[n:], sx, sy, ox, oy, ratio, ranges=p.ranges)
+    return pos, CellTensors(pos[:n], pos[n:], sx, sy, ox, oy, ratio, ranges=p.ranges), to
+
+
+def _flush_buffer(dev):
+    import torch
+    l2 = getattr(torch.cuda.get_device_properties(dev), "L2_cache_size", 126 * 2 ** 20)
+    return torch.empty(max(2 * l2, 256 * 2 ** 20) // 4, dtype=torch.float32, device=dev)
+
+
+def _kernels(stages, bytes_of, peak):
+    kern = {}
+    for name, (ms, cnt) in stages.items():
+        if cnt == 0:
+            continue
+        avg_s = ms / cnt / 1000.0
+        b = bytes_of(name)
+        kern[name] = {"avg_us": avg_s * 1e6, "launches": cnt, "bytes": b, "gbs": b / avg_s / 1e9,
+                      "frac": b / avg_s / 1e9 / peak}
+    return kern
+
+
+def measure_single(p, dev, K, W, flush, peak, e2e=False, path=None):
+    """One GPU: W eager warm-up steps, per-stage times from eager profiled
+    steps, then K timed replays of one captured graph of forward + backward
+    (L2 flushed between steps, outside the events).  Returns the numbers of
+    the line (and, with e2e, the host-buffer API timing)."""
+    import numpy as np
+    import torch
+    from dreamplacett_framework_b200.engine import ElectricPotentialEngine
+    pos, cells, to = _cells_on(p, dev)
+    n = p.num_nodes
+    eng = ElectricPotentialEngine(p.num_bins_x, p.num_bins_y, p.xl, p.yl, p.xh, p.yh, device=dev, path=path)
+    eng.set_initial_density(to(p.initial_density_norm()))
+    M, N = p.num_bins_x, p.num_bins_y
+    outs = {k: torch.empty((M, N), dtype=torch.float32, device=dev)
+            for k in ("density", "potential", "field_x", "field_y")}
+    outs["energy"] = torch.empty(1, dtype=torch.float32, device=dev)
+    grad = torch.zeros(2 * n, dtype=torch.float32, device=dev)
+
+    def step():
+        eng.forward(cells, out=outs)
+        eng.backward(cells, grad_x=grad[:n], grad_y=grad[n:])
+
+    stream = torch.cuda.current_stream(dev)
+    tiles = path == "tiles"
+    for _ in range(W):
+        step()
+    torch.cuda.synchronize(dev)
+    if eng.error_flags() != 0:
+        raise SystemExit("engine flagged non-finite cells during warm-up")
+    K_prof = max(10, min(K, 500))
+    eng.profile_start(2 * K_prof)  # forward + backward per step
+    for _ in range(K_prof):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize(dev)
+    stages = eng.profile_stop()
+    # the timed steps replay one CUDA graph of forward + backward (the engine's calls
+    # are stream-ordered and allocation-free once warmed up, so they capture as they are)
+    graph = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream(dev)
+    cap.wait_stream(stream)
+    with torch.cuda.stream(cap):
+        step()
+    stream.wait_stream(cap)
+    torch.cuda.synchronize(dev)
+    with torch.cuda.graph(graph, stream=cap):
+        step()
+    for _ in range(W):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+
+    def soak_once():
+        flush.zero_()
+        graph.replay()
+
+    t_soak0 = clock_soak(soak_once, dev)
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    for i in range(K):
+        flush.zero_()
+        ev[i][0].record(stream)
+        graph.replay()
+        ev[i][1].record(stream)
+    torch.cuda.synchronize(dev)
+    t1 = time.perf_counter()
+    total_ms = sum(a.elapsed_time(b) for a, b in ev)
+    res = {"total_ms": total_ms, "K": K, "K_prof": K_prof, "stages": stages, "t_soak0": t_soak0, "t0": t0, "t1": t1}
+    if eng.error_flags() != 0:
+        raise SystemExit("engine flagged an error during the graph replays")
+    graph = None
+    if e2e:
+        # end to end through the engine API with host buffers (pos in, grad + energy out)
+        pos_host = torch.empty(2 * n, dtype=torch.float32).pin_memory()
+        pos_host.copy_(pos.cpu())
+        grad_host = torch.empty(2 * n, dtype=torch.float32).pin_memory()
+        energy_host = torch.empty(1, dtype=torch.float32).pin_memory()
+
+        def e2e_step():
+            eng.forward_host(cells, pos_host[:n], pos_host[n:], out=outs)
+            eng.backward_host(cells, grad_host[:n], grad_host[n:], grad_x=grad[:n], grad_y=grad[n:])
+            energy_host.copy_(outs["energy"], non_blocking=True)
+
+        K_e2e = max(10, min(K, 200))
+        for _ in range(W):
+            e2e_step()
+        ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K_e2e)]
+        torch.cuda.synchronize(dev)
+        for i in range(K_e2e):
+            ev2[i][0].record(stream)
+            e2e_step()
+            ev2[i][1].record(stream)
+        torch.cuda.synchronize(dev)
+        res["e2e_ms"] = sum(a.elapsed_time(b) for a, b in ev2)
+        res["K_e2e"] = K_e2e
+    res["flags"] = eng.error_flags()
+    eng.close()
+    bins = M * N
+    listings = tile_listings(p) if tiles else 0
+    stage_set = STAGE_BYTES if tiles else STAGE_BYTES_CELL_ORDER
+    res["kernels"] = _kernels(stages, lambda k: algorithmic_bytes(k, p.num_cells, bins, listings, not tiles), peak)
+    kern = res["kernels"]
+    st = ("bin", "scatter", "gather") if tiles else ("scatter", "gather")
+    sc_ga_us = sum(kern[k]["avg_us"] for k in st if k in kern)
+    scb = sc_ga_bytes(p.num_cells, bins, with_convert=tiles)
+    res["sc_ga"] = {"stages": list(st), "us": sc_ga_us, "bytes": scb,
+                    "gbs": scb / sc_ga_us / 1e3, "frac": scb / sc_ga_us / 1e3 / peak,
+                    "bytes_rule": ("48 B/cell + 28 B/bin (scatter 20n+8B, convert 12B, gather 28n+8B)" if tiles else
+                                   "48 B/cell + 16 B/bin (scatter 20n+8B, gather 28n+8B; the conversion runs in "
+                                   "the row pass)")}
+    if tiles:
+        res["sc_ga"]["listings"] = listings
+    else:
+        na = scatter_atomics(p)
+        res["sc_ga"]["atomics"] = na
+        res["sc_ga"]["atomic_floor_us"] = na / (ATOMIC_RATE_GOPS * 1e3)
+        res["sc_ga"]["atomic_rate_source"] = "standalone probe on this pool's B200 (profiles/scatter_atomic_rate.md)"
+    res["step_bytes"] = sum(algorithmic_bytes(k, p.num_cells, bins, listings, not tiles) for k in stage_set)
+    res["launches_per_step"] = 12 if tiles else 5
+    return res
+
+
+def config_item(name, dev, flush, peak, K=200, W=5, path=None):
+    """A single-GPU line item of another BASELINE configuration (the same step
+    and timing as the headline, fewer steps), or of the headline's on another
+    path."""
+    from dreamplacett_framework_b200 import synth
+    p = synth.make_placement(name)
+    r = measure_single(p, dev, K, W, flush, peak, path=path)
+    dom = max(r["kernels"], key=lambda k: r["kernels"][k]["avg_us"])
+    return {"workload": f"{name}: {p.num_movable} movable + {p.num_filler} fillers + {p.num_terminals} fixed "
+                        f"macros, {p.num_bins_x}x{p.num_bins_y} bins; forward + backward, graph replay",
+            "cells": p.num_cells, "bins": [p.num_bins_x, p.num_bins_y], "steps": K,
+            "ms_per_step": r["total_ms"] / K, "iters_per_s": K / (r["total_ms"] / 1000.0),
+            "kernels": r["kernels"], "sc_ga": r["sc_ga"],
+            "roofline": {"bound": "hbm", "kernel": dom, "achieved": r["kernels"][dom]["gbs"], "peak": peak,
+                         "unit": "GB/s", "frac": r["kernels"][dom]["frac"]},
+            "error_flags": r["flags"]}
+
+
+def measure_sharded(args, p, dev, world, rank, K, W, flush, e2e=True):
+    """One grid over `world` GPUs (strong scaling of the same workload): the
+    timed steps replay one captured graph per rank (peer transport) or run
+    eagerly (NCCL); max over ranks is taken by the caller."""
+    import torch
+    import torch.distributed as dist
+    from dreamplacett_framework_b200.sharded import ShardedElectricPotential
+
+    pos, cells, to = _cells_on(p, dev)
+    n = p.num_nodes
     sh = ShardedElectricPotential(p.num_bins_x, p.num_bins_y, p.xl, p.yl, p.xh, p.yh,
                                   float(p.size_x_clamped.max()), device=dev, transport=args.transport)
     sh.set_initial_density(to(p.initial_density_norm()))
@@ -345,17 +556,12 @@ def run_sharded(args, p, dev, world, rank):
         sh.forward(cells, out=outs)
         sh.backward(cells, grad_x=grad[:n], grad_y=grad[n:])
 
-    l2 = getattr(torch.cuda.get_device_properties(dev), "L2_cache_size", 126 * 2 ** 20)
-    flush = torch.empty(max(2 * l2, 256 * 2 ** 20) // 4, dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
-    sampler = ClockSampler(gpu_smi_id(dev))
-    sampler.start()
-    time.sleep(0.5)
-    for _ in range(args.warmup):
+    for _ in range(W):
         step()
     torch.cuda.synchronize(dev)
-    K = args.steps
     graph = None
+    stages = None
     if args.transport == "peer":
         # per-stage times from an eager profiled pass; the timed steps replay one
         # captured graph per rank (the peer signals keep their epoch on the device)
@@ -378,7 +584,7 @@ def run_sharded(args, p, dev, world, rank):
         with torch.cuda.graph(graph, stream=cap):
             step()
         dist.barrier()
-        for _ in range(args.warmup):
+        for _ in range(W):
             graph.replay()
         torch.cuda.synchronize(dev)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
@@ -387,13 +593,13 @@ def run_sharded(args, p, dev, world, rank):
         flush.zero_()
         graph.replay() if graph is not None else step()
 
-    # every rank runs the same number of soak steps (the peer transport's steps wait on one another)
-    n_soak = torch.tensor([0], dtype=torch.int64, device=dev)
-    if rank == 0:
-        ts = time.perf_counter()
-        soak_once()
-        torch.cuda.synchronize(dev)
-        n_soak[0] = max(20, int(1.0 / max(time.perf_counter() - ts, 1e-5)))
+    # every rank runs the same steps (the peer transport's steps wait on one another):
+    # one step on all ranks times a step, and rank 0's count of soak steps goes to all
+    dist.barrier()
+    ts = time.perf_counter()
+    soak_once()
+    torch.cuda.synchronize(dev)
+    n_soak = torch.tensor([max(20, int(1.0 / max(time.perf_counter() - ts, 1e-5)))], dtype=torch.int64, device=dev)
     dist.broadcast(n_soak, 0)
     dist.barrier()
     t_soak0 = time.perf_counter()
@@ -417,80 +623,113 @@ def run_sharded(args, p, dev, world, rank):
     t1 = time.perf_counter()
     if graph is None:
         stages = sh.be.profile_stop()
-    total_ms = sum(a.elapsed_time(b) for a, b in ev)
-    clocks = sampler.summary(t_soak0, t1)
-    clocks["window"] = f"{int(n_soak.item())} untimed steps (about 1 s) right before the timed steps, and the timed steps"
-    # e2e: pinned host pos in, this rank's gradient array and the energy out
-    pos_host = torch.empty(2 * n, dtype=torch.float32).pin_memory()
-    pos_host.copy_(pos.cpu())
-    grad_host = torch.empty(2 * n, dtype=torch.float32).pin_memory()
-    energy_host = torch.empty(1, dtype=torch.float64).pin_memory()
-
-    def e2e_step():
-        pos.copy_(pos_host, non_blocking=True)
-        step()
-        grad_host.copy_(grad, non_blocking=True)
-        energy_host.copy_(sh.energy, non_blocking=True)
-
-    K_e2e = max(10, min(K, 200))
-    for _ in range(args.warmup):
-        e2e_step()
-    ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K_e2e)]
-    dist.barrier()
-    torch.cuda.synchronize(dev)
-    for i in range(K_e2e):
-        ev2[i][0].record(stream)
-        e2e_step()
-        ev2[i][1].record(stream)
-    torch.cuda.synchronize(dev)
-    dist.barrier()
-    e2e_ms = sum(a.elapsed_time(b) for a, b in ev2)
-    sampler.stop()
-    flags = sh.be.error_flags()
-    vals = torch.tensor([total_ms, e2e_ms, float(flags)], dtype=torch.float64, device=dev)
-    dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    total_ms, e2e_ms, flags = float(vals[0]), float(vals[1]), int(vals[2])
-    if rank == 0:
-        peak, peak_kind = load_peaks()
-        bins = p.num_bins_x * p.num_bins_y
-        kern = {}
-        for name, (ms, cnt) in stages.items():
-            if cnt == 0:
-                continue
-            avg_s = ms / cnt / 1000.0
-            b = sharded_bytes(name, p.num_cells, bins, world)
-            kern[name] = {"avg_us": avg_s * 1e6, "launches": cnt, "bytes": b,
-                          "gbs": b / avg_s / 1e9, "frac": b / avg_s / 1e9 / peak}
-        dom = max(kern, key=lambda k: kern[k]["avg_us"])
-        kernel_us = sum(v["avg_us"] for v in kern.values())
-        # our kernels per rank and step: k_band_select, k_scatter, k_row_fwd, k_col, k_row_inv, k_gather
-        # (the gather reuses the forward's selection); the peer transport adds k_push and a
-        # k_signal + k_wait pair after each of its three exchanges
-        launches_per_step = 13 if args.transport == "peer" else 6
-        line = {
-            "metric": METRIC, "value": K / (total_ms / 1000.0), "unit": UNIT, "n_gpus": world, "steps": K,
-            "warmup": args.warmup, "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded stand-in for ISPD-2005 shapes)",
-            "config": workload_config(args, p),
-            "roofline": {"bound": "hbm", "kernel": dom, "achieved": kern[dom]["gbs"], "peak": peak, "unit": "GB/s",
-                         "frac": kern[dom]["frac"], "traffic": None,
-                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"},
-            "kernels": kern,
-            "exchange_us_per_step": 1000.0 * total_ms / K - kernel_us,
-            "e2e": {"value": K_e2e / (e2e_ms / 1000.0), "unit": UNIT, "steps": K_e2e,
-                    "h2d_bytes_per_step": world * 2 * n * 4, "d2h_bytes_per_step": world * (2 * n * 4 + 8),
-                    "path": "each rank: pinned pos[2n] H2D, sharded forward+backward, grad[2n] + energy D2H"},
-            "gpu_launches": launches_per_step * K * world,
-            "cuda_graph": ("timed steps replay one captured graph of forward+backward per rank; per-stage times "
-                           "from eager profiled steps; e2e is eager API calls") if graph is not None else
-                          "eager (NCCL collectives between the kernels)",
-            "clocks": clocks,
-            "error_flags": flags,
-            "wall_s_timed_region": t1 - t0,
-        }
-        print(json.dumps(line), flush=True)
     graph = None
+    total_ms = sum(a.elapsed_time(b) for a, b in ev)
+    res = {"total_ms": total_ms, "stages": stages, "t_soak0": t_soak0, "t0": t0, "t1": t1,
+           "n_soak": int(n_soak.item()), "graph": args.transport == "peer"}
+    if e2e:
+        # pinned host pos in, this rank's gradient array and the energy out
+        pos_host = torch.empty(2 * n, dtype=torch.float32).pin_memory()
+        pos_host.copy_(pos.cpu())
+        grad_host = torch.empty(2 * n, dtype=torch.float32).pin_memory()
+        energy_host = torch.empty(1, dtype=torch.float64).pin_memory()
+
+        def e2e_step():
+            pos.copy_(pos_host, non_blocking=True)
+            step()
+            grad_host.copy_(grad, non_blocking=True)
+            energy_host.copy_(sh.energy, non_blocking=True)
+
+        K_e2e = max(10, min(K, 200))
+        for _ in range(W):
+            e2e_step()
+        ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K_e2e)]
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+        for i in range(K_e2e):
+            ev2[i][0].record(stream)
+            e2e_step()
+            ev2[i][1].record(stream)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        res["e2e_ms"] = sum(a.elapsed_time(b) for a, b in ev2)
+        res["K_e2e"] = K_e2e
+    res["flags"] = sh.be.error_flags()
     sh.close()
+    return res
+
+
+def _max_over_ranks(dev, values):
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(v) for v in values], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t]
+
+
+def run_sharded(args, p, dev, world, rank):
+    """The headline on `world` GPUs, plus the C4 (4096^2, 2.5M cells) item."""
+    from dreamplacett_framework_b200 import synth
+    flush = _flush_buffer(dev)
+    sampler = ClockSampler(gpu_smi_id(dev))
+    sampler.start()
+    time.sleep(0.5)
+    K = args.steps
+    r = measure_sharded(args, p, dev, world, rank, K, args.warmup, flush)
+    total_ms, e2e_ms, flags = _max_over_ranks(dev, [r["total_ms"], r["e2e_ms"], r["flags"]])
+    clocks = sampler.summary(r["t_soak0"], r["t1"])
+    clocks["window"] = f"{r['n_soak']} untimed steps (about 1 s) right before the timed steps, and the timed steps"
+    if int(flags) != 0:
+        # a timed-out wait or a saturated bin: the numbers do not describe a correct run
+        raise SystemExit(f"rank {rank}: engine error flags {int(flags):#x} during the sharded run")
+    c4 = None
+    if not args.no_c4:
+        p4 = synth.make_placement("c4")
+        K4 = max(20, min(K, 200))
+        r4 = measure_sharded(args, p4, dev, world, rank, K4, args.warmup, flush, e2e=False)
+        t4, f4 = _max_over_ranks(dev, [r4["total_ms"], r4["flags"]])
+        c4 = {"workload": f"c4: {p4.num_movable} movable + {p4.num_filler} fillers + {p4.num_terminals} fixed "
+                          f"macros, {p4.num_bins_x}x{p4.num_bins_y} bins, {world} row-band shards",
+              "steps": K4, "ms_per_step": t4 / K4, "iters_per_s": K4 / (t4 / 1000.0), "error_flags": int(f4)}
+    sampler.stop()
+    if rank != 0:
+        return
+    peak, peak_kind = load_peaks()
+    bins = p.num_bins_x * p.num_bins_y
+    listings = tile_listings(p, margin=0)
+    kern = _kernels(r["stages"], lambda k: sharded_bytes(k, p.num_cells, bins, world, listings), peak)
+    dom = max(kern, key=lambda k: kern[k]["avg_us"])
+    kernel_us = sum(v["avg_us"] for v in kern.values())
+    n = p.num_nodes
+    # our kernels per rank and step: k_tile_decide, k_rebuild_count, k_rebuild_scan, k_rebuild_fill,
+    # k_validate, k_esc_scatter, k_tile_scatter, k_row_fwd, k_col, k_row_inv, k_tile_gather,
+    # k_esc_gather; the peer transport adds k_push and a k_signal + k_wait pair after each of
+    # its three exchanges
+    launches_per_step = 19 if args.transport == "peer" else 12
+    line = {
+        "metric": METRIC, "value": K / (total_ms / 1000.0), "unit": UNIT, "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded stand-in for ISPD-2005 shapes)",
+        "config": workload_config(args, p),
+        "roofline": {"bound": "hbm", "kernel": dom, "achieved": kern[dom]["gbs"], "peak": peak, "unit": "GB/s",
+                     "frac": kern[dom]["frac"], "traffic": None,
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"},
+        "kernels": kern,
+        "exchange_us_per_step": 1000.0 * total_ms / K - kernel_us,
+        "e2e": {"value": r["K_e2e"] / (e2e_ms / 1000.0), "unit": UNIT, "steps": r["K_e2e"],
+                "h2d_bytes_per_step": world * 2 * n * 4, "d2h_bytes_per_step": world * (2 * n * 4 + 8),
+                "path": "each rank: pinned pos[2n] H2D, sharded forward+backward, grad[2n] + energy D2H"},
+        "gpu_launches": launches_per_step * K * world,
+        "cuda_graph": ("timed steps replay one captured graph of forward+backward per rank; per-stage times "
+                       "from eager profiled steps; e2e is eager API calls") if r["graph"] else
+                      "eager (NCCL collectives between the kernels)",
+        "clocks": clocks,
+        "error_flags": int(flags),
+        "wall_s_timed_region": r["t1"] - r["t0"],
+    }
+    if c4 is not None:
+        line["c4"] = c4
+    print(json.dumps(line), flush=True)
 
 
 def main():
@@ -503,7 +742,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
     ap.add_argument("--ref-seconds", type=float, default=120.0, help="reference arm time cap")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-loop", action="store_true", help="skip the C5 200-step placement-loop line item")
+    ap.add_argument("--no-loop", action="store_true", help="skip the C5 loop and the wirelength line items")
+    ap.add_argument("--no-configs", action="store_true", help="skip the C1 / C2 / C4 line items")
+    ap.add_argument("--no-c4", action="store_true", help="multi-GPU: skip the C4 item")
     ap.add_argument("--transport", default="peer", choices=["peer", "nccl"],
                     help="multi-GPU exchange: stores into peer memory fused into the kernels, or NCCL collectives")
     args = ap.parse_args()
@@ -516,10 +757,8 @@ def main():
         run_reference(args, p)
         return
 
-    import numpy as np
     import torch
     import torch.distributed as dist
-    from dreamplacett_framework_b200.engine import CellTensors, ElectricPotentialEngine
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -531,206 +770,78 @@ def main():
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-
-    if world > 1:
         try:
             run_sharded(args, p, dev, world, rank)
         finally:
             dist.destroy_process_group()
         return
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    stream = torch.cuda.current_stream(dev)
-    to = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dev)
-    n = p.num_nodes
-    pos = torch.empty(2 * n, dtype=torch.float32, device=dev)
-    pos[:n].copy_(to(p.x))
-    pos[n:].copy_(to(p.y))
-    sx, sy, ox, oy, ratio = (to(a) for a in (p.size_x_clamped, p.size_y_clamped, p.offset_x, p.offset_y, p.ratio))
-    cells = CellTensors(pos[:n], pos[n:], sx, sy, ox, oy, ratio, ranges=p.ranges)
-    eng = ElectricPotentialEngine(p.num_bins_x, p.num_bins_y, p.xl, p.yl, p.xh, p.yh, device=dev)
-    eng.set_initial_density(to(p.initial_density_norm()))
-    M, N = p.num_bins_x, p.num_bins_y
-    outs = {k: torch.empty((M, N), dtype=torch.float32, device=dev)
-            for k in ("density", "potential", "field_x", "field_y")}
-    outs["energy"] = torch.empty(1, dtype=torch.float32, device=dev)
-    grad = torch.zeros(2 * n, dtype=torch.float32, device=dev)
-
-    def step():
-        eng.forward(cells, out=outs)
-        eng.backward(cells, grad_x=grad[:n], grad_y=grad[n:])
-
-    l2 = getattr(torch.cuda.get_device_properties(dev), "L2_cache_size", 126 * 2 ** 20)
-    flush = torch.empty(max(2 * l2, 256 * 2 ** 20) // 4, dtype=torch.float32, device=dev)
-
+    flush = _flush_buffer(dev)
     sampler = ClockSampler(gpu_smi_id(dev))
     sampler.start()
     time.sleep(0.5)
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize(dev)
-    if eng.error_flags() != 0:
-        raise SystemExit("engine flagged non-finite cells during warm-up")
-
+    peak, peak_kind = load_peaks()
     K = args.steps
-    # per-kernel durations: an eager pass with CUDA events between the engine's kernels
-    K_prof = max(10, min(K, 500))
-    eng.profile_start(2 * K_prof)  # forward + backward per step
-    for _ in range(K_prof):
-        flush.zero_()
-        step()
-    torch.cuda.synchronize(dev)
-    stages = eng.profile_stop()
-
-    # the timed steps replay one CUDA graph of forward + backward (the engine's calls are
-    # stream-ordered and allocation-free, so they capture as they are)
-    graph = torch.cuda.CUDAGraph()
-    cap = torch.cuda.Stream(dev)
-    cap.wait_stream(stream)
-    with torch.cuda.stream(cap):
-        step()  # one eager call on the capture stream before capture
-    stream.wait_stream(cap)
-    torch.cuda.synchronize(dev)
-    with torch.cuda.graph(graph, stream=cap):
-        step()
-    for _ in range(args.warmup):
-        graph.replay()
-    torch.cuda.synchronize(dev)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
-
-    def soak_once():
-        flush.zero_()
-        graph.replay()
-
-    t_soak0 = clock_soak(soak_once, dev)
-    barrier()
-    torch.cuda.synchronize(dev)
-    t_wall0 = time.perf_counter()
-    for i in range(K):
-        flush.zero_()
-        ev[i][0].record(stream)
-        graph.replay()
-        ev[i][1].record(stream)
-    torch.cuda.synchronize(dev)
-    barrier()
-    t_wall1 = time.perf_counter()
-    step_ms = [a.elapsed_time(b) for a, b in ev]
-    total_ms = sum(step_ms)
-    clocks = sampler.summary(t_soak0, t_wall1)
+    r = measure_single(p, dev, K, args.warmup, flush, peak, e2e=True)
+    clocks = sampler.summary(r["t_soak0"], r["t1"])
     clocks["window"] = "1 s of untimed graph replays right before the timed steps, and the timed steps"
-    if eng.error_flags() != 0:
-        raise SystemExit("engine flagged an error during the graph replays")
-
-    # --- end to end through the engine API with host buffers (pos in, grad + energy out)
-    pos_host = torch.empty(2 * n, dtype=torch.float32).pin_memory()
-    pos_host.copy_(pos.cpu())
-    grad_host = torch.empty(2 * n, dtype=torch.float32).pin_memory()
-    energy_host = torch.empty(1, dtype=torch.float32).pin_memory()
-
-    def e2e_step():
-        # host positions in and host gradients out, each copy pipelined with the cell kernels
-        eng.forward_host(cells, pos_host[:n], pos_host[n:], out=outs)
-        eng.backward_host(cells, grad_host[:n], grad_host[n:], grad_x=grad[:n], grad_y=grad[n:])
-        energy_host.copy_(outs["energy"], non_blocking=True)
-
-    K_e2e = max(10, min(K, 200))
-    for _ in range(args.warmup):
-        e2e_step()
-    ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K_e2e)]
-    barrier()
-    torch.cuda.synchronize(dev)
-    for i in range(K_e2e):
-        ev2[i][0].record(stream)
-        e2e_step()
-        ev2[i][1].record(stream)
-    torch.cuda.synchronize(dev)
-    barrier()
-    e2e_ms = sum(a.elapsed_time(b) for a, b in ev2)
     sampler.stop()
-    flags = eng.error_flags()
-
-    # --- max over ranks
-    vals = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    total_ms, e2e_ms = float(vals[0]), float(vals[1])
-
-    if rank == 0:
-        peak, peak_kind = load_peaks()
-        bins = M * N
-        kern = {}
-        for name, (ms, cnt) in stages.items():
-            if cnt == 0:
-                continue
-            avg_s = ms / cnt / 1000.0
-            b = algorithmic_bytes(name, p.num_cells, bins)
-            kern[name] = {"avg_us": avg_s * 1e6, "launches": cnt, "bytes": b,
-                          "gbs": b / avg_s / 1e9, "frac": b / avg_s / 1e9 / peak}
-        dom = max(kern, key=lambda k: kern[k]["avg_us"])
-        roof = {"bound": "hbm", "kernel": dom, "achieved": kern[dom]["gbs"], "peak": peak, "unit": "GB/s",
-                "frac": kern[dom]["frac"],
-                "traffic": NCU_TRAFFIC_C3.get(dom) if args.config == "c3" else None, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"}
-        if "scatter" in kern:
-            # the scatter's own ceiling: one 64-bit atomic add per (cell, bin) at the probed rate
-            na = scatter_atomics(p)
-            floor_us = na / (ATOMIC_RATE_GOPS * 1e3)
-            kern["scatter"]["atomic_bound"] = {
-                "atomics": na, "rate_gops": ATOMIC_RATE_GOPS, "floor_us": floor_us,
-                "frac": floor_us / kern["scatter"]["avg_us"],
-                "rate_source": "standalone probe on this pool's B200 (profiles/scatter_atomic_rate.md)"}
-        step_bytes = sum(algorithmic_bytes(k, p.num_cells, bins) for k in STAGE_BYTES)
-        value = world * K / (total_ms / 1000.0)
-        line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": args.warmup,
-            "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic (seeded stand-in for ISPD-2005 shapes)",
-            "config": workload_config(args, p),
-            "roofline": roof,
-            "kernels": kern,
-            "step_algorithmic_bytes": step_bytes,
-            "step_gbs": step_bytes / (total_ms / K / 1000.0) / 1e9,
-            "e2e": {"value": world * K_e2e / (e2e_ms / 1000.0), "unit": UNIT, "steps": K_e2e,
-                    "h2d_bytes_per_step": 2 * n * 4, "d2h_bytes_per_step": 2 * n * 4 + 4,
-                    "path": "engine API with host buffers: epb_forward_host (the scatter reads pinned pos[2n] "
-                            "over PCIe), epb_backward_host (the gather stores grad[2n] to pinned host memory), "
-                            "energy D2H"},
-            "gpu_launches": 5 * K,
-            "cuda_graph": "timed steps replay one captured graph of forward+backward; per-kernel "
-                          f"times from {K_prof} eager profiled steps; e2e is eager API calls",
-            "clocks": clocks,
-            "error_flags": flags,
-            "wall_s_timed_region": t_wall1 - t_wall0,
-        }
-        if world == 1 and not args.no_loop:
-            from dreamplacett_framework_b200.placement import DensityDescent
-            p5 = synth.make_placement("c5")
-            with DensityDescent(p5, device=dev) as loop:
-                r5 = loop.run(200, graph=True)
-            line["placement_loop"] = {
-                "workload": f"C5: {p5.num_cells} cells, {p5.num_bins_x}x{p5.num_bins_y} bins, 200 normalised "
-                            "density-descent steps (fused overflow + forward with one scatter, backward, step "
-                            "per iteration; one CUDA graph per step, no host reads inside the loop)",
-                "ms_per_step": r5["ms"] / 200, "steps_per_s": 200 * 1000.0 / r5["ms"],
-                "overflow_first": float(r5["overflow"][0]), "overflow_final": float(r5["overflow"][-1]),
-                "max_density_final": float(r5["max_density"][-1]), "error_flags": r5["flags"]}
-        if world == 1 and not args.no_loop:
-            line["wirelength"] = wirelength_item(p, dev, flush, peak)
-        if world == 1 and not args.no_cpu_baseline:
-            nthreads = os.cpu_count() or 1
-            cstep = cpu_step_factory(p, nthreads)
-            cn, cel = time_cpu(cstep, max_seconds=args.cpu_seconds, warmup=1)
-            line["cpu_baseline"] = {
-                "value": cn / cel, "unit": UNIT, "cores": nthreads, "kind": "port",
-                "sample": f"{cn} full {args.config} steps in {cel:.1f} s (oracle port: OpenMP int64 density, "
-                          f"scipy.fft fp32 DCT chain, OpenMP gather), CPU {cpu_model()}"}
-        print(json.dumps(line), flush=True)
-    eng.close()
-    if world > 1:
-        dist.destroy_process_group()
+    n = p.num_nodes
+    kern = r["kernels"]
+    dom = max(kern, key=lambda k: kern[k]["avg_us"])
+    roof = {"bound": "hbm", "kernel": dom, "achieved": kern[dom]["gbs"], "peak": peak, "unit": "GB/s",
+            "frac": kern[dom]["frac"], "traffic": NCU_TRAFFIC_C3.get(dom) if args.config == "c3" else None,
+            "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"}
+    total_ms = r["total_ms"]
+    line = {
+        "metric": METRIC, "value": K / (total_ms / 1000.0), "unit": UNIT, "n_gpus": 1, "steps": K,
+        "warmup": args.warmup, "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded stand-in for ISPD-2005 shapes)",
+        "config": workload_config(args, p),
+        "roofline": roof,
+        "kernels": kern,
+        "sc_ga": r["sc_ga"],
+        "step_algorithmic_bytes": r["step_bytes"],
+        "step_gbs": r["step_bytes"] / (total_ms / K / 1000.0) / 1e9,
+        "e2e": {"value": r["K_e2e"] / (r["e2e_ms"] / 1000.0), "unit": UNIT, "steps": r["K_e2e"],
+                "h2d_bytes_per_step": 2 * n * 4, "d2h_bytes_per_step": 2 * n * 4 + 4,
+                "path": "engine API with host buffers: epb_forward_host (the scatter reads pinned pos[2n] over "
+                        "PCIe), epb_backward_host (the gather stores grad[2n] to pinned host memory), energy D2H"},
+        # per step (the cell-order path): k_scatter, k_row_fwd, k_col, k_row_inv (forward), k_gather (backward)
+        "gpu_launches": r["launches_per_step"] * K,
+        "cuda_graph": "timed steps replay one captured graph of forward+backward; per-kernel "
+                      f"times from {r['K_prof']} eager profiled steps; e2e is eager API calls",
+        "clocks": clocks,
+        "error_flags": r["flags"],
+        "wall_s_timed_region": r["t1"] - r["t0"],
+    }
+    if not args.no_configs:
+        line["configs"] = {name: config_item(name, dev, flush, peak) for name in ("c1", "c2", "c4")
+                           if name != args.config}
+        # the same workload through the cell tiles (EPB_CONFIG_TILES), for comparison
+        line["tiles"] = config_item(args.config, dev, flush, peak, path="tiles")
+    if not args.no_loop:
+        from dreamplacett_framework_b200.placement import DensityDescent
+        p5 = synth.make_placement("c5")
+        with DensityDescent(p5, device=dev) as loop:
+            r5 = loop.run(200, graph=True)
+        line["placement_loop"] = {
+            "workload": f"C5: {p5.num_cells} cells, {p5.num_bins_x}x{p5.num_bins_y} bins, 200 normalised "
+                        "density-descent steps (fused overflow + forward with one scatter, backward, step per "
+                        "iteration; one CUDA graph per step, no host reads inside the loop)",
+            "ms_per_step": r5["ms"] / 200, "steps_per_s": 200 * 1000.0 / r5["ms"],
+            "overflow_first": float(r5["overflow"][0]), "overflow_final": float(r5["overflow"][-1]),
+            "max_density_final": float(r5["max_density"][-1]), "error_flags": r5["flags"]}
+        line["wirelength"] = wirelength_item(p, dev, flush, peak)
+    if not args.no_cpu_baseline:
+        nthreads = os.cpu_count() or 1
+        cstep = cpu_step_factory(p, nthreads)
+        cn, cel = time_cpu(cstep, max_seconds=args.cpu_seconds, warmup=1)
+        line["cpu_baseline"] = {
+            "value": cn / cel, "unit": UNIT, "cores": nthreads, "kind": "port",
+            "sample": f"{cn} full {args.config} steps in {cel:.1f} s (oracle port: OpenMP int64 density, "
+                      f"scipy.fft fp32 DCT chain, OpenMP gather), CPU {cpu_model()}"}
+    print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":

@@ -45,7 +45,10 @@ EXPORTS = (
 NOALLOC_MAX_BINS = 1024 * 1024
 
 # Stage indices of epb_profile_stop (EPB_STAGE_* in include/epb.h).
-STAGES = ("scatter", "row_fwd", "column", "row_inv", "gather")
+STAGES = ("scatter", "row_fwd", "column", "row_inv", "gather", "bin")
+# epb_config.flags: the cell-order scatter / gather, or the cell tiles.
+CONFIG_CELL_ORDER = 0x1
+CONFIG_TILES = 0x2
 
 
 class EpbConfig(ctypes.Structure):

@@ -17,6 +17,7 @@
 
 #include "../../include/epb.h"
 #include "epb_kernels.cuh"
+#include "tile_kernels.cuh"
 #include "wirelength.cuh"
 #include "placement_kernels.cuh"
 
@@ -80,6 +81,25 @@ struct epb_handle {
     unsigned char* peer_sig[kMaxShards] = {nullptr};
     double* energy_total = nullptr;
     long long max_polls = 40000000;  // bounded waits: ~5 s of 128 ns polls
+    // cell tiles (whole-grid handles without EPB_CONFIG_CELL_ORDER): the lists,
+    // kept across calls (tile_prepare), and the cell view they were made from
+    bool cell_order = false;
+    TileGeom tg{};
+    TileBins tb{};
+    int ntiles = 0;
+    int64_t tb_cells = 0;       // cells the buffers hold (escape lists, grows)
+    int64_t tb_cap = 0;         // listing capacity = kMaxTilesPerCell * tb_cells
+    int tb_items = 0;           // work-item capacity
+    bool tb_force = true;       // the next list maintenance must rebuild (new buffers or cell arrays)
+    bool tb_stale = false;      // epb_descent_step moved the cells since the lists were last validated
+    float* rho = nullptr;       // [M*N] density when the caller passes none
+    unsigned tile_grid = 1;     // persistent CTAs of k_tile_scatter / k_tile_gather
+    unsigned tile_grid_ovf = 1; // persistent CTAs of k_tile_scatter<true> (two limb sets)
+    unsigned long long* esc_grid0 = nullptr;  // [M*N] escape sums of the overflow cells (lazy)
+    double* tile_ovf_part = nullptr;          // [2 * ntiles]
+    unsigned* tile_ovf_counter = nullptr;
+    bool tb_valid = false;
+    CellView tb_key{};
     // stage timing (epb_profile_start/stop)
     struct Span { int stage, a, b; };
     bool prof_on = false;
@@ -199,7 +219,10 @@ void free_all(epb_handle* h) {
     void* ptrs[] = {h->grid, h->grid2, h->init, h->t1, h->g, h->fxy, h->twM, h->qwM,
                     h->twN, h->qwN, h->partials, h->counter, h->energy_d, h->flags,
                     h->ovf_partials, h->ovf_counter, h->linf_bits, h->sel_list, h->sel_count,
-                    h->own_list, h->own_count};
+                    h->own_list, h->own_count, h->rho, h->tb.cnt, h->tb.cur, h->tb.start, h->tb.nown,
+                    h->tb.first_item, h->tb.items, h->tb.arrive, h->tb.part, h->tb.meta, h->tb.stat, h->tb.key,
+                    h->tb.geo, h->tb.bins, h->tb.esc_dyn, h->tb.esc_static, h->tb.esc_grid, h->esc_grid0,
+                    h->tile_ovf_part, h->tile_ovf_counter};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     for (int q = 0; q < kMaxShards; ++q) {
@@ -500,8 +523,12 @@ int scatter_into(epb_handle* h, const CellView& v0, cudaStream_t st, long long* 
 
 // Gather of a shard's own cells (first bin row in the band) from fields holding
 // rows [row0, row0 + RB + halo).
+int tile_gather(epb_handle* h, const CellView& v, const float2* fxy, int halo, int owned_only, const float* grad_out,
+                float* grad_x, float* grad_y, cudaStream_t st);
+
 int shard_gather(epb_handle* h, const CellView& v0, const float2* fxy, int halo, const float* grad_out,
                  float* grad_x, float* grad_y, cudaStream_t st) {
+    if (!h->cell_order) return tile_gather(h, v0, fxy, halo, 1, grad_out, grad_x, grad_y, st);
     CellView v = v0;
     unsigned blocks = cell_blocks(v.n);
     if (h->P > 1) {
@@ -517,6 +544,155 @@ int shard_gather(epb_handle* h, const CellView& v0, const float2* fxy, int halo,
     k_gather<false><<<blocks, 256, 0, st>>>(v, geom(h), fxy, nullptr, nullptr, h->row0, h->row0 + h->RB, halo, 1, grad_out,
                                      grad_x, grad_y, h->flags);
     EPB_LAUNCHED(h, "k_gather launch");
+    return EPB_OK;
+}
+
+// ----- cell tiles ------------------------------------------------------------
+
+// Bins the listings are widened by on a whole grid: a cell may move this far
+// between rebuilds of the lists (a shard rebuilds its band's lists every call).
+constexpr int kTileMargin = kGatherLo;
+
+unsigned fixed_blocks(const epb_handle* h) { return (unsigned)(8 * h->sms); }
+
+// Listing and escape buffers for n cells (grown when more cells come; that
+// call synchronises the stream and allocates, and the lists are rebuilt).
+int tile_reserve(epb_handle* h, int64_t n, cudaStream_t st) {
+    if (n <= h->tb_cells) return EPB_OK;
+    if (n > (int64_t)kNodeMask / kMaxTilesPerCell) return fail(h, EPB_EINVAL, "too many cells for the tile lists");
+    EPB_CUDA(h, cudaStreamSynchronize(st));
+    void** bufs[] = {(void**)&h->tb.stat, (void**)&h->tb.key, (void**)&h->tb.geo, (void**)&h->tb.bins,
+                     (void**)&h->tb.esc_dyn, (void**)&h->tb.esc_static, (void**)&h->tb.items, (void**)&h->tb.part};
+    for (void** b : bufs) {
+        if (*b) cudaFree(*b);
+        *b = nullptr;
+    }
+    h->tb_cells = 0;
+    h->tb_valid = false;
+    const int64_t cap = (int64_t)kMaxTilesPerCell * n;
+    const int64_t items = h->ntiles + cap / kChunk + 1;
+    if (int rc = dev_alloc(h, &h->tb.stat, (size_t)cap)) return rc;
+    if (int rc = dev_alloc(h, &h->tb.key, (size_t)cap)) return rc;
+    if (int rc = dev_alloc(h, &h->tb.geo, (size_t)cap)) return rc;
+    if (int rc = dev_alloc(h, &h->tb.bins, (size_t)cap)) return rc;
+    if (int rc = dev_alloc(h, &h->tb.esc_dyn, (size_t)n)) return rc;
+    if (int rc = dev_alloc(h, &h->tb.esc_static, (size_t)n)) return rc;
+    if (int rc = dev_alloc(h, &h->tb.items, (size_t)items)) return rc;
+    if (int rc = dev_alloc(h, &h->tb.part, (size_t)items * 2 * kTileBinsMax)) return rc;
+    h->tb_cells = n;
+    h->tb_cap = cap;
+    h->tb_items = (int)items;
+    h->tb_force = true;
+    return EPB_OK;
+}
+
+bool same_view(const CellView& a, const CellView& b) {
+    return same_cells(a, b) && a.y == b.y && a.oy == b.oy && a.sy == b.sy && a.ratio == b.ratio;
+}
+
+// The list maintenance of a forward: rebuild when needed (on the device: the
+// kernels return at once otherwise), then validate the lists against the
+// positions now.  A view other than the lists' forces a rebuild.
+int tile_prepare(epb_handle* h, const CellView& v, cudaStream_t st) {
+    if (int rc = tile_reserve(h, std::max<int64_t>(v.n, 1), st)) return rc;
+    for (int64_t e : {v.b0 + v.n0, v.b1 + (v.n - v.n0)})
+        if (e > (int64_t)kNodeMask) return fail(h, EPB_EINVAL, "node indices must be below 2^30");
+    // a shard rebuilds its band's lists every call: a cell may have moved in from
+    // another band, which this band's lists cannot see
+    const bool force = h->P > 1 || h->tb_force || !h->tb_valid || !same_view(h->tb_key, v);
+    k_tile_decide<<<1, 32, 0, st>>>(h->tb, force ? 1 : 0);
+    EPB_LAUNCHED(h, "k_tile_decide launch");
+    const GridGeom g = geom(h);
+    k_rebuild_count<<<fixed_blocks(h), 256, 0, st>>>(v, g, h->tg, h->tb, h->flags);
+    EPB_LAUNCHED(h, "k_rebuild_count launch");
+    k_rebuild_scan<<<1, kScanThreads, 0, st>>>(h->ntiles, h->tb);
+    EPB_LAUNCHED(h, "k_rebuild_scan launch");
+    k_rebuild_fill<<<fixed_blocks(h), 256, 0, st>>>(v, g, h->tg, h->tb);
+    EPB_LAUNCHED(h, "k_rebuild_fill launch");
+    k_validate<<<fixed_blocks(h), 256, 0, st>>>(v, g, h->tb);
+    EPB_LAUNCHED(h, "k_validate launch");
+    h->tb_force = false;
+    h->tb_stale = false;
+    h->tb_key = v;
+    h->tb_valid = true;
+    return EPB_OK;
+}
+
+// Overflow request of a tile scatter: the overflow cells are the nodes of the
+// two ranges set0; their map's overflow terms go to out[2].
+struct TileOverflow {
+    int64_t set0[4];
+    float target;
+    double* out;
+};
+
+// Density of the listed cells (plus the initial density) into rho [band rows * N]
+// (nullable with an overflow request).
+int tile_scatter(epb_handle* h, const CellView& v, float* rho, cudaStream_t st, const TileOverflow* ovf = nullptr) {
+    if (ovf && !h->esc_grid0) {
+        // scratch of the overflow variant (allocated once; the first call synchronises)
+        EPB_CUDA(h, cudaStreamSynchronize(st));
+        const size_t MN = (size_t)h->RB * h->N;
+        if (int rc = dev_alloc(h, &h->esc_grid0, MN)) return rc;
+        if (int rc = dev_alloc(h, &h->tile_ovf_part, 2 * (size_t)h->ntiles)) return rc;
+        if (int rc = dev_alloc(h, &h->tile_ovf_counter, 1)) return rc;
+        EPB_CUDA(h, cudaMemset(h->esc_grid0, 0, MN * sizeof(unsigned long long)));
+        EPB_CUDA(h, cudaMemset(h->tile_ovf_counter, 0, sizeof(unsigned)));
+    }
+    const int64_t* s0 = ovf ? ovf->set0 : nullptr;
+    k_esc_scatter<<<(unsigned)(2 * h->sms), 256, 0, st>>>(v, geom(h), h->tg, ldexpf(1.0f, h->S), h->tb,
+                                                          ovf ? h->esc_grid0 : nullptr, s0 ? s0[0] : 0, s0 ? s0[1] : 0,
+                                                          s0 ? s0[2] : 0, s0 ? s0[3] : 0);
+    EPB_LAUNCHED(h, "k_esc_scatter launch");
+    TileScatterArgs a;
+    a.g = geom(h);
+    a.t = h->tg;
+    a.b = h->tb;
+    a.qscale = ldexpf(1.0f, h->S);
+    a.dscale = h->dscale;
+    a.init = h->has_init ? h->init : nullptr;
+    a.rho = rho;
+    a.flags = h->flags;
+    if (ovf) {
+        for (int k = 0; k < 4; ++k) a.set0[k] = ovf->set0[k];
+        a.target = ovf->target;
+        a.bin_area = (double)h->bsx * (double)h->bsy;
+        a.ovf_part = h->tile_ovf_part;
+        a.ovf_counter = h->tile_ovf_counter;
+        a.ovf_out = ovf->out;
+        a.esc_grid0 = h->esc_grid0;
+        k_tile_scatter<true><<<h->tile_grid_ovf, kTileThreads, 0, st>>>(a);
+    } else {
+        k_tile_scatter<false><<<h->tile_grid, kTileThreads, 0, st>>>(a);
+    }
+    EPB_LAUNCHED(h, "k_tile_scatter launch");
+    return EPB_OK;
+}
+
+// Gradients of the cells of v from the interleaved fields fxy (rows [row0,
+// row0 + RB + halo)): the positions of the last forward on the same cell
+// arrays; other arrays are listed first.  owned_only: only the cells whose
+// first bin row is in the band are written (a shard).
+int tile_gather(epb_handle* h, const CellView& v, const float2* fxy, int halo, int owned_only, const float* grad_out,
+                float* grad_x, float* grad_y, cudaStream_t st) {
+    if (!h->tb_valid || h->tb_stale || !same_view(h->tb_key, v))
+        if (int rc = tile_prepare(h, v, st)) return rc;
+    TileGatherArgs a;
+    a.g = geom(h);
+    a.t = h->tg;
+    a.b = h->tb;
+    a.fxy = fxy;
+    a.halo = halo;
+    a.grad_out = grad_out;
+    a.grad_x = grad_x;
+    a.grad_y = grad_y;
+    a.flags = h->flags;
+    EPB_CUDA(h, cudaMemsetAsync(h->tb.meta + kMetaWorkGather, 0, sizeof(int), st));
+    k_tile_gather<<<h->tile_grid, kTileThreads, 0, st>>>(a);
+    EPB_LAUNCHED(h, "k_tile_gather launch");
+    k_esc_gather<<<(unsigned)(2 * h->sms), 256, 0, st>>>(v, geom(h), h->tg, h->tb, fxy, halo, owned_only, grad_out,
+                                                         grad_x, grad_y, h->flags);
+    EPB_LAUNCHED(h, "k_esc_gather launch");
     return EPB_OK;
 }
 
@@ -552,7 +728,9 @@ int create_handle(const epb_config* cfg, int P, int p, epb_handle** out) {
     if (!(cfg->xh > cfg->xl) || !(cfg->yh > cfg->yl) || !std::isfinite(cfg->xl) || !std::isfinite(cfg->xh) ||
         !std::isfinite(cfg->yl) || !std::isfinite(cfg->yh))
         return EPB_EINVAL;
-    if (cfg->flags != 0 || cfg->fixed_point_bits > 60) return EPB_EINVAL;
+    if ((cfg->flags & ~(EPB_CONFIG_CELL_ORDER | EPB_CONFIG_TILES)) != 0 ||
+        (cfg->flags & EPB_CONFIG_CELL_ORDER) && (cfg->flags & EPB_CONFIG_TILES) || cfg->fixed_point_bits > 60)
+        return EPB_EINVAL;
     // shards: P a power of two, each band at least 16 rows / columns
     if (P < 1 || p < 0 || p >= P || (P & (P - 1)) != 0) return EPB_EINVAL;
     if (cfg->num_bins_x / P < 16 || cfg->num_bins_y / P < 16) return EPB_EINVAL;
@@ -575,6 +753,16 @@ int create_handle(const epb_config* cfg, int P, int p, epb_handle** out) {
         h->S = 63 - ib;
     }
     h->dscale = std::ldexp(1.0, -h->S) / ((double)h->bsx * (double)h->bsy);
+    // whole grid: cell order unless the tiles are asked for; shard: tiles unless cell order is
+    h->cell_order = P == 1 ? (cfg->flags & EPB_CONFIG_TILES) == 0 : (cfg->flags & EPB_CONFIG_CELL_ORDER) != 0;
+    h->tg.ltx = ilog2(std::min(kTileMax, h->RB));
+    h->tg.lty = ilog2(std::min(kTileMax, h->N));
+    h->tg.ntx = h->RB >> h->tg.ltx;
+    h->tg.nty = h->N >> h->tg.lty;
+    h->tg.row0 = h->row0;
+    h->tg.rows = h->RB;
+    h->tg.margin = P == 1 ? kTileMargin : 0;
+    h->ntiles = h->tg.ntx * h->tg.nty;
 
     DeviceGuard guard(h->dev);
     if (!guard.ok) { delete h; return EPB_ECUDA; }
@@ -600,6 +788,17 @@ int create_handle(const epb_config* cfg, int P, int p, epb_handle** out) {
     if (!rc) rc = dev_alloc(h, &h->ovf_partials, 2 * (size_t)kOvfMaxBlocks);
     if (!rc) rc = dev_alloc(h, &h->ovf_counter, 1);
     if (!rc) rc = dev_alloc(h, &h->linf_bits, 1);
+    if (!h->cell_order) {
+        if (!rc) rc = dev_alloc(h, &h->tb.cnt, (size_t)h->ntiles * kCounterStride);
+        if (!rc) rc = dev_alloc(h, &h->tb.cur, (size_t)h->ntiles * kCounterStride);
+        if (!rc) rc = dev_alloc(h, &h->tb.start, (size_t)h->ntiles + 1);
+        if (!rc) rc = dev_alloc(h, &h->tb.nown, (size_t)h->ntiles);
+        if (!rc) rc = dev_alloc(h, &h->tb.first_item, (size_t)h->ntiles);
+        if (!rc) rc = dev_alloc(h, &h->tb.arrive, (size_t)h->ntiles);
+        if (!rc) rc = dev_alloc(h, &h->tb.meta, (size_t)kMetaWords);
+        if (!rc) rc = dev_alloc(h, &h->tb.esc_grid, band);
+        if (!rc) rc = dev_alloc(h, &h->rho, band);
+    }
     if (rc) { free_all(h); delete h; return rc; }
 
     std::vector<float2> tw, qw;
@@ -615,6 +814,12 @@ int create_handle(const epb_config* cfg, int P, int p, epb_handle** out) {
     if (e == cudaSuccess) e = cudaMemset(h->ovf_counter, 0, sizeof(unsigned));
     if (e == cudaSuccess) e = cudaMemset(h->flags, 0, sizeof(unsigned));
     if (e == cudaSuccess) e = cudaMemset(h->energy_d, 0, sizeof(double));
+    if (!h->cell_order) {
+        if (e == cudaSuccess) e = cudaMemset(h->tb.cnt, 0, (size_t)h->ntiles * kCounterStride * sizeof(int));
+        if (e == cudaSuccess) e = cudaMemset(h->tb.arrive, 0, (size_t)h->ntiles * sizeof(unsigned));
+        if (e == cudaSuccess) e = cudaMemset(h->tb.meta, 0, kMetaWords * sizeof(int));
+        if (e == cudaSuccess) e = cudaMemset(h->tb.esc_grid, 0, band * sizeof(unsigned long long));
+    }
     int sms = 0, occ0 = 0, occ1 = 0;
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, h->dev);
     h->sms = std::max(1, sms);
@@ -622,6 +827,12 @@ int create_handle(const epb_config* cfg, int P, int p, epb_handle** out) {
     if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ1, k_gather<true>, 256, 0);
     h->gather_grid[0] = (unsigned)std::max(1, sms * occ0 * EPB_GATHER_WAVES);
     h->gather_grid[1] = (unsigned)std::max(1, sms * occ1 * EPB_GATHER_WAVES);
+    int occ_ts = 0, occ_tg = 0, occ_to = 0;
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_ts, k_tile_scatter<false>, kTileThreads, 0);
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_tg, k_tile_gather, kTileThreads, 0);
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_to, k_tile_scatter<true>, kTileThreads, 0);
+    h->tile_grid = (unsigned)std::max(1, sms * std::max(1, std::min(occ_ts, occ_tg)));
+    h->tile_grid_ovf = (unsigned)std::max(1, sms * std::max(1, occ_to));
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) { free_all(h); delete h; return EPB_ECUDA; }
     *out = h;
@@ -684,6 +895,19 @@ int epb_forward(epb_handle* h, const epb_cells* cells, epb_stream stream, float*
     if (int rc = make_view(h, cells, v)) return rc;
     DeviceGuard guard(h->dev);
     cudaStream_t st = (cudaStream_t)stream;
+    if (!h->cell_order) {
+        // cell tiles: bin, then every tile writes its finished density bins
+        ProfCall pc(h, st);
+        pc.begin();
+        if (int rc = tile_prepare(h, v, st)) return rc;
+        pc.end_stage(EPB_STAGE_BIN);
+        float* rho = density ? density : h->rho;
+        if (int rc = tile_scatter(h, v, rho, st)) return rc;
+        pc.end_stage(EPB_STAGE_SCATTER);
+        if (int rc = launch_row_fwd(h, false, rho, nullptr, blocked(h->t1, 0, 1), 0, st)) return rc;
+        pc.end_stage(EPB_STAGE_ROW_FWD);
+        return solve_from_t1(h, st, potential, field_x, field_y, energy, pc);
+    }
     if (h->grid_dirty) {
         EPB_CUDA(h, cudaMemsetAsync(h->grid, 0, (size_t)h->M * h->N * sizeof(long long), st));
         h->grid_dirty = false;
@@ -711,6 +935,11 @@ int epb_backward(epb_handle* h, const epb_cells* cells, const float* grad_out, e
     DeviceGuard guard(h->dev);
     ProfCall pc(h, (cudaStream_t)stream);
     pc.begin();
+    if (!h->cell_order) {
+        if (int rc = tile_gather(h, v, h->fxy, 0, 0, grad_out, grad_x, grad_y, (cudaStream_t)stream)) return rc;
+        pc.end_stage(EPB_STAGE_GATHER);
+        return EPB_OK;
+    }
     k_gather<false><<<gather_blocks(h, v.n, false), 256, 0, (cudaStream_t)stream>>>(v, geom(h), h->fxy, nullptr, nullptr, 0, h->M, 0, 0,
                                                                grad_out, grad_x, grad_y, h->flags);
     EPB_LAUNCHED(h, "k_gather launch");
@@ -795,6 +1024,28 @@ int epb_forward_host(epb_handle* h, const epb_cells* cells, const float* host_x,
     void *hx = nullptr, *hy = nullptr;
     if (int rc = host_device_ptr(h, host_x, &hx)) return rc;
     if (int rc = host_device_ptr(h, host_y, &hy)) return rc;
+    if (!h->cell_order) {
+        // the positions of the two node ranges are copied into cells->x / cells->y,
+        // then the device path runs on them
+        ProfCall pc(h, st);
+        pc.begin();
+        const int64_t rb[2][2] = {{v.b0, v.n0}, {v.b1, v.n - v.n0}};
+        for (const auto& r : rb) {
+            if (r[1] == 0) continue;
+            EPB_CUDA(h, cudaMemcpyAsync(const_cast<float*>(cells->x) + r[0], host_x + r[0], (size_t)r[1] * sizeof(float),
+                                        cudaMemcpyHostToDevice, st));
+            EPB_CUDA(h, cudaMemcpyAsync(const_cast<float*>(cells->y) + r[0], host_y + r[0], (size_t)r[1] * sizeof(float),
+                                        cudaMemcpyHostToDevice, st));
+        }
+        if (int rc = tile_prepare(h, v, st)) return rc;
+        pc.end_stage(EPB_STAGE_BIN);
+        float* rho = density ? density : h->rho;
+        if (int rc = tile_scatter(h, v, rho, st)) return rc;
+        pc.end_stage(EPB_STAGE_SCATTER);
+        if (int rc = launch_row_fwd(h, false, rho, nullptr, blocked(h->t1, 0, 1), 0, st)) return rc;
+        pc.end_stage(EPB_STAGE_ROW_FWD);
+        return solve_from_t1(h, st, potential, field_x, field_y, energy, pc);
+    }
     if (h->grid_dirty) {
         EPB_CUDA(h, cudaMemsetAsync(h->grid, 0, (size_t)h->M * h->N * sizeof(long long), st));
         h->grid_dirty = false;
@@ -836,6 +1087,20 @@ int epb_backward_host(epb_handle* h, const epb_cells* cells, const float* grad_o
     if (v.n == 0) return EPB_OK;
     ProfCall pc(h, st);
     pc.begin();
+    if (!h->cell_order) {
+        // gradients into the device arrays, then each node range to host memory
+        if (int rc = tile_gather(h, v, h->fxy, 0, 0, grad_out, grad_x, grad_y, st)) return rc;
+        const int64_t rb[2][2] = {{v.b0, v.n0}, {v.b1, v.n - v.n0}};
+        for (const auto& r : rb) {
+            if (r[1] == 0) continue;
+            EPB_CUDA(h, cudaMemcpyAsync(host_grad_x + r[0], grad_x + r[0], (size_t)r[1] * sizeof(float),
+                                        cudaMemcpyDeviceToHost, st));
+            EPB_CUDA(h, cudaMemcpyAsync(host_grad_y + r[0], grad_y + r[0], (size_t)r[1] * sizeof(float),
+                                        cudaMemcpyDeviceToHost, st));
+        }
+        pc.end_stage(EPB_STAGE_GATHER);
+        return EPB_OK;
+    }
     k_gather<true><<<gather_blocks(h, v.n, true), 256, 0, st>>>(v, geom(h), h->fxy, nullptr, nullptr, 0, h->M, 0, 0, grad_out,
                                                      grad_x, grad_y, h->flags, static_cast<float*>(hgx),
                                                      static_cast<float*>(hgy));
@@ -852,6 +1117,12 @@ int epb_overflow(epb_handle* h, const epb_cells* cells, float target_density, ep
     if (int rc = make_view(h, cells, v)) return rc;
     DeviceGuard guard(h->dev);
     cudaStream_t st = (cudaStream_t)stream;
+    if (!h->cell_order) {
+        // every cell given is an overflow cell; no density map is written
+        if (int rc = tile_prepare(h, v, st)) return rc;
+        TileOverflow ov{{v.b0, v.b0 + v.n0, v.b1, v.b1 + (v.n - v.n0)}, target_density, out};
+        return tile_scatter(h, v, nullptr, st, &ov);
+    }
     const int64_t nbins = (int64_t)h->RB * h->N;
     if (h->grid_dirty) {
         EPB_CUDA(h, cudaMemsetAsync(h->grid, 0, (size_t)nbins * sizeof(long long), st));
@@ -878,6 +1149,20 @@ int epb_forward_overflow(epb_handle* h, const epb_cells* cells, float target_den
     if (int rc = make_view(h, cells, v)) return rc;
     DeviceGuard guard(h->dev);
     cudaStream_t st = (cudaStream_t)stream;
+    if (!h->cell_order) {
+        // one set of lists for both ranges; the tiles sum the first range apart for its overflow
+        ProfCall pc(h, st);
+        pc.begin();
+        if (int rc = tile_prepare(h, v, st)) return rc;
+        pc.end_stage(EPB_STAGE_BIN);
+        float* rho = density ? density : h->rho;
+        TileOverflow ov{{v.b0, v.b0 + v.n0, 0, 0}, target_density, overflow};
+        if (int rc = tile_scatter(h, v, rho, st, &ov)) return rc;
+        pc.end_stage(EPB_STAGE_SCATTER);
+        if (int rc = launch_row_fwd(h, false, rho, nullptr, blocked(h->t1, 0, 1), 0, st)) return rc;
+        pc.end_stage(EPB_STAGE_ROW_FWD);
+        return solve_from_t1(h, st, potential, field_x, field_y, energy, pc);
+    }
     const int64_t nbins = (int64_t)h->M * h->N;
     if (!h->grid2) {
         // second grid for the first range (allocated once; the first call synchronises)
@@ -924,6 +1209,9 @@ int epb_descent_step(epb_handle* h, const epb_cells* cells, float* x, float* y, 
     cudaStream_t st = (cudaStream_t)stream;
     EPB_CUDA(h, cudaMemsetAsync(h->linf_bits, 0, sizeof(unsigned), st));
     h->own_valid = false;  // positions move: no selection made before this step stays valid
+    // the tile lists stay (every forward validates them against the positions it is
+    // given); a gather before the next forward validates them first
+    h->tb_stale = true;
     if (v.n > 0) {
         k_grad_linf<<<cell_blocks(v.n), 256, 0, st>>>(v, grad_x, grad_y, h->linf_bits, h->flags);
         EPB_LAUNCHED(h, "k_grad_linf launch");
@@ -969,6 +1257,20 @@ int epb_shard_rows_forward(epb_handle* h, const epb_cells* cells, epb_stream str
     if (int rc = make_view(h, cells, v)) return rc;
     DeviceGuard guard(h->dev);
     cudaStream_t st = (cudaStream_t)stream;
+    if (!h->cell_order) {
+        // the band's cell tiles: its density, then the row DCT blocks
+        ProfCall pc(h, st);
+        pc.begin();
+        if (int rc = tile_prepare(h, v, st)) return rc;
+        pc.end_stage(EPB_STAGE_BIN);
+        float* rho = density_band ? density_band : h->rho;
+        if (int rc = tile_scatter(h, v, rho, st)) return rc;
+        pc.end_stage(EPB_STAGE_SCATTER);
+        if (int rc = launch_row_fwd(h, false, rho, nullptr, blocked(t1_send, (int64_t)h->RB * h->NB, h->P), 0, st))
+            return rc;
+        pc.end_stage(EPB_STAGE_ROW_FWD);
+        return EPB_OK;
+    }
     if (h->grid_dirty) {
         EPB_CUDA(h, cudaMemsetAsync(h->grid, 0, (size_t)h->RB * h->N * sizeof(long long), st));
         h->grid_dirty = false;
@@ -1138,21 +1440,31 @@ int epb_shard_forward_peer(epb_handle* h, const epb_cells* cells, epb_stream str
     if (int rc = make_view(h, cells, v)) return rc;
     DeviceGuard guard(h->dev);
     cudaStream_t st = (cudaStream_t)stream;
-    if (h->grid_dirty) {
-        EPB_CUDA(h, cudaMemsetAsync(h->grid, 0, (size_t)h->RB * h->N * sizeof(long long), st));
-        h->grid_dirty = false;
-    }
-    h->grid_dirty = true;
     ProfCall pc(h, st);
     pc.begin();
-    if (int rc = scatter_into(h, v, st, h->grid)) return rc;
-    pc.end_stage(EPB_STAGE_SCATTER);
     // row DCT blocks go straight into every shard's column strip
     DstTable t1;
     for (int q = 0; q < kMaxShards; ++q) t1.p[q] = q < h->P ? h->peer_t1[q] : nullptr;
-    if (int rc = launch_row_fwd(h, true, nullptr, density_band, t1, h->row0, st)) return rc;
-    pc.end_stage(EPB_STAGE_ROW_FWD);
-    h->grid_dirty = false;
+    if (!h->cell_order) {
+        if (int rc = tile_prepare(h, v, st)) return rc;
+        pc.end_stage(EPB_STAGE_BIN);
+        float* rho = density_band ? density_band : h->rho;
+        if (int rc = tile_scatter(h, v, rho, st)) return rc;
+        pc.end_stage(EPB_STAGE_SCATTER);
+        if (int rc = launch_row_fwd(h, false, rho, nullptr, t1, h->row0, st)) return rc;
+        pc.end_stage(EPB_STAGE_ROW_FWD);
+    } else {
+        if (h->grid_dirty) {
+            EPB_CUDA(h, cudaMemsetAsync(h->grid, 0, (size_t)h->RB * h->N * sizeof(long long), st));
+            h->grid_dirty = false;
+        }
+        h->grid_dirty = true;
+        if (int rc = scatter_into(h, v, st, h->grid)) return rc;
+        pc.end_stage(EPB_STAGE_SCATTER);
+        if (int rc = launch_row_fwd(h, true, nullptr, density_band, t1, h->row0, st)) return rc;
+        pc.end_stage(EPB_STAGE_ROW_FWD);
+        h->grid_dirty = false;
+    }
     if (int rc = signal_and_wait(h, 0, st)) return rc;
     pc.last = pc.mark();
     // column outputs: this band's block in place, the other bands' blocks staged

@@ -171,6 +171,86 @@ k_wa_big_nets(NetlistView nl, const float* __restrict__ x, const float* __restri
 // pin order; per-pin WA gradients into pin_grad[pin] (zero for pins of nets
 // that contribute nothing).  Its last block writes out[0] = WA, out[1] = HPWL:
 // the warp pass's block partials, then this pass's, each in block order.
+// Nets of at most kWlSmall pins take a register path: every level of loads
+// (pins, then nodes and offsets, then positions) is issued for all pins at
+// once, and each pin's exponentials are computed once.  The operations and
+// their order are those of the general loops, so both give the same bits.
+constexpr int kWlSmall = 4;
+
+__device__ __forceinline__ void wa_small_net(const NetlistView& nl, const float* __restrict__ x,
+                                             const float* __restrict__ y, float inv_gamma, int s, int deg, float w,
+                                             float2* __restrict__ pin_grad, double& wa_sum, double& hp_sum,
+                                             unsigned& bad) {
+    int pin[kWlSmall], node[kWlSmall];
+    float px[kWlSmall], py[kWlSmall];
+    bool ok = deg >= 2;
+#pragma unroll
+    for (int j = 0; j < kWlSmall; ++j) pin[j] = j < deg ? __ldg(nl.net_pins + s + j) : 0;
+#pragma unroll
+    for (int j = 0; j < kWlSmall; ++j) {
+        node[j] = 0;
+        if (j < deg) {
+            if (pin[j] < 0 || pin[j] >= nl.P) { bad |= kFlagBadIndex; ok = false; pin[j] = -1; }
+            else node[j] = __ldg(nl.pin_node + pin[j]);
+        }
+    }
+    float ox[kWlSmall], oy[kWlSmall];
+#pragma unroll
+    for (int j = 0; j < kWlSmall; ++j) {
+        ox[j] = oy[j] = 0.0f;
+        if (j < deg && pin[j] >= 0) {
+            if (node[j] < 0 || node[j] >= nl.V) { bad |= kFlagBadIndex; ok = false; node[j] = -1; }
+            else { ox[j] = __ldg(nl.pin_ox + pin[j]); oy[j] = __ldg(nl.pin_oy + pin[j]); }
+        }
+    }
+    float xmax = -INFINITY, xmin = INFINITY, ymax = -INFINITY, ymin = INFINITY;
+#pragma unroll
+    for (int j = 0; j < kWlSmall; ++j) {
+        px[j] = py[j] = 0.0f;
+        if (j < deg && pin[j] >= 0 && node[j] >= 0) {
+            px[j] = __fadd_rn(__ldg(x + node[j]), ox[j]);
+            py[j] = __fadd_rn(__ldg(y + node[j]), oy[j]);
+            if (!isfinite(px[j]) || !isfinite(py[j])) { bad |= kFlagNonFinite; ok = false; px[j] = py[j] = 0.0f; }
+        }
+        if (j < deg) {
+            xmax = fmaxf(xmax, px[j]); xmin = fminf(xmin, px[j]);
+            ymax = fmaxf(ymax, py[j]); ymin = fminf(ymin, py[j]);
+        }
+    }
+    if (ok) hp_sum += (double)(w * ((xmax - xmin) + (ymax - ymin)));
+    const bool in_wa = ok && deg <= nl.ignore_degree;
+    float ax[kWlSmall], cx[kWlSmall], ay[kWlSmall], cy[kWlSmall];
+    float fx = 0.0f, hx = 0.0f, fy = 0.0f, hy = 0.0f, bx = 1.0f, dx = 1.0f, by = 1.0f, dy = 1.0f;
+    if (in_wa) {
+        float sax = 0.0f, scx = 0.0f, say = 0.0f, scy = 0.0f;
+        bx = dx = by = dy = 0.0f;
+#pragma unroll
+        for (int j = 0; j < kWlSmall; ++j) {
+            if (j >= deg) break;
+            ax[j] = expf((px[j] - xmax) * inv_gamma); cx[j] = expf((xmin - px[j]) * inv_gamma);
+            ay[j] = expf((py[j] - ymax) * inv_gamma); cy[j] = expf((ymin - py[j]) * inv_gamma);
+            bx += ax[j]; dx += cx[j]; sax += px[j] * ax[j]; scx += px[j] * cx[j];
+            by += ay[j]; dy += cy[j]; say += py[j] * ay[j]; scy += py[j] * cy[j];
+        }
+        fx = sax / bx; hx = scx / dx;
+        fy = say / by; hy = scy / dy;
+        wa_sum += (double)(w * ((fx - hx) + (fy - hy)));
+    }
+#pragma unroll
+    for (int j = 0; j < kWlSmall; ++j) {
+        if (j >= deg) break;
+        if (pin[j] < 0) continue;
+        float2 gp = make_float2(0.0f, 0.0f);
+        if (in_wa) {
+            gp.x = w * ((ax[j] / bx) * (1.0f + (px[j] - fx) * inv_gamma) -
+                        (cx[j] / dx) * (1.0f - (px[j] - hx) * inv_gamma));
+            gp.y = w * ((ay[j] / by) * (1.0f + (py[j] - fy) * inv_gamma) -
+                        (cy[j] / dy) * (1.0f - (py[j] - hy) * inv_gamma));
+        }
+        pin_grad[pin[j]] = gp;
+    }
+}
+
 __global__ void __launch_bounds__(kWlThreads)
 k_wa_nets(NetlistView nl, const float* __restrict__ x, const float* __restrict__ y, float inv_gamma,
           float2* __restrict__ pin_grad, float2* __restrict__ slot_pos, double* __restrict__ partials,
@@ -183,6 +263,10 @@ k_wa_nets(NetlistView nl, const float* __restrict__ x, const float* __restrict__
         if (s < 0 || t < s || t > nl.P) { bad |= kFlagBadIndex; continue; }
         if (t - s > kWlWarpDegree) continue;        // the warp pass's net
         const float w = nl.net_weight ? __ldg(nl.net_weight + e) : 1.0f;
+        if (t - s <= kWlSmall) {
+            wa_small_net(nl, x, y, inv_gamma, s, t - s, w, pin_grad, wa_sum, hp_sum, bad);
+            continue;
+        }
         bool ok = t - s >= 2;
         float xmax = -INFINITY, xmin = INFINITY, ymax = -INFINITY, ymin = INFINITY;
 #pragma unroll 4

@@ -77,7 +77,7 @@ class ElectricPotentialEngine:
     -> close, in process, on device tensors."""
 
     def __init__(self, num_bins_x: int, num_bins_y: int, xl: float, yl: float, xh: float, yh: float,
-                 fixed_point_bits: int = 0, device=None):
+                 fixed_point_bits: int = 0, device=None, path: Optional[str] = None):
         if not torch.cuda.is_available():
             raise RuntimeError("ElectricPotentialEngine needs a CUDA device (no CPU path)")
         self.lib = _lib.load()
@@ -86,7 +86,8 @@ class ElectricPotentialEngine:
         self.M, self.N = int(num_bins_x), int(num_bins_y)
         self.xl, self.yl, self.xh, self.yh = float(xl), float(yl), float(xh), float(yh)
         cfg = _lib.EpbConfig(self.M, self.N, self.xl, self.yl, self.xh, self.yh,
-                             int(fixed_point_bits), self.device.index, 0, 0)
+                             int(fixed_point_bits), self.device.index,
+                             {None: 0, "cell_order": _lib.CONFIG_CELL_ORDER, "tiles": _lib.CONFIG_TILES}[path], 0)
         h = ctypes.c_void_p()
         st = self.lib.epb_create(ctypes.byref(cfg), ctypes.byref(h))
         if st != _lib.EPB_OK:

