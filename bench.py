@@ -343,7 +343,7 @@ def workload_config(args, p):
         "density": "int64 fixed point (bit-exact), fp32 DCT/fields",
         "l2": "flushed between timed steps (write of 2x L2 size)",
         "parallelism": "single" if args.gpus == 1 else
-        f"row-band shards x{args.gpus}, transport {args.transport} "
+        f"row-band shards x{args.gpus} ({args.shard_path}), transport {args.transport} "
         f"({'kernel stores into peer memory over NVLink' if args.transport == 'peer' else 'NCCL all-to-all, all-reduce, p2p'})",
     }
 
@@ -545,7 +545,8 @@ def measure_sharded(args, p, dev, world, rank, K, W, flush, e2e=True):
     pos, cells, to = _cells_on(p, dev)
     n = p.num_nodes
     sh = ShardedElectricPotential(p.num_bins_x, p.num_bins_y, p.xl, p.yl, p.xh, p.yh,
-                                  float(p.size_x_clamped.max()), device=dev, transport=args.transport)
+                                  float(p.size_x_clamped.max()), device=dev, transport=args.transport,
+                                  path=args.shard_path)
     sh.set_initial_density(to(p.initial_density_norm()))
     RB, N = sh.RB, p.num_bins_y
     outs = {k: torch.empty((RB, N), dtype=torch.float32, device=dev)
@@ -667,6 +668,16 @@ def _max_over_ranks(dev, values):
     return [float(v) for v in t]
 
 
+def sharded_bytes_cell_order(stage, n_cells, bins, P):
+    """Per rank and launch on the cell-order shard path: every rank reads the x
+    data of all cells for its band selection and the cells it keeps, the grids
+    are 1/P per rank."""
+    per_cell, _, per_bin = STAGE_BYTES_CELL_ORDER[stage]
+    if stage == "gather":
+        return 28 * n_cells + 8 * n_cells // P + per_bin * bins // P
+    return per_cell * n_cells + per_bin * bins // P
+
+
 def run_sharded(args, p, dev, world, rank):
     """The headline on `world` GPUs, plus the C4 (4096^2, 2.5M cells) item."""
     from dreamplacett_framework_b200 import synth
@@ -697,7 +708,10 @@ def run_sharded(args, p, dev, world, rank):
     peak, peak_kind = load_peaks()
     bins = p.num_bins_x * p.num_bins_y
     listings = tile_listings(p, margin=0)
-    kern = _kernels(r["stages"], lambda k: sharded_bytes(k, p.num_cells, bins, world, listings), peak)
+    if args.shard_path == "tiles":
+        kern = _kernels(r["stages"], lambda k: sharded_bytes(k, p.num_cells, bins, world, listings), peak)
+    else:
+        kern = _kernels(r["stages"], lambda k: sharded_bytes_cell_order(k, p.num_cells, bins, world), peak)
     dom = max(kern, key=lambda k: kern[k]["avg_us"])
     kernel_us = sum(v["avg_us"] for v in kern.values())
     n = p.num_nodes
@@ -705,7 +719,7 @@ def run_sharded(args, p, dev, world, rank):
     # k_validate, k_esc_scatter, k_tile_scatter, k_row_fwd, k_col, k_row_inv, k_tile_gather,
     # k_esc_gather; the peer transport adds k_push and a k_signal + k_wait pair after each of
     # its three exchanges
-    launches_per_step = 19 if args.transport == "peer" else 12
+    launches_per_step = (12 if args.shard_path == "tiles" else 6) + (7 if args.transport == "peer" else 0)
     line = {
         "metric": METRIC, "value": K / (total_ms / 1000.0), "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": args.warmup, "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "strong",
@@ -745,6 +759,8 @@ def main():
     ap.add_argument("--no-loop", action="store_true", help="skip the C5 loop and the wirelength line items")
     ap.add_argument("--no-configs", action="store_true", help="skip the C1 / C2 / C4 line items")
     ap.add_argument("--no-c4", action="store_true", help="multi-GPU: skip the C4 item")
+    ap.add_argument("--shard-path", default="cell_order", choices=["cell_order", "tiles"],
+                    help="multi-GPU: each band's cells through its tile lists, or selected per call in cell order")
     ap.add_argument("--transport", default="peer", choices=["peer", "nccl"],
                     help="multi-GPU exchange: stores into peer memory fused into the kernels, or NCCL collectives")
     args = ap.parse_args()

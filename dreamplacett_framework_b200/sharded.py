@@ -46,11 +46,12 @@ class EngineShard:
     """Backend: the CUDA engine's epb_shard_* stages (one shard handle)."""
 
     def __init__(self, num_bins_x, num_bins_y, xl, yl, xh, yh, num_shards, shard, device,
-                 fixed_point_bits=0):
+                 fixed_point_bits=0, path=None):
         self.lib = _lib.load()
         self.device = device
+        flags = {None: 0, "cell_order": _lib.CONFIG_CELL_ORDER, "tiles": _lib.CONFIG_TILES}[path]
         cfg = _lib.EpbConfig(int(num_bins_x), int(num_bins_y), float(xl), float(yl), float(xh), float(yh),
-                             int(fixed_point_bits), device.index, 0, 0)
+                             int(fixed_point_bits), device.index, flags, 0)
         h = ctypes.c_void_p()
         st = self.lib.epb_create_shard(ctypes.byref(cfg), int(num_shards), int(shard), ctypes.byref(h))
         if st != _lib.EPB_OK:
@@ -156,7 +157,7 @@ class ShardedElectricPotential:
     """Forward/backward of one grid over the ranks of a process group."""
 
     def __init__(self, num_bins_x, num_bins_y, xl, yl, xh, yh, max_cell_size_x, group=None, device=None,
-                 backend=None, fixed_point_bits=0, transport="nccl"):
+                 backend=None, fixed_point_bits=0, transport="nccl", path=None):
         self.group = group
         self.P = dist.get_world_size(group)
         self.p = dist.get_rank(group)
@@ -165,7 +166,7 @@ class ShardedElectricPotential:
             device = torch.device("cuda", torch.cuda.current_device())
         self.device = torch.device(device)
         self.be = backend if backend is not None else EngineShard(
-            num_bins_x, num_bins_y, xl, yl, xh, yh, self.P, self.p, self.device, fixed_point_bits)
+            num_bins_x, num_bins_y, xl, yl, xh, yh, self.P, self.p, self.device, fixed_point_bits, path)
         RB, NB, M, N = self.M // self.P, self.N // self.P, self.M, self.N
         self.RB, self.NB = RB, NB
         H = halo_rows_for(max_cell_size_x, self.be.bin_size_x)

@@ -76,14 +76,17 @@ typedef enum epb_status {
 #define EPB_FLAG_SATURATED      0x2u  /* a fixed-point bin left [0, 2^62) */
 
 /* epb_config.flags selects how the cells reach the grid:
- * EPB_CONFIG_CELL_ORDER: one 64-bit global atomic add per (cell, bin) into an
- *   int64 grid, and a gather that reads the fields per cell in node order
- *   (the default of a whole-grid handle);
+ * EPB_CONFIG_CELL_ORDER (the default, also when flags is 0): one 64-bit
+ *   global atomic add per (cell, bin) into an int64 grid, and a gather that
+ *   reads the fields per cell in node order (a shard first selects the cells
+ *   that meet its band);
  * EPB_CONFIG_TILES: cell tiles -- each cell listed in the 32 x 32-bin tiles its
  *   footprint (widened by 2 bins) meets, the lists kept across calls and
- *   validated against the positions of every forward, each tile summed exactly
- *   in shared memory and written once, its gradients read from the tile's
- *   field region in shared memory (the default of a shard, epb_create_shard).
+ *   validated against the positions of every forward (a shard rebuilds its
+ *   band's lists every call), each tile summed exactly in shared memory and
+ *   written once, its gradients read from the tile's field region in shared
+ *   memory.  Measured slower than cell order on B200 (the list upkeep costs
+ *   more than the atomics it saves); kept for comparison.
  * Both give the same density bit for bit and the same gradients bit for bit.
  * With the tiles, epb_backward gives the gradient at the positions of the
  * last forward on the same cell arrays (positions moved by epb_descent_step

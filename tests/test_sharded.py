@@ -300,14 +300,16 @@ def test_shard_stages_reject_misaligned_buffers(cuda_device):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("path", ["cell_order", "tiles"])
 @pytest.mark.parametrize("P", [2, 4, 8])
-def test_shards_on_one_gpu_match_single_gpu(cuda_device, P):
+def test_shards_on_one_gpu_match_single_gpu(cuda_device, P, path):
     """Every shard of a P-way split run in turn on one GPU, the all-to-alls, the
     energy sum and the field halo done by tensor copies in the layouts the NCCL
     transport moves: the density is the one-GPU density bit for bit, the fields,
     energy and summed gradients agree within 1e-5.  At 2048² and P >= 4 a band's
     row pass and a strip's column pass launch fewer CTAs than the GPU has SMs, so
-    this covers their half-size CTAs."""
+    this covers their half-size CTAs.  Both shard paths: cells selected per
+    call in cell order (the default), or each band's tile lists."""
     from dreamplacett_framework_b200 import _lib
     from dreamplacett_framework_b200.engine import ElectricPotentialEngine
     from dreamplacett_framework_b200.sharded import EngineShard, halo_rows_for
@@ -321,7 +323,7 @@ def test_shards_on_one_gpu_match_single_gpu(cuda_device, P):
         rgx, rgy = (g.clone() for g in eng.backward(cells))
     RB, NB, K = M // P, N // P, _lib.COL_OUTPUTS
     f = lambda *s, dt=torch.float32: torch.zeros(*s, dtype=dt, device=cuda_device)
-    shards = [EngineShard(M, N, p.xl, p.yl, p.xh, p.yh, P, q, cuda_device) for q in range(P)]
+    shards = [EngineShard(M, N, p.xl, p.yl, p.xh, p.yh, P, q, cuda_device, path=path) for q in range(P)]
     try:
         H = halo_rows_for(float(np.max(p.size_x_clamped)), shards[0].bin_size_x)
         assert H <= RB

@@ -1,6 +1,5 @@
-"""The cell-tile path (EPB_CONFIG_TILES; the default of a shard) against the
-cell-order path (EPB_CONFIG_CELL_ORDER; the default of a whole grid) and the
-CPU oracle.
+"""The cell-tile path (EPB_CONFIG_TILES) against the cell-order path (the
+default) and the CPU oracle.
 
 Both paths sum the same integer contributions, so the density is compared bit
 for bit, and their gathers do the same fp32 arithmetic per cell, so the
