@@ -171,6 +171,8 @@ def wirelength_item(p, dev, flush, peak, K=200, W=5):
             "us_per_call": us, "calls": K, "algorithmic_bytes": nbytes, "gbs": nbytes / us / 1e3,
             "frac": nbytes / us / 1e3 / peak,
             "wirelength": float(r["wirelength"].item()), "hpwl": float(r["hpwl"].item()),
+            # k_wa_pins (pin positions), k_wa_windows (nets), k_wa_nodes (node gradients);
+            # plus a 4-byte counter memset
             "gpu_launches_per_call": 3,
             "error_flags": op.error_flags()}
 
@@ -342,6 +344,7 @@ def workload_config(args, p):
         "cells": p.num_cells, "bins": [p.num_bins_x, p.num_bins_y],
         "density": "int64 fixed point (bit-exact), fp32 DCT/fields",
         "l2": "flushed between timed steps (write of 2x L2 size)",
+        "path": args.path if args.gpus == 1 else args.shard_path,
         "parallelism": "single" if args.gpus == 1 else
         f"row-band shards x{args.gpus} ({args.shard_path}), transport {args.transport} "
         f"({'kernel stores into peer memory over NVLink' if args.transport == 'peer' else 'NCCL all-to-all, all-reduce, p2p'})",
@@ -682,6 +685,11 @@ def run_sharded(args, p, dev, world, rank):
     """The headline on `world` GPUs, plus the C4 (4096^2, 2.5M cells) item."""
     from dreamplacett_framework_b200 import synth
     flush = _flush_buffer(dev)
+    if args.wirelength_only:
+        peak, _ = load_peaks()
+        print(json.dumps({"config": workload_config(args, p),
+                          "wirelength": wirelength_item(p, dev, flush, peak, K=args.steps, W=args.warmup)}), flush=True)
+        return
     sampler = ClockSampler(gpu_smi_id(dev))
     sampler.start()
     time.sleep(0.5)
@@ -759,6 +767,10 @@ def main():
     ap.add_argument("--no-loop", action="store_true", help="skip the C5 loop and the wirelength line items")
     ap.add_argument("--no-configs", action="store_true", help="skip the C1 / C2 / C4 line items")
     ap.add_argument("--no-c4", action="store_true", help="multi-GPU: skip the C4 item")
+    ap.add_argument("--wirelength-only", action="store_true",
+                    help="one GPU: time only the wirelength op on the workload's netlist and print its item")
+    ap.add_argument("--path", default="cell_order", choices=["cell_order", "tiles"],
+                    help="one GPU: the cell-order scatter / gather (default) or the cell tiles")
     ap.add_argument("--shard-path", default="cell_order", choices=["cell_order", "tiles"],
                     help="multi-GPU: each band's cells through its tile lists, or selected per call in cell order")
     ap.add_argument("--transport", default="peer", choices=["peer", "nccl"],
@@ -793,12 +805,18 @@ def main():
         return
 
     flush = _flush_buffer(dev)
+    if args.wirelength_only:
+        peak, _ = load_peaks()
+        print(json.dumps({"config": workload_config(args, p),
+                          "wirelength": wirelength_item(p, dev, flush, peak, K=args.steps, W=args.warmup)}), flush=True)
+        return
     sampler = ClockSampler(gpu_smi_id(dev))
     sampler.start()
     time.sleep(0.5)
     peak, peak_kind = load_peaks()
     K = args.steps
-    r = measure_single(p, dev, K, args.warmup, flush, peak, e2e=True)
+    r = measure_single(p, dev, K, args.warmup, flush, peak, e2e=True,
+                       path=None if args.path == "cell_order" else args.path)
     clocks = sampler.summary(r["t_soak0"], r["t1"])
     clocks["window"] = "1 s of untimed graph replays right before the timed steps, and the timed steps"
     sampler.stop()
@@ -834,8 +852,9 @@ def main():
     if not args.no_configs:
         line["configs"] = {name: config_item(name, dev, flush, peak) for name in ("c1", "c2", "c4")
                            if name != args.config}
-        # the same workload through the cell tiles (EPB_CONFIG_TILES), for comparison
-        line["tiles"] = config_item(args.config, dev, flush, peak, path="tiles")
+        # the same workload through the other path, for comparison
+        other = "tiles" if args.path == "cell_order" else "cell_order"
+        line[other] = config_item(args.config, dev, flush, peak, path=other)
     if not args.no_loop:
         from dreamplacett_framework_b200.placement import DensityDescent
         p5 = synth.make_placement("c5")

@@ -16,7 +16,7 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libepb200.so")
 SOURCES = ["epb_engine.cu"]
-HEADERS = ["epb_kernels.cuh", "fft.cuh", "geometry.cuh", "placement_kernels.cuh"]
+HEADERS = ["epb_kernels.cuh", "fft.cuh", "geometry.cuh", "placement_kernels.cuh", "tile_kernels.cuh", "wirelength.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -1732,21 +1732,26 @@ extern "C" int epb_wirelength(const epb_netlist* nl, const float* x, const float
     float2* slot_pos = pin_grad + v.P;
     cudaError_t e = cudaMemsetAsync(counter, 0, sizeof(unsigned), st);
     if (e != cudaSuccess) return noalloc_fail(err, err_len, EPB_ECUDA, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
-    // nets of more than kWlWarpDegree pins first, a warp each (a block scans 256 nets per round);
-    // then the rest, a thread each, whose last block adds up both passes' block partials
-    const int nets_blocks = (int)std::max<int64_t>(((int64_t)v.E + kWlThreads - 1) / kWlThreads, 1);
-    const int bb = std::min(nets_blocks, kWlBigBlocks);
-    double* big_partials = partials + 2 * kWlMaxBlocks;
-    k_wa_big_nets<<<bb, kWlThreads, 0, st>>>(v, x, y, 1.0f / gamma, pin_grad, slot_pos, big_partials, flags);
+    // pin positions by net-list slot, a thread each
+    if (v.P > 0) {
+        const int64_t per_block = (int64_t)kWlThreads * kWlPinsPerThread;
+        const int pb = (int)(((int64_t)v.P + per_block - 1) / per_block);
+        k_wa_pins<<<pb, kWlThreads, 0, st>>>(v, x, y, slot_pos, flags);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return noalloc_fail(err, err_len, EPB_ECUDA, std::string("k_wa_pins: ") + cudaGetErrorString(e));
+    }
+    // windows of 32 nets, a warp each, over a fixed grid (one wave of resident
+    // blocks on a B200; the same partition of the windows, so the same bits, on
+    // every device); the last block adds up the block partials
+    const int64_t windows = ((int64_t)v.E + 31) / 32;
+    const int nb = (int)std::min<int64_t>(std::max<int64_t>((windows + kWlWarps - 1) / kWlWarps, 1), kWlWindowBlocks);
+    const float inv_gamma = 1.0f / gamma;
+    const float ig2 = (float)(1.4426950408889634 / (double)gamma);   // log2(e) / gamma
+    k_wa_windows<<<nb, kWlThreads, 0, st>>>(v, inv_gamma, ig2, pin_grad, slot_pos, partials, counter, out, flags);
     e = cudaGetLastError();
-    if (e != cudaSuccess) return noalloc_fail(err, err_len, EPB_ECUDA, std::string("k_wa_big_nets: ") + cudaGetErrorString(e));
-    const int nb = std::min(nets_blocks, kWlMaxBlocks);
-    k_wa_nets<<<nb, kWlThreads, 0, st>>>(v, x, y, 1.0f / gamma, pin_grad, slot_pos, partials, big_partials, bb,
-                                         counter, out, flags);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return noalloc_fail(err, err_len, EPB_ECUDA, std::string("k_wa_nets: ") + cudaGetErrorString(e));
+    if (e != cudaSuccess) return noalloc_fail(err, err_len, EPB_ECUDA, std::string("k_wa_windows: ") + cudaGetErrorString(e));
     if (want_grad && v.V > 0) {
-        const int gb = (int)std::min<int64_t>(((int64_t)v.V + kWlThreads - 1) / kWlThreads, 4096);
+        const int gb = (int)(((int64_t)v.V + kWlThreads - 1) / kWlThreads);
         k_wa_nodes<<<gb, kWlThreads, 0, st>>>(v, pin_grad, grad_x, grad_y, flags);
         e = cudaGetLastError();
         if (e != cudaSuccess) return noalloc_fail(err, err_len, EPB_ECUDA, std::string("k_wa_nodes: ") + cudaGetErrorString(e));

@@ -120,7 +120,8 @@ def test_abi_rejects_bad_arguments_without_cuda():
     from dreamplacett_framework_b200 import _lib, build
     build.build()
     L = _lib.load()
-    assert L.epb_wirelength_scratch_bytes(1000) == 16 + 16 * (1184 + 592) + 16 * 1000
+    # the block counter, 1184 block partials (WA, HPWL), then pin gradients and pin positions
+    assert L.epb_wirelength_scratch_bytes(1000) == 16 + 16 * 1184 + 16 * 1000
     fake = ctypes.c_void_p(1 << 20)   # never dereferenced: every case fails its host check first
     nl = _lib.EpbNetlist(fake, fake, fake, fake, fake, None, fake, fake, 10, 20, 5, 100, 0)
     err = ctypes.create_string_buffer(128)
