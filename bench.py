@@ -86,12 +86,23 @@ NCU_TRAFFIC_C3 = {
 }
 
 
-# 64-bit atomic adds per second on this pool's B200 for scatter-like footprints
-# (2x2, 2x3, 3x3 adds at hashed positions of a 2048 x 2048 int64 grid: 194-212 G/s),
-# measured by a standalone probe (profiles/scatter_atomic_rate.md).  The
-# cell-order scatter issues one such add per (cell, bin) pair, so count / rate
-# is its floor.
-ATOMIC_RATE_GOPS = 205.0
+def atomic_rate(eng, n_adds, flush, reps=5):
+    """64-bit atomic adds per second on this GPU, measured in this run: the
+    scatter's atomic (result unused) at hashed 2x2, 2x3 and 3x3 footprints of
+    the engine's grid, n_adds each, L2 flushed before each timed probe; the
+    median of `reps` per pattern.  The cell-order scatter issues one such add
+    per (cell, bin) pair, so its count / this rate is the scatter's floor."""
+    import statistics
+    out = {}
+    for fw, fh in ((2, 2), (2, 3), (3, 3)):
+        n = max(n_adds // (fw * fh), 1)
+        eng.atomic_probe(n, fw, fh)   # warm-up
+        ts = []
+        for _ in range(reps):
+            flush.zero_()
+            ts.append(eng.atomic_probe(n, fw, fh))
+        out[f"{fw}x{fh}"] = n * fw * fh / (statistics.median(ts) / 1e3) / 1e9
+    return out
 
 
 def footprints(p):
@@ -493,6 +504,8 @@ def measure_single(p, dev, K, W, flush, peak, e2e=False, path=None):
         res["e2e_ms"] = sum(a.elapsed_time(b) for a, b in ev2)
         res["K_e2e"] = K_e2e
     res["flags"] = eng.error_flags()
+    if not tiles:
+        res["atomic_rate"] = atomic_rate(eng, scatter_atomics(p), flush)
     eng.close()
     bins = M * N
     listings = tile_listings(p) if tiles else 0
@@ -512,8 +525,11 @@ def measure_single(p, dev, K, W, flush, peak, e2e=False, path=None):
     else:
         na = scatter_atomics(p)
         res["sc_ga"]["atomics"] = na
-        res["sc_ga"]["atomic_floor_us"] = na / (ATOMIC_RATE_GOPS * 1e3)
-        res["sc_ga"]["atomic_rate_source"] = "standalone probe on this pool's B200 (profiles/scatter_atomic_rate.md)"
+        rate = max(res["atomic_rate"].values())
+        res["sc_ga"]["atomic_rate_gops"] = res["atomic_rate"]
+        res["sc_ga"]["atomic_floor_us"] = na / (rate * 1e3)
+        res["sc_ga"]["atomic_rate_source"] = ("epb_atomic_probe in this run, same GPU, same grid: the fastest of "
+                                              "the 2x2 / 2x3 / 3x3 footprint patterns, as many adds as the scatter")
     res["step_bytes"] = sum(algorithmic_bytes(k, p.num_cells, bins, listings, not tiles) for k in stage_set)
     res["launches_per_step"] = 12 if tiles else 5
     return res

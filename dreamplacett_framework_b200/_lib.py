@@ -38,7 +38,7 @@ EXPORTS = (
     "epb_shard_backward_peer", "epb_shard_wait_test",
     "epb_overflow", "epb_descent_step", "epb_forward_overflow",
     "epb_forward_host", "epb_backward_host",
-    "epb_wirelength_scratch_bytes", "epb_wirelength",
+    "epb_wirelength_scratch_bytes", "epb_wirelength", "epb_atomic_probe",
 )
 
 # Largest grid (M*N bins) epb_density_noalloc accepts (EPB_NOALLOC_MAX_BINS).
@@ -139,6 +139,7 @@ def load():
     L.epb_forward_overflow.argtypes = [vp, cp, ctypes.c_float, vp, vp, vp, vp, vp, vp, vp]
     L.epb_forward_host.argtypes = [vp, cp, vp, vp, vp, vp, vp, vp, vp, vp]
     L.epb_backward_host.argtypes = [vp, cp, vp, vp, vp, vp, vp, vp]
+    L.epb_atomic_probe.argtypes = [vp, i64, i32, i32, vp, ctypes.POINTER(ctypes.c_double)]
     L.epb_wirelength_scratch_bytes.argtypes = [i32]
     L.epb_wirelength_scratch_bytes.restype = ctypes.c_size_t
     L.epb_wirelength.argtypes = [ctypes.POINTER(EpbNetlist), vp, vp, ctypes.c_float, vp, vp, ctypes.c_size_t, vp,

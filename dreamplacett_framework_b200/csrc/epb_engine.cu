@@ -1553,6 +1553,36 @@ int epb_profile_start(epb_handle* h, int32_t max_calls) {
     return EPB_OK;
 }
 
+int epb_atomic_probe(epb_handle* h, int64_t n_cells, int32_t fw, int32_t fh, epb_stream stream, double* ms) {
+    if (!h) return EPB_EINVAL;
+    if (!ms || n_cells < 0 || n_cells >= ((int64_t)1 << 31) || fw < 1 || fw > 8 || fh < 1 || fh > 8 || fw > h->M ||
+        fh > h->N)
+        return fail(h, EPB_EINVAL, "ms must be non-NULL, 0 <= n_cells < 2^31, footprints 1..8 and within the grid");
+    if (h->P > 1) return fail(h, EPB_EINVAL, "the probe runs on a whole-grid handle");
+    DeviceGuard guard(h->dev);
+    if (!guard.ok) return fail(h, EPB_ECUDA, "cudaSetDevice failed");
+    cudaStream_t st = (cudaStream_t)stream;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    cudaError_t e = cudaEventCreate(&e0);
+    if (e == cudaSuccess) e = cudaEventCreate(&e1);
+    if (e == cudaSuccess) e = cudaEventRecord(e0, st);
+    if (e == cudaSuccess && n_cells > 0) {
+        k_atomic_probe<<<(unsigned)((n_cells + 255) / 256), 256, 0, st>>>((unsigned long long*)h->grid, h->M, h->N,
+                                                                          n_cells, fw, fh);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaEventRecord(e1, st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(h->grid, 0, sizeof(long long) * (size_t)h->M * h->N, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    float t = 0.0f;
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&t, e0, e1);
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    if (e != cudaSuccess) return fail(h, EPB_ECUDA, std::string("atomic probe: ") + cudaGetErrorString(e));
+    *ms = t;
+    return EPB_OK;
+}
+
 int epb_profile_stop(epb_handle* h, double* stage_ms, int32_t* stage_launches) {
     if (!h) return EPB_EINVAL;
     DeviceGuard guard(h->dev);

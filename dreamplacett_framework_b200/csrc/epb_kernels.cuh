@@ -785,6 +785,24 @@ k_band_select(CellView c, GridGeom g, int row0, int row1, int* __restrict__ meet
     if (bad) atomicOr(flags, kFlagNonFinite);
 }
 
+// Atomic-rate probe: footprint i of fw x fh bins at a hashed bin of the grid,
+// one 64-bit atomic add per bin with its result unused (the scatter's
+// reduction, without its loads).
+__global__ void __launch_bounds__(256)
+k_atomic_probe(unsigned long long* __restrict__ grid, int M, int N, int64_t n, int fw, int fh) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    // a 32-bit integer hash of the footprint index (multiply-xorshift rounds)
+    uint32_t h = (uint32_t)i * 0x9e3779b9u;
+    h ^= h >> 16; h *= 0x85ebca6bu; h ^= h >> 13; h *= 0xc2b2ae35u; h ^= h >> 16;
+    const uint32_t wx = (uint32_t)(M - fw + 1), wy = (uint32_t)(N - fh + 1);
+    const int bx = (int)(h % wx);
+    const int by = (int)((h / wx) % wy);
+    for (int dx = 0; dx < fw; ++dx)
+        for (int dy = 0; dy < fh; ++dy)
+            atomicAdd(grid + (int64_t)(bx + dx) * N + (by + dy), 1ull);
+}
+
 // ---------------------------------------------------------------------------
 // Gather: grad[node] = -g * ratio * sum (ox*oy) * field
 // ---------------------------------------------------------------------------

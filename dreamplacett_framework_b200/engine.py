@@ -343,6 +343,15 @@ class ElectricPotentialEngine:
         _lib.check(self._h, self.lib.epb_profile_stop(self._h, ms, cnt))
         return {name: (float(ms[i]), int(cnt[i])) for i, name in enumerate(_lib.STAGES)}
 
+    def atomic_probe(self, n_cells, fw=2, fh=3, stream=None) -> float:
+        """Milliseconds of n_cells * fw * fh 64-bit atomic adds into this
+        engine's grid (the scatter's atomic at hashed footprints); the grid is
+        zeroed again afterwards.  Synchronises."""
+        ms = ctypes.c_double()
+        _lib.check(self._h, self.lib.epb_atomic_probe(self._h, int(n_cells), int(fw), int(fh),
+                                                      _stream_ptr(stream, self.device), ctypes.byref(ms)))
+        return ms.value
+
     def error_flags(self, stream=None) -> int:
         """Synchronises; returns and clears EPB_FLAG_* bits.  Raises EpbError
         with EPB_EOVERFLOW when the fixed-point grid saturated."""

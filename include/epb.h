@@ -336,6 +336,17 @@ int epb_descent_step(epb_handle* h, const epb_cells* cells, float* x, float* y, 
 int epb_profile_start(epb_handle* h, int32_t max_calls);
 int epb_profile_stop(epb_handle* h, double* stage_ms, int32_t* stage_launches);
 
+/* Diagnostic (no reference counterpart): the device's rate of the scatter's
+ * atomics, measured beside the scatter.  n_cells synthetic footprints of
+ * fw x fh bins (1..8 each) at hashed positions of the handle's grid, one
+ * 64-bit atomic add per (footprint, bin) with its result unused, as the
+ * scatter issues them; timed with CUDA events on `stream` around that kernel
+ * alone.  The grid is zeroed again afterwards, as a forward expects it.
+ * Whole-grid handles only.  Synchronises the stream.  *ms = the kernel's
+ * time; the rate is n_cells * fw * fh / ms.  Not for use inside a graph
+ * capture. */
+int epb_atomic_probe(epb_handle* h, int64_t n_cells, int32_t fw, int32_t fh, epb_stream stream, double* ms);
+
 /* Allocation-free density map.  This entry point has no counterpart in the
  * reference; it exists for callers that cannot allocate device memory: code
  * whose device memory is owned by another allocator (a framework's caching

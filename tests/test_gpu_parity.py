@@ -74,6 +74,24 @@ def test_scatter_deterministic_run_to_run(cuda_device):
                 assert torch.equal(o[k], outs[0][k]), k
 
 
+def test_atomic_probe_leaves_the_grid_zeroed(cuda_device):
+    """The bench's atomic-rate probe writes the engine's own grid: a forward
+    after it gives the same bits as one before it, and bad sizes are refused."""
+    p = synth.make_placement("c1", scale=0.2)
+    arrs, ranges = placement_cells(p)
+    cells = to_device(arrs, ranges, cuda_device)
+    with engine_for(p, cuda_device) as eng:
+        before = eng.forward(cells)
+        ms = eng.atomic_probe(200000, 2, 3)
+        assert ms > 0.0
+        after = eng.forward(cells)
+        for k in ("density", "potential", "field_x", "field_y", "energy"):
+            assert torch.equal(after[k], before[k]), k
+        for args in ((-1, 2, 2), (10, 0, 2), (10, 2, 9)):
+            with pytest.raises(_lib.EpbError):
+                eng.atomic_probe(*args)
+
+
 # ---------------------------------------------------------------- DCT solve
 
 @pytest.mark.parametrize("M,N", [(16, 16), (32, 64), (64, 16), (128, 128), (256, 512), (512, 512),
