@@ -688,12 +688,16 @@ def _max_over_ranks(dev, values):
 
 
 def sharded_bytes_cell_order(stage, n_cells, bins, P):
-    """Per rank and launch on the cell-order shard path: every rank reads the x
-    data of all cells for its band selection and the cells it keeps, the grids
+    """Per rank and launch on the cell-order shard path (band lists): the check
+    reads the x data and the list flag of every cell (13 B); the scatter reads
+    the positions and the list slot (x, y, sizes, offsets, ratio: 28 B) of the
+    ~n/P listed cells; the gather the same plus the gradient (36 B); the grids
     are 1/P per rank."""
     per_cell, _, per_bin = STAGE_BYTES_CELL_ORDER[stage]
+    if stage == "scatter":
+        return 13 * n_cells + 28 * n_cells // P + per_bin * bins // P
     if stage == "gather":
-        return 28 * n_cells + 8 * n_cells // P + per_bin * bins // P
+        return 36 * n_cells // P + per_bin * bins // P
     return per_cell * n_cells + per_bin * bins // P
 
 
@@ -739,11 +743,12 @@ def run_sharded(args, p, dev, world, rank):
     dom = max(kern, key=lambda k: kern[k]["avg_us"])
     kernel_us = sum(v["avg_us"] for v in kern.values())
     n = p.num_nodes
-    # our kernels per rank and step: k_tile_decide, k_rebuild_count, k_rebuild_scan, k_rebuild_fill,
-    # k_validate, k_esc_scatter, k_tile_scatter, k_row_fwd, k_col, k_row_inv, k_tile_gather,
-    # k_esc_gather; the peer transport adds k_push and a k_signal + k_wait pair after each of
-    # its three exchanges
-    launches_per_step = (12 if args.shard_path == "tiles" else 6) + (7 if args.transport == "peer" else 0)
+    # our kernels per rank and step: cell order k_band_check, k_band_list, k_scatter_listed, k_row_fwd,
+    # k_col, k_row_inv, k_gather_listed; tiles k_tile_decide, k_rebuild_count, k_rebuild_scan,
+    # k_rebuild_fill, k_validate, k_esc_scatter, k_tile_scatter, k_row_fwd, k_col, k_row_inv,
+    # k_tile_gather, k_esc_gather; the peer transport adds k_push and a k_signal + k_wait pair after
+    # each of its three exchanges
+    launches_per_step = (12 if args.shard_path == "tiles" else 7) + (7 if args.transport == "peer" else 0)
     line = {
         "metric": METRIC, "value": K / (total_ms / 1000.0), "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": args.warmup, "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "strong",
@@ -788,7 +793,7 @@ def main():
     ap.add_argument("--path", default="cell_order", choices=["cell_order", "tiles"],
                     help="one GPU: the cell-order scatter / gather (default) or the cell tiles")
     ap.add_argument("--shard-path", default="cell_order", choices=["cell_order", "tiles"],
-                    help="multi-GPU: each band's cells through its tile lists, or selected per call in cell order")
+                    help="multi-GPU: each band's cells through its tile lists, or its band list in cell order")
     ap.add_argument("--transport", default="peer", choices=["peer", "nccl"],
                     help="multi-GPU exchange: stores into peer memory fused into the kernels, or NCCL collectives")
     args = ap.parse_args()

@@ -55,16 +55,13 @@ struct epb_handle {
     // whole-grid gather: CTAs resident at once (k_gather<false>, k_gather<true>),
     // the grid of its cell-striding launch
     unsigned gather_grid[2] = {1, 1};
-    // band selection of a shard's scatter / gather (k_band_select): the cells
-    // meeting the band and the cells owned by it, with the cell view the own
-    // list was made from (the gather reuses it for the same cell arrays)
-    int* sel_list = nullptr;
-    int* sel_count = nullptr;
-    int* own_list = nullptr;
-    int* own_count = nullptr;
-    int64_t sel_cap = 0;
-    bool own_valid = false;
-    CellView own_key{};
+    // band lists of a shard in cell order (k_band_check / k_band_list): kept
+    // across calls, with the cell view they were made from
+    BandList bl{};
+    int64_t bl_cap = 0;         // cells the buffers hold (grows)
+    bool bl_force = true;       // the next list maintenance lists again (new buffers or cell arrays)
+    bool bl_stale = false;      // epb_descent_step moved the cells since the lists were last checked
+    CellView bl_key{};
     // peer transport (epb_shard_peer_buffers / epb_shard_connect)
     float* p_t1 = nullptr;      // t1_recv [M*NB]
     float* p_g = nullptr;       // g_recv [kColOutputs*M*NB]
@@ -168,7 +165,6 @@ int make_view(epb_handle* h, const epb_cells* c, CellView& v) {
     v.x = c->x; v.y = c->y; v.sx = c->size_x; v.sy = c->size_y;
     v.ox = c->offset_x; v.oy = c->offset_y; v.ratio = c->ratio;
     v.b0 = c->begin0; v.n0 = n0; v.b1 = c->begin1; v.n = n0 + n1;
-    v.sel = nullptr; v.sel_n = nullptr;
     return EPB_OK;
 }
 
@@ -218,8 +214,8 @@ int dev_alloc(epb_handle* h, T** p, size_t count) {
 void free_all(epb_handle* h) {
     void* ptrs[] = {h->grid, h->grid2, h->init, h->t1, h->g, h->fxy, h->twM, h->qwM,
                     h->twN, h->qwN, h->partials, h->counter, h->energy_d, h->flags,
-                    h->ovf_partials, h->ovf_counter, h->linf_bits, h->sel_list, h->sel_count,
-                    h->own_list, h->own_count, h->rho, h->tb.cnt, h->tb.cur, h->tb.start, h->tb.nown,
+                    h->ovf_partials, h->ovf_counter, h->linf_bits, h->bl.sel, h->bl.cnt,
+                    h->bl.geo, h->bl.r, h->bl.listed, h->rho, h->tb.cnt, h->tb.cur, h->tb.start, h->tb.nown,
                     h->tb.first_item, h->tb.items, h->tb.arrive, h->tb.part, h->tb.meta, h->tb.stat, h->tb.key,
                     h->tb.geo, h->tb.bins, h->tb.esc_dyn, h->tb.esc_static, h->tb.esc_grid, h->esc_grid0,
                     h->tile_ovf_part, h->tile_ovf_counter};
@@ -470,35 +466,47 @@ bool same_cells(const CellView& a, const CellView& b) {
     return a.x == b.x && a.ox == b.ox && a.sx == b.sx && a.b0 == b.b0 && a.n0 == b.n0 && a.b1 == b.b1 && a.n == b.n;
 }
 
-// On a shard (P > 1): list the cells meeting this band (the scatter's list,
-// when `meet`) and the cells owned by it (the gather's list, always); v then
-// points at the first list made.  The buffers grow with the cell count (that
-// call synchronises and allocates).
-int band_selection(epb_handle* h, CellView& v, bool meet, cudaStream_t st) {
-    const int64_t nseg = (v.n + kSelChunk - 1) / kSelChunk;
-    if (v.n > h->sel_cap) {
-        EPB_CUDA(h, cudaStreamSynchronize(st));
-        int** bufs[] = {&h->sel_list, &h->sel_count, &h->own_list, &h->own_count};
-        for (int** b : bufs) {
-            if (*b) cudaFree(*b);
-            *b = nullptr;
-        }
-        h->sel_cap = 0;
-        h->own_valid = false;
-        if (int rc = dev_alloc(h, &h->sel_list, (size_t)(nseg * kSelChunk))) return rc;
-        if (int rc = dev_alloc(h, &h->sel_count, (size_t)nseg)) return rc;
-        if (int rc = dev_alloc(h, &h->own_list, (size_t)(nseg * kSelChunk))) return rc;
-        if (int rc = dev_alloc(h, &h->own_count, (size_t)nseg)) return rc;
-        h->sel_cap = v.n;
+bool same_view(const CellView& a, const CellView& b);
+
+// Band-list buffers for n cells (grown when more cells come; that call
+// synchronises the stream and allocates, and the lists are made again).
+int band_list_reserve(epb_handle* h, int64_t n, cudaStream_t st) {
+    if (n <= h->bl_cap) return EPB_OK;
+    EPB_CUDA(h, cudaStreamSynchronize(st));
+    void** bufs[] = {(void**)&h->bl.sel, (void**)&h->bl.cnt, (void**)&h->bl.geo, (void**)&h->bl.r,
+                     (void**)&h->bl.listed};
+    for (void** b : bufs) {
+        if (*b) cudaFree(*b);
+        *b = nullptr;
     }
-    k_band_select<<<(unsigned)nseg, 256, 0, st>>>(v, geom(h), h->row0, h->row0 + h->RB,
-                                                  meet ? h->sel_list : nullptr, meet ? h->sel_count : nullptr,
-                                                  h->own_list, h->own_count, h->flags);
-    EPB_LAUNCHED(h, "k_band_select launch");
-    h->own_key = v;
-    h->own_valid = true;
-    v.sel = meet ? h->sel_list : h->own_list;
-    v.sel_n = meet ? h->sel_count : h->own_count;
+    h->bl_cap = 0;
+    const int64_t nseg = (n + kSelChunk - 1) / kSelChunk;
+    if (int rc = dev_alloc(h, &h->bl.sel, (size_t)(nseg * kSelChunk))) return rc;
+    if (int rc = dev_alloc(h, &h->bl.cnt, (size_t)nseg)) return rc;
+    if (int rc = dev_alloc(h, &h->bl.geo, (size_t)(nseg * kSelChunk))) return rc;
+    if (int rc = dev_alloc(h, &h->bl.r, (size_t)(nseg * kSelChunk))) return rc;
+    if (int rc = dev_alloc(h, &h->bl.listed, (size_t)n)) return rc;
+    EPB_CUDA(h, cudaMemset(h->bl.listed, 0, (size_t)n));
+    h->bl_cap = n;
+    h->bl_force = true;
+    return EPB_OK;
+}
+
+// On a shard (P > 1) in cell order: check the band's list against the
+// positions of v, segment by segment, and list a segment again when a cell
+// came into the band (on the device); every segment when the buffers or the
+// cell arrays are new.
+int band_list_prepare(epb_handle* h, const CellView& v, cudaStream_t st) {
+    if (int rc = band_list_reserve(h, std::max<int64_t>(v.n, 1), st)) return rc;
+    if (!same_view(h->bl_key, v)) h->bl_force = true;
+    const int row1 = h->row0 + h->RB;
+    const int64_t nseg = (v.n + kSelChunk - 1) / kSelChunk;
+    k_band_update<<<(unsigned)std::max<int64_t>(nseg, 1), 256, 0, st>>>(v, geom(h), h->row0, row1, h->bl,
+                                                                        h->bl_force ? 1 : 0, h->flags);
+    EPB_LAUNCHED(h, "k_band_update launch");
+    h->bl_force = false;
+    h->bl_stale = false;
+    h->bl_key = v;
     return EPB_OK;
 }
 
@@ -506,17 +514,20 @@ int scatter_into(epb_handle* h, const CellView& v0, cudaStream_t st, long long* 
     if (v0.n == 0) return EPB_OK;
     if (v0.n >= ((int64_t)1 << 31)) return fail(h, EPB_EINVAL, "at most 2^31 - 1 cells");
     const float qscale = ldexpf(1.0f, h->S);
-    CellView v = v0;
-    unsigned blocks = cell_blocks(v.n);
+    const CellView& v = v0;
     if (h->P > 1) {
-        if (int rc = band_selection(h, v, true, st)) return rc;
-        // a band holds about 1/P of a segment's cells: CTAs per segment so that a
+        if (int rc = band_list_prepare(h, v, st)) return rc;
+        // a band lists about 1/P of a segment's cells: CTAs per segment so that a
         // thread has about one cell, as in the whole-grid scatter
         const int64_t split = std::max(1, EPB_SEL_SCATTER_SPLIT / h->P);
-        blocks = (unsigned)(((v.n + kSelChunk - 1) / kSelChunk) * split);
+        const unsigned blocks = (unsigned)(((v.n + kSelChunk - 1) / kSelChunk) * split);
+        k_scatter_listed<<<blocks, 256, 0, st>>>(v, geom(h), qscale, (unsigned long long*)grid, h->row0,
+                                                 h->row0 + h->RB, h->bl, h->flags);
+        EPB_LAUNCHED(h, "k_scatter_listed launch");
+        return EPB_OK;
     }
-    k_scatter<false><<<blocks, 256, 0, st>>>(v, geom(h), qscale, (unsigned long long*)grid, h->row0, h->row0 + h->RB,
-                                      h->flags);
+    k_scatter<false><<<cell_blocks(v.n), 256, 0, st>>>(v, geom(h), qscale, (unsigned long long*)grid, h->row0,
+                                                      h->row0 + h->RB, h->flags);
     EPB_LAUNCHED(h, "k_scatter launch");
     return EPB_OK;
 }
@@ -529,20 +540,20 @@ int tile_gather(epb_handle* h, const CellView& v, const float2* fxy, int halo, i
 int shard_gather(epb_handle* h, const CellView& v0, const float2* fxy, int halo, const float* grad_out,
                  float* grad_x, float* grad_y, cudaStream_t st) {
     if (!h->cell_order) return tile_gather(h, v0, fxy, halo, 1, grad_out, grad_x, grad_y, st);
-    CellView v = v0;
-    unsigned blocks = cell_blocks(v.n);
+    const CellView& v = v0;
     if (h->P > 1) {
-        if (h->own_valid && same_cells(h->own_key, v)) {
-            // the forward's selection of the same cells (positions are the forward's)
-            v.sel = h->own_list;
-            v.sel_n = h->own_count;
-        } else if (int rc = band_selection(h, v, false, st)) {
-            return rc;
-        }
-        blocks = (unsigned)((v.n + kSelChunk - 1) / kSelChunk);   // one CTA per segment
+        if (v.n == 0) return EPB_OK;
+        // the forward's list, checked again when the cells or their positions may differ
+        if (h->bl_force || h->bl_stale || !same_view(h->bl_key, v))
+            if (int rc = band_list_prepare(h, v, st)) return rc;
+        const unsigned blocks = (unsigned)((v.n + kSelChunk - 1) / kSelChunk);   // one CTA per segment
+        k_gather_listed<<<blocks, 256, 0, st>>>(v, geom(h), fxy, h->row0, h->row0 + h->RB, halo, grad_out, grad_x,
+                                                grad_y, h->bl, h->flags);
+        EPB_LAUNCHED(h, "k_gather_listed launch");
+        return EPB_OK;
     }
-    k_gather<false><<<blocks, 256, 0, st>>>(v, geom(h), fxy, nullptr, nullptr, h->row0, h->row0 + h->RB, halo, 1, grad_out,
-                                     grad_x, grad_y, h->flags);
+    k_gather<false><<<cell_blocks(v.n), 256, 0, st>>>(v, geom(h), fxy, nullptr, nullptr, h->row0, h->row0 + h->RB,
+                                                     halo, 1, grad_out, grad_x, grad_y, h->flags);
     EPB_LAUNCHED(h, "k_gather launch");
     return EPB_OK;
 }
@@ -1208,7 +1219,7 @@ int epb_descent_step(epb_handle* h, const epb_cells* cells, float* x, float* y, 
     DeviceGuard guard(h->dev);
     cudaStream_t st = (cudaStream_t)stream;
     EPB_CUDA(h, cudaMemsetAsync(h->linf_bits, 0, sizeof(unsigned), st));
-    h->own_valid = false;  // positions move: no selection made before this step stays valid
+    h->bl_stale = true;    // positions move: a gather before the next forward checks the band list first
     // the tile lists stay (every forward validates them against the positions it is
     // given); a gather before the next forward validates them first
     h->tb_stale = true;

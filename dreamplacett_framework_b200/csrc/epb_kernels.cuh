@@ -102,53 +102,58 @@ constexpr int kOyCache = 4;
 // ---------------------------------------------------------------------------
 // IO: c.x / c.y point into pinned host memory (read over PCIe) and every
 // visited node's position is also stored to xcopy / ycopy in device memory.
+// The fixed-point contributions of footprint f to rows [row0, row1) of the
+// density grid (grid holds those rows): one 64-bit atomic add per bin.
+__device__ __forceinline__ void deposit(const Footprint& f, const GridGeom& g, float qscale,
+                                        unsigned long long* __restrict__ grid, int row0, int row1) {
+    const int kxa = max(f.kx0, row0), kxb = min(f.kx1, row1 - 1);
+    if (EPB_OY_CACHE && f.ky1 - f.ky0 < kOyCache) {
+        // the column overlaps are the same for every row: computed once
+        float oy[kOyCache];
+#pragma unroll
+        for (int j = 0; j < kOyCache; ++j)
+            oy[j] = f.ky0 + j <= f.ky1 ? bin_overlap(f.y, f.ey, g.yl, g.bsy, f.ky0 + j) : 0.0f;
+        for (int kx = kxa; kx <= kxb; ++kx) {
+            const float oxr = __fmul_rn(bin_overlap(f.x, f.ex, g.xl, g.bsx, kx), f.r);
+            if (oxr == 0.0f) continue;
+            unsigned long long* row = grid + (int64_t)(kx - row0) * g.N + f.ky0;
+#pragma unroll
+            for (int j = 0; j < kOyCache; ++j) {
+                if (f.ky0 + j > f.ky1) break;
+                const long long q = __float2ll_rn(__fmul_rn(__fmul_rn(oxr, oy[j]), qscale));
+                if (q != 0) atomicAdd(row + j, (unsigned long long)q);
+            }
+        }
+        return;
+    }
+    for (int kx = kxa; kx <= kxb; ++kx) {
+        const float oxr = __fmul_rn(bin_overlap(f.x, f.ex, g.xl, g.bsx, kx), f.r);
+        if (oxr == 0.0f) continue;
+        unsigned long long* row = grid + (int64_t)(kx - row0) * g.N;
+        for (int ky = f.ky0; ky <= f.ky1; ++ky) {
+            const float a = __fmul_rn(oxr, bin_overlap(f.y, f.ey, g.yl, g.bsy, ky));
+            const long long q = __float2ll_rn(__fmul_rn(a, qscale));
+            if (q != 0) atomicAdd(row + ky, (unsigned long long)q);
+        }
+    }
+}
+
 template <bool IO = false>
 __global__ void EPB_SCATTER_BOUNDS
 k_scatter(CellView c, GridGeom g, float qscale, unsigned long long* __restrict__ grid,
           int row0, int row1, unsigned* __restrict__ flags, float* __restrict__ xcopy = nullptr,
           float* __restrict__ ycopy = nullptr) {
     // grid holds rows [row0, row1) of the density grid; footprints are clipped to them.
-    // Cells of a selection are known to meet the band: they skip the band test.
-    const int blo = c.sel ? 0 : row0, bhi = c.sel ? g.M : row1;
     for_each_cell(c, [&](int64_t node) {
         if constexpr (IO) {
             xcopy[node] = __ldg(c.x + node);
             ycopy[node] = __ldg(c.y + node);
         }
         Footprint f;
-        const int st = cell_footprint(c, g, node, f, blo, bhi, false);
+        const int st = cell_footprint(c, g, node, f, row0, row1, false);
         if (st < 0) { atomicOr(flags, kFlagNonFinite); return; }
         if (st != 1) return;
-        const int kxa = max(f.kx0, row0), kxb = min(f.kx1, row1 - 1);
-        if (EPB_OY_CACHE && f.ky1 - f.ky0 < kOyCache) {
-            // the column overlaps are the same for every row: computed once
-            float oy[kOyCache];
-#pragma unroll
-            for (int j = 0; j < kOyCache; ++j)
-                oy[j] = f.ky0 + j <= f.ky1 ? bin_overlap(f.y, f.ey, g.yl, g.bsy, f.ky0 + j) : 0.0f;
-            for (int kx = kxa; kx <= kxb; ++kx) {
-                const float oxr = __fmul_rn(bin_overlap(f.x, f.ex, g.xl, g.bsx, kx), f.r);
-                if (oxr == 0.0f) continue;
-                unsigned long long* row = grid + (int64_t)(kx - row0) * g.N + f.ky0;
-#pragma unroll
-                for (int j = 0; j < kOyCache; ++j) {
-                    if (f.ky0 + j > f.ky1) break;
-                    const long long q = __float2ll_rn(__fmul_rn(__fmul_rn(oxr, oy[j]), qscale));
-                    if (q != 0) atomicAdd(row + j, (unsigned long long)q);
-                }
-            }
-            return;
-        }
-        for (int kx = kxa; kx <= kxb; ++kx) {
-            const float oxr = __fmul_rn(bin_overlap(f.x, f.ex, g.xl, g.bsx, kx), f.r);
-            if (oxr == 0.0f) continue;
-            unsigned long long* row = grid + (int64_t)(kx - row0) * g.N;
-            for (int ky = f.ky0; ky <= f.ky1; ++ky) {
-                const float a = __fmul_rn(oxr, bin_overlap(f.y, f.ey, g.yl, g.bsy, ky));
-                const long long q = __float2ll_rn(__fmul_rn(a, qscale));
-                if (q != 0) atomicAdd(row + ky, (unsigned long long)q);
-            }
-        }
+        deposit(f, g, qscale, grid, row0, row1);
     });
 }
 
@@ -718,72 +723,6 @@ k_row_inv(RowInvArgs a) {
     }
 }
 
-// ---------------------------------------------------------------------------
-// Band selection (sharded grids): the cells a row band's scatter or gather
-// visits, listed so those kernels run full warps instead of testing every cell.
-// Only the x data is read.  Two lists, each optional: `meet`, the cells whose
-// rows meet [row0, row1) (the scatter; cells that contribute nothing go to the
-// list of the band holding row 0, which then reports their non-finite data),
-// and `own`, the cells whose first row is in [row0, row1) (the gather).  Cells
-// with non-finite x data are flagged here.  Each CTA compacts a fixed segment
-// of kSelChunk cells (no global atomics); the consumers run one or more CTAs
-// per segment.
-// ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256)
-k_band_select(CellView c, GridGeom g, int row0, int row1, int* __restrict__ meet, int* __restrict__ meet_n,
-              int* __restrict__ own, int* __restrict__ own_n, unsigned* __restrict__ flags) {
-    // CTA s compacts cells [s * kSelChunk, (s + 1) * kSelChunk) into list[s * kSelChunk ...]
-    // in increasing order and writes their number to list_n[s], for each list given
-    __shared__ int wtot[2][8];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int64_t seg0 = (int64_t)blockIdx.x * kSelChunk;
-    int run_m = 0, run_o = 0;
-    unsigned bad = 0;
-    for (int r = 0; r < kSelChunk / 256; ++r) {
-        const int64_t i = seg0 + r * 256 + threadIdx.x;
-        bool in_m = false, in_o = false;
-        if (i < c.n) {
-            const int64_t node = cell_node(c, i);
-            float x = __ldg(c.x + node);
-            if (c.ox) x = __fadd_rn(x, __ldg(c.ox + node));
-            const float sx = __ldg(c.sx + node);
-            if (!isfinite(x) || !isfinite(sx)) {
-                bad = 1;
-            } else {
-                const int kx0 = bin_floor(x, g.xl, g.bsx, g.ibsx, g.M);
-                const int kx1 = min(bin_floor(__fadd_rn(x, sx), g.xl, g.bsx, g.ibsx, g.M), g.M - 1);
-                const bool empty = !(sx > 0.0f) || kx0 > kx1;
-                in_m = empty ? row0 == 0 : !(kx1 < row0 || kx0 >= row1);
-                in_o = !empty && kx0 >= row0 && kx0 < row1;
-            }
-        }
-        const unsigned mm = __ballot_sync(0xffffffffu, in_m), mo = __ballot_sync(0xffffffffu, in_o);
-        if (lane == 0) {
-            wtot[0][warp] = __popc(mm);
-            wtot[1][warp] = __popc(mo);
-        }
-        __syncthreads();
-        int bm = 0, tm = 0, bo = 0, to = 0;
-#pragma unroll
-        for (int w = 0; w < 8; ++w) {
-            bm += w < warp ? wtot[0][w] : 0;
-            tm += wtot[0][w];
-            bo += w < warp ? wtot[1][w] : 0;
-            to += wtot[1][w];
-        }
-        const unsigned below = (1u << lane) - 1u;
-        if (meet && in_m) meet[seg0 + run_m + bm + __popc(mm & below)] = (int)i;
-        if (own && in_o) own[seg0 + run_o + bo + __popc(mo & below)] = (int)i;
-        run_m += tm;
-        run_o += to;
-        __syncthreads();
-    }
-    if (threadIdx.x == 0) {
-        if (meet_n) meet_n[blockIdx.x] = run_m;
-        if (own_n) own_n[blockIdx.x] = run_o;
-    }
-    if (bad) atomicOr(flags, kFlagNonFinite);
-}
 
 // Atomic-rate probe: footprint i of fw x fh bins at a hashed bin of the grid,
 // one 64-bit atomic add per bin with its result unused (the scatter's
@@ -804,8 +743,202 @@ k_atomic_probe(unsigned long long* __restrict__ grid, int M, int N, int64_t n, i
 }
 
 // ---------------------------------------------------------------------------
+// Band lists of a shard (cell order): the cells whose rows meet the band widened
+// by kBandMargin rows on each side, kept across calls.  Each segment of
+// kSelChunk cells keeps its listed cells in increasing order at
+// sel[s * kSelChunk + j], j < cnt[s], and beside each the cell's static inputs
+// (sizes, offsets, ratio) copied at list time, so the scatter and the gather
+// read those contiguously and gather only the positions by node.
+//
+// Every forward, k_band_update checks each segment: when one of its unlisted
+// cells now meets the band itself, that segment alone is listed again (a
+// listed cell that has left the band costs a band test and nothing else).
+// Segments are independent, so the check and the listing are one kernel with
+// no grid-wide step.  The static inputs are read at list time: a caller that
+// changes sizes, offsets or ratio in place between calls with the same arrays
+// must hand in other arrays (or a new handle).
+// ---------------------------------------------------------------------------
+constexpr int kBandMargin = 8;
+
+struct BandList {
+    int* sel;               // [nseg * kSelChunk] cell indices, per segment
+    int* cnt;               // [nseg]
+    float4* geo;            // [nseg * kSelChunk] sx, sy, ox, oy of the listed cell (0 for absent offsets)
+    float* r;               // [nseg * kSelChunk] ratio (1 when absent)
+    unsigned char* listed;  // [n] 1 when the cell is in the list
+};
+
+// Whether a cell's x extent [xe, xe + sx] (offset added, finite) reaches the
+// coordinates (lo_c, hi_c) of a band widened by some rows, or its footprint
+// may be empty (a non-positive width, or a start past the grid's last row):
+// a superset of the cells whose bin rows meet the band (an edge band's outer
+// side is open, as bins clamp cells beyond the die into the first and last
+// rows), decided with two additions and compares instead of bin arithmetic.
+__device__ __forceinline__ bool band_reaches(float xe, float sx, float lo_c, float hi_c, float last_c) {
+    return !(sx > 0.0f) || xe >= last_c || (xe < hi_c && __fadd_rn(xe, sx) > lo_c);
+}
+
+// The coordinate of row k's lower edge, as bin_floor computes it.
+__device__ __forceinline__ float row_edge(const GridGeom& g, int k) {
+    return __fadd_rn(g.xl, __fmul_rn((float)k, g.bsx));
+}
+
+// CTA s checks segment s of the cells (kSelChunk / 256 cells a thread, all
+// their loads issued first) and lists the segment again when an unlisted cell
+// reaches the band [row0, row1) widened by one row, or when force.  A listing
+// takes the cells that reach the band widened by kBandMargin rows, so a cell
+// must travel that far before it makes its segment list again.  Cells with
+// non-finite x data are flagged (and never listed).
+__global__ void __launch_bounds__(256)
+k_band_update(CellView c, GridGeom g, int row0, int row1, BandList b, int force, unsigned* __restrict__ flags) {
+    constexpr int R = kSelChunk / 256;
+    const int64_t seg0 = (int64_t)blockIdx.x * kSelChunk;
+    float x[R], ox[R], sx[R];
+    unsigned char was[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int64_t i = seg0 + r * 256 + threadIdx.x;
+        x[r] = ox[r] = 0.0f;
+        sx[r] = 1.0f;
+        was[r] = 1;
+        if (i < c.n) {
+            const int64_t node = cell_node(c, i);
+            was[r] = b.listed[i];
+            x[r] = __ldg(c.x + node);
+            ox[r] = c.ox ? __ldg(c.ox + node) : 0.0f;
+            sx[r] = __ldg(c.sx + node);
+        }
+    }
+    const float last_c = row_edge(g, g.M - 1);
+    const float lo1 = row0 == 0 ? -INFINITY : row_edge(g, row0 - 1);
+    const float hi1 = row1 >= g.M ? INFINITY : row_edge(g, row1 + 1);
+    const float loM = row0 == 0 ? -INFINITY : row_edge(g, max(row0 - kBandMargin, 0));
+    const float hiM = row1 >= g.M ? INFINITY : row_edge(g, min(row1 + kBandMargin, g.M));
+    bool need = false, in[R];
+    unsigned bad = 0;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int64_t i = seg0 + r * 256 + threadIdx.x;
+        const float xe = c.ox ? __fadd_rn(x[r], ox[r]) : x[r];
+        const bool ok = i < c.n && isfinite(xe) && isfinite(sx[r]);
+        bad |= (i < c.n && !ok) ? 1u : 0u;
+        need |= ok && !was[r] && band_reaches(xe, sx[r], lo1, hi1, last_c);
+        in[r] = ok && band_reaches(xe, sx[r], loM, hiM, last_c);
+    }
+    if (bad) atomicOr(flags, kFlagNonFinite);
+    if (!__syncthreads_or(need || force)) return;
+    // list the segment again
+    __shared__ int wtot[8];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int run = 0;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int64_t i = seg0 + r * 256 + threadIdx.x;
+        if (i < c.n) b.listed[i] = in[r] ? 1 : 0;
+        const unsigned m = __ballot_sync(0xffffffffu, in[r]);
+        if (lane == 0) wtot[warp] = __popc(m);
+        __syncthreads();
+        int base = 0, tot = 0;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+            base += w < warp ? wtot[w] : 0;
+            tot += wtot[w];
+        }
+        if (in[r]) {
+            const int64_t node = cell_node(c, i);
+            const int64_t slot = seg0 + run + base + __popc(m & ((1u << lane) - 1u));
+            b.sel[slot] = (int)i;
+            b.geo[slot] = make_float4(sx[r], __ldg(c.sy + node), ox[r], c.oy ? __ldg(c.oy + node) : 0.0f);
+            b.r[slot] = c.ratio ? __ldg(c.ratio + node) : 1.0f;
+        }
+        run += tot;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) b.cnt[blockIdx.x] = run;
+}
+
+// A listed cell's inputs: the positions by node, the rest from its list slot.
+__device__ __forceinline__ CellData listed_cell(const CellView& c, const BandList& b, int64_t slot, int64_t node) {
+    CellData d;
+    const float4 q = b.geo[slot];
+    d.x = __ldg(c.x + node);
+    d.y = __ldg(c.y + node);
+    d.sx = q.x; d.sy = q.y; d.ox = q.z; d.oy = q.w;
+    d.r = b.r[slot];
+    return d;
+}
+
+// Scatter of a band's listed cells into rows [row0, row1) (grid holds them).
+// G consecutive CTAs share a segment when the grid has G CTAs per segment.
+__global__ void EPB_SCATTER_BOUNDS
+k_scatter_listed(CellView c, GridGeom g, float qscale, unsigned long long* __restrict__ grid, int row0, int row1,
+                 BandList b, unsigned* __restrict__ flags) {
+    const int64_t nseg = (c.n + kSelChunk - 1) / kSelChunk;
+    const int64_t G = gridDim.x >= nseg ? gridDim.x / nseg : 1;
+    const int64_t slots = gridDim.x / G;
+    if (blockIdx.x >= slots * G) return;
+    const int sub = (int)(blockIdx.x % G);
+    for (int64_t s = blockIdx.x / G; s < nseg; s += slots) {
+        const int cnt = b.cnt[s];
+        for (int j = sub * (int)blockDim.x + threadIdx.x; j < cnt; j += (int)(G * blockDim.x)) {
+            const int64_t slot = s * kSelChunk + j;
+            const CellData d = listed_cell(c, b, slot, cell_node(c, b.sel[slot]));
+            Footprint f;
+            const int st = footprint_of(c, g, d, f);
+            if (st < 0) { atomicOr(flags, kFlagNonFinite); continue; }
+            if (st != 1) continue;
+            deposit(f, g, qscale, grid, row0, row1);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
 // Gather: grad[node] = -g * ratio * sum (ox*oy) * field
 // ---------------------------------------------------------------------------
+// The overlap-weighted field sums (ax, ay) of footprint f over field maps that
+// hold rows [row0, row1 + halo); rows past them are dropped and flagged.
+__device__ __forceinline__ void gather_sum(const Footprint& f, const GridGeom& g, const float2* __restrict__ fxy,
+                                           const float* __restrict__ fx, const float* __restrict__ fy, int row0,
+                                           int row1, int halo, unsigned* __restrict__ flags, float& ax, float& ay) {
+    int kxb = f.kx1;
+    if (kxb >= row1 + halo) {
+        atomicOr(flags, kFlagHalo);
+        kxb = row1 + halo - 1;
+    }
+    if (EPB_OY_CACHE && fxy && f.ky1 - f.ky0 < kOyCache) {
+        // column overlaps computed once per cell; the same products in the same order
+        float oy[kOyCache];
+#pragma unroll
+        for (int j = 0; j < kOyCache; ++j)
+            oy[j] = f.ky0 + j <= f.ky1 ? bin_overlap(f.y, f.ey, g.yl, g.bsy, f.ky0 + j) : 0.0f;
+        for (int kx = f.kx0; kx <= kxb; ++kx) {
+            const float ox = bin_overlap(f.x, f.ex, g.xl, g.bsx, kx);
+            const float2* rowp = fxy + (int64_t)(kx - row0) * g.N + f.ky0;
+#pragma unroll
+            for (int j = 0; j < kOyCache; ++j) {
+                if (f.ky0 + j > f.ky1) break;
+                const float w = ox * oy[j];
+                const float2 fv = __ldg(rowp + j);
+                ax = fmaf(w, fv.x, ax);
+                ay = fmaf(w, fv.y, ay);
+            }
+        }
+        return;
+    }
+    for (int kx = f.kx0; kx <= kxb; ++kx) {
+        const float ox = bin_overlap(f.x, f.ex, g.xl, g.bsx, kx);
+        const int64_t rowoff = (int64_t)(kx - row0) * g.N;
+        for (int ky = f.ky0; ky <= f.ky1; ++ky) {
+            const float w = ox * bin_overlap(f.y, f.ey, g.yl, g.bsy, ky);
+            float2 fv;
+            if (fxy) fv = __ldg(fxy + rowoff + ky);
+            else fv = make_float2(__ldg(fx + rowoff + ky), __ldg(fy + rowoff + ky));
+            ax = fmaf(w, fv.x, ax);
+            ay = fmaf(w, fv.y, ay);
+        }
+    }
+}
+
 // IO: the gradients are also stored to host_gx / host_gy in pinned host memory
 // (written over PCIe).
 template <bool IO = false>
@@ -826,42 +959,7 @@ k_gather(CellView c, GridGeom g, const float2* __restrict__ fxy,
         if (owned_only && st != 1) return;
         if (st == 1) {
             r = f.r;
-            int kxb = f.kx1;
-            if (kxb >= row1 + halo) {
-                atomicOr(flags, kFlagHalo);
-                kxb = row1 + halo - 1;
-            }
-            if (EPB_OY_CACHE && fxy && f.ky1 - f.ky0 < kOyCache) {
-                // column overlaps computed once per cell; the same products in the same order
-                float oy[kOyCache];
-#pragma unroll
-                for (int j = 0; j < kOyCache; ++j)
-                    oy[j] = f.ky0 + j <= f.ky1 ? bin_overlap(f.y, f.ey, g.yl, g.bsy, f.ky0 + j) : 0.0f;
-                for (int kx = f.kx0; kx <= kxb; ++kx) {
-                    const float ox = bin_overlap(f.x, f.ex, g.xl, g.bsx, kx);
-                    const float2* rowp = fxy + (int64_t)(kx - row0) * g.N + f.ky0;
-#pragma unroll
-                    for (int j = 0; j < kOyCache; ++j) {
-                        if (f.ky0 + j > f.ky1) break;
-                        const float w = ox * oy[j];
-                        const float2 fv = __ldg(rowp + j);
-                        ax = fmaf(w, fv.x, ax);
-                        ay = fmaf(w, fv.y, ay);
-                    }
-                }
-            } else
-            for (int kx = f.kx0; kx <= kxb; ++kx) {
-                const float ox = bin_overlap(f.x, f.ex, g.xl, g.bsx, kx);
-                const int64_t rowoff = (int64_t)(kx - row0) * g.N;
-                for (int ky = f.ky0; ky <= f.ky1; ++ky) {
-                    const float w = ox * bin_overlap(f.y, f.ey, g.yl, g.bsy, ky);
-                    float2 fv;
-                    if (fxy) fv = __ldg(fxy + rowoff + ky);
-                    else fv = make_float2(__ldg(fx + rowoff + ky), __ldg(fy + rowoff + ky));
-                    ax = fmaf(w, fv.x, ax);
-                    ay = fmaf(w, fv.y, ay);
-                }
-            }
+            gather_sum(f, g, fxy, fx, fy, row0, row1, halo, flags, ax, ay);
         }
         const float s = gscale * r;
         grad_x[node] = s * ax;
@@ -871,10 +969,10 @@ k_gather(CellView c, GridGeom g, const float2* __restrict__ fxy,
             host_gy[node] = s * ay;
         }
     };
-    if (c.sel || (row0 == 0 && row1 >= g.M)) {
-        // the whole grid, or a selection (the band's own cells, which need no band
-        // test): a footprint from loaded inputs, the next cell's loads in flight
-        // while the current cell's fields are read (one round trip per cell, not two)
+    if (row0 == 0 && row1 >= g.M) {
+        // the whole grid: a footprint from loaded inputs, the next cell's loads in
+        // flight while the current cell's fields are read (one round trip per cell,
+        // not two)
         for_each_cell_prefetched(c, [&](int64_t node, const CellData& d) {
             Footprint f;
             finish(node, footprint_of(c, g, d, f), f);
@@ -887,6 +985,52 @@ k_gather(CellView c, GridGeom g, const float2* __restrict__ fxy,
         const int st = cell_footprint(c, g, node, f, row0, row1, owned_only != 0);
         finish(node, st, f);
     });
+}
+
+// Gather of a band's own listed cells (first bin row in [row0, row1)) from
+// field maps holding rows [row0, row1 + halo).  One CTA
+// per segment, the next listed cell's inputs loaded while the current cell's
+// fields are read.  Other entries of grad_x / grad_y are left as they are.
+__global__ void EPB_GATHER_BOUNDS
+k_gather_listed(CellView c, GridGeom g, const float2* __restrict__ fxy, int row0, int row1, int halo,
+                const float* __restrict__ grad_out, float* __restrict__ grad_x, float* __restrict__ grad_y, BandList b,
+                unsigned* __restrict__ flags) {
+    const float gscale = grad_out ? -__ldg(grad_out) : -1.0f;
+    const int64_t nseg = (c.n + kSelChunk - 1) / kSelChunk;
+    for (int64_t s = blockIdx.x; s < nseg; s += gridDim.x) {
+        const int cnt = b.cnt[s];
+        int j = threadIdx.x;
+        if (j >= cnt) continue;
+        int64_t slot = s * kSelChunk + j;
+        int64_t node = cell_node(c, b.sel[slot]);
+        CellData cur = listed_cell(c, b, slot, node);
+        for (;;) {
+            const int jn = j + (int)blockDim.x;
+            int64_t nslot = slot, nnode = node;
+            CellData nxt = cur;
+            if (jn < cnt) {
+                nslot = s * kSelChunk + jn;
+                nnode = cell_node(c, b.sel[nslot]);
+                nxt = listed_cell(c, b, nslot, nnode);
+            }
+            Footprint f;
+            const int st = footprint_of(c, g, cur, f);
+            if (st < 0) {
+                atomicOr(flags, kFlagNonFinite);
+            } else if (st == 1 && f.kx0 >= row0 && f.kx0 < row1) {
+                float ax = 0.0f, ay = 0.0f;
+                gather_sum(f, g, fxy, nullptr, nullptr, row0, row1, halo, flags, ax, ay);
+                const float sc = gscale * f.r;
+                grad_x[node] = sc * ax;
+                grad_y[node] = sc * ay;
+            }
+            if (jn >= cnt) break;
+            j = jn;
+            slot = nslot;
+            node = nnode;
+            cur = nxt;
+        }
+    }
 }
 
 // ---------------------------------------------------------------------------

@@ -32,40 +32,20 @@ struct CellView {
     int64_t b0, n0;  // first range: nodes b0 .. b0+n0-1
     int64_t b1;      // second range starts at node b1
     int64_t n;       // total cells (n0 + second range length)
-    // optional selection: when sel is set, the cells visited are, for each
-    // segment s < ceil(n / kSelChunk), sel[s * kSelChunk + j] for j < sel_n[s]
-    // (cell indices in [0, n), increasing within a segment)
-    const int* __restrict__ sel;
-    const int* __restrict__ sel_n;
 };
 
-constexpr int kSelChunk = 2048;   // cells per selection segment
+constexpr int kSelChunk = 2048;   // cells per segment of a shard's band list
 
 __device__ __forceinline__ int64_t cell_node(const CellView& c, int64_t i) {
     return i < c.n0 ? c.b0 + i : c.b1 + (i - c.n0);
 }
 
-// Visit every cell of v (all cells, or the selected ones) with body(node), the
-// work spread over the grid: a grid-stride loop, or G CTAs per segment when the
-// grid has G times as many CTAs as there are segments (else one).
+// Visit every cell of v with body(node), the work spread over the grid by a
+// grid-stride loop.
 template <typename F>
 __device__ __forceinline__ void for_each_cell(const CellView& c, F&& body) {
-    if (c.sel) {
-        // G consecutive CTAs share a segment when the grid has G CTAs per segment
-        const int64_t nseg = (c.n + kSelChunk - 1) / kSelChunk;
-        const int64_t G = gridDim.x >= nseg ? gridDim.x / nseg : 1;
-        const int64_t slots = gridDim.x / G;
-        if (blockIdx.x >= slots * G) return;
-        const int sub = (int)(blockIdx.x % G);
-        for (int64_t s = blockIdx.x / G; s < nseg; s += slots) {
-            const int cnt = c.sel_n[s];
-            for (int j = sub * (int)blockDim.x + threadIdx.x; j < cnt; j += (int)(G * blockDim.x))
-                body(cell_node(c, c.sel[s * kSelChunk + j]));
-        }
-    } else {
-        const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-        for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < c.n; i += stride) body(cell_node(c, i));
-    }
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < c.n; i += stride) body(cell_node(c, i));
 }
 
 __device__ __forceinline__ int bin_floor(float v, float origin, float bs, float ibs, int nb) {
@@ -152,44 +132,18 @@ __device__ __forceinline__ int footprint_of(const CellView& c, const GridGeom& g
 // works on the current one, so that load overlaps the body's own reads.
 template <typename F>
 __device__ __forceinline__ void for_each_cell_prefetched(const CellView& c, F&& body) {
-    if (c.sel) {
-        const int64_t nseg = (c.n + kSelChunk - 1) / kSelChunk;
-        for (int64_t s = blockIdx.x; s < nseg; s += gridDim.x) {
-            const int cnt = c.sel_n[s];
-            const int* lst = c.sel + s * kSelChunk;
-            int j = threadIdx.x;
-            if (j >= cnt) continue;
-            int64_t node = cell_node(c, lst[j]);
-            CellData cur = load_cell(c, node);
-            for (;;) {
-                const int jn = j + (int)blockDim.x;
-                int64_t nnode = node;
-                CellData nxt = cur;
-                if (jn < cnt) {
-                    nnode = cell_node(c, lst[jn]);
-                    nxt = load_cell(c, nnode);
-                }
-                body(node, cur);
-                if (jn >= cnt) break;
-                j = jn;
-                node = nnode;
-                cur = nxt;
-            }
-        }
-    } else {
-        const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-        int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-        if (i >= c.n) return;
-        CellData cur = load_cell(c, cell_node(c, i));
-        for (;;) {
-            const int64_t inext = i + stride;
-            CellData nxt = cur;
-            if (inext < c.n) nxt = load_cell(c, cell_node(c, inext));
-            body(cell_node(c, i), cur);
-            if (inext >= c.n) break;
-            cur = nxt;
-            i = inext;
-        }
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= c.n) return;
+    CellData cur = load_cell(c, cell_node(c, i));
+    for (;;) {
+        const int64_t inext = i + stride;
+        CellData nxt = cur;
+        if (inext < c.n) nxt = load_cell(c, cell_node(c, inext));
+        body(cell_node(c, i), cur);
+        if (inext >= c.n) break;
+        cur = nxt;
+        i = inext;
     }
 }
 

@@ -78,8 +78,12 @@ typedef enum epb_status {
 /* epb_config.flags selects how the cells reach the grid:
  * EPB_CONFIG_CELL_ORDER (the default, also when flags is 0): one 64-bit
  *   global atomic add per (cell, bin) into an int64 grid, and a gather that
- *   reads the fields per cell in node order (a shard first selects the cells
- *   that meet its band);
+ *   reads the fields per cell in node order.  A shard keeps a list of the
+ *   cells that meet its band widened by 8 rows, with their sizes, offsets and
+ *   ratio copied beside it; every forward checks the unlisted cells against
+ *   the band and lists again (on the device) when one came in.  The sizes,
+ *   offsets and ratio are read when the list is made: change them in place
+ *   and the shard needs other arrays (or a new handle);
  * EPB_CONFIG_TILES: cell tiles -- each cell listed in the 32 x 32-bin tiles its
  *   footprint (widened by 2 bins) meets, the lists kept across calls and
  *   validated against the positions of every forward (a shard rebuilds its
@@ -212,10 +216,11 @@ int epb_shard_columns(epb_handle* h, const float* t1_recv, epb_stream stream, fl
  * match the epb_shard_columns call (non-NULL potential_band) */
 int epb_shard_rows_inverse(epb_handle* h, const float* g_recv, epb_stream stream, float* potential_band,
                            float* field_x_band, float* field_y_band, float* fxy_band);
-/* gradient of the cells whose first bin row lies in this band.  Given the
- * same cell arrays and ranges as the shard's last forward (and no
- * epb_descent_step since), the gather reuses that forward's list of the band's
- * cells.  The positions must be the ones the forward saw, as in the
+/* gradient of the cells whose first bin row lies in this band (other entries
+ * of grad_x / grad_y are left as they are).  Given the same cell arrays and
+ * ranges as the shard's last forward (and no epb_descent_step since), the
+ * gather uses the band list that forward checked; otherwise it checks the
+ * list first.  The positions must be the ones the forward saw, as in the
  * reference, whose backward reads the pos the forward saved
  * (integration/scatter_ttnn_client.py:833). */
 int epb_shard_gather(epb_handle* h, const epb_cells* cells, const float* fxy_ext, int32_t halo_rows,

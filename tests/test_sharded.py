@@ -210,11 +210,11 @@ def _cloned(c):
 
 
 @pytest.mark.gpu
-def test_shard_gather_reuses_forward_selection(cuda_device):
-    """A shard's gather reuses the list of its own cells that its forward made
-    when it gets the same cell arrays, recomputes it for other arrays, and drops
-    it once epb_descent_step has moved the cells: every way gives the gradient
-    of a fresh selection."""
+def test_shard_gather_reuses_forward_band_list(cuda_device):
+    """A shard's gather uses the band list its forward kept when it gets the
+    same cell arrays, lists again for other arrays, and checks the list again
+    once epb_descent_step has moved the cells: every way gives the gradient of
+    a fresh listing."""
     import ctypes
     from dreamplacett_framework_b200 import _lib
     from dreamplacett_framework_b200.sharded import EngineShard, halo_rows_for
@@ -300,6 +300,54 @@ def test_shard_stages_reject_misaligned_buffers(cuda_device):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("P", [2, 4])
+def test_band_lists_follow_moving_cells(cuda_device, P):
+    """The band lists are kept across forwards and checked against the
+    positions every time.  Cells moved in place by less than the list margin
+    (nothing to list again), then by tens of bins (cells enter other bands and
+    are listed), then a little again: each time every band's density is the
+    one-GPU density bit for bit, and the bands' gathers over the one-GPU field
+    maps give the one-GPU gradients bit for bit (each cell by its owner band)."""
+    from dreamplacett_framework_b200.engine import ElectricPotentialEngine
+    from dreamplacett_framework_b200.sharded import EngineShard, halo_rows_for
+    p = synth.make_placement("c3", scale=0.1, grid=512)
+    M, N = p.num_bins_x, p.num_bins_y
+    cells = _shard_inputs(p, cuda_device)
+    n = p.num_nodes
+    shards = [EngineShard(M, N, p.xl, p.yl, p.xh, p.yh, P, q, cuda_device) for q in range(P)]
+    gen = torch.Generator(device=cuda_device).manual_seed(3)
+    try:
+        RB = shards[0].RB
+        H = halo_rows_for(float(np.max(p.size_x_clamped)), shards[0].bin_size_x)
+        dens = torch.zeros(P, RB * N, device=cuda_device)
+        t1 = torch.zeros(P, RB * N, device=cuda_device)
+        with ElectricPotentialEngine(M, N, p.xl, p.yl, p.xh, p.yh, device=cuda_device) as eng:
+            for bins in (0.0, 3.0, 30.0, 2.0):
+                if bins:
+                    for a, lo, hi, bs in ((cells.x, p.xl, p.xh, shards[0].bin_size_x),
+                                          (cells.y, p.yl, p.yh, shards[0].bin_size_y)):
+                        step = (torch.rand(n, generator=gen, device=cuda_device) * 2 - 1) * bins * bs
+                        a.add_(step).clamp_(lo, hi - 1.0)
+                ref = {k: v.clone() for k, v in eng.forward(cells).items()}
+                rgx, rgy = (g.clone() for g in eng.backward(cells))
+                gx = torch.zeros(n, device=cuda_device)
+                gy = torch.zeros(n, device=cuda_device)
+                for q, be in enumerate(shards):
+                    be.rows_forward(cells, dens[q], t1[q])
+                    r0, h = q * RB, (0 if q == P - 1 else H)
+                    fxy = torch.stack([ref["field_x"][r0:r0 + RB + h], ref["field_y"][r0:r0 + RB + h]], dim=-1)
+                    be.gather(cells, fxy.reshape(-1).contiguous(), h, None, gx, gy)
+                torch.cuda.synchronize()
+                assert torch.equal(dens.reshape(M, N), ref["density"]), bins
+                assert torch.equal(gx, rgx) and torch.equal(gy, rgy), bins
+                for be in shards:
+                    assert be.error_flags() == 0
+    finally:
+        for be in shards:
+            be.close()
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("path", ["cell_order", "tiles"])
 @pytest.mark.parametrize("P", [2, 4, 8])
 def test_shards_on_one_gpu_match_single_gpu(cuda_device, P, path):
@@ -308,8 +356,8 @@ def test_shards_on_one_gpu_match_single_gpu(cuda_device, P, path):
     transport moves: the density is the one-GPU density bit for bit, the fields,
     energy and summed gradients agree within 1e-5.  At 2048² and P >= 4 a band's
     row pass and a strip's column pass launch fewer CTAs than the GPU has SMs, so
-    this covers their half-size CTAs.  Both shard paths: cells selected per
-    call in cell order (the default), or each band's tile lists."""
+    this covers their half-size CTAs.  Both shard paths: the band lists in cell
+    order (the default), or each band's tile lists."""
     from dreamplacett_framework_b200 import _lib
     from dreamplacett_framework_b200.engine import ElectricPotentialEngine
     from dreamplacett_framework_b200.sharded import EngineShard, halo_rows_for
