@@ -188,6 +188,60 @@ def wirelength_item(p, dev, flush, peak, K=200, W=5):
             "error_flags": op.error_flags()}
 
 
+def shard_stages_item(p, dev, P, flush, K=50, W=5):
+    """One rank's own work in a P-way row-band split, run on one GPU for the
+    first and the last band: epb_shard_rows_forward (band-list update, listed
+    scatter, convert + row DCT-II) and epb_shard_gather over given field maps,
+    each timed with CUDA events per call, L2 flushed before each.  The column
+    pass and the exchanges are left out (they need the other ranks)."""
+    import numpy as np
+    import torch
+    from dreamplacett_framework_b200.engine import CellTensors
+    from dreamplacett_framework_b200.sharded import EngineShard, halo_rows_for
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dev)
+    cells = CellTensors(t(p.x), t(p.y), t(p.size_x_clamped), t(p.size_y_clamped), t(p.offset_x), t(p.offset_y),
+                        t(p.ratio), ranges=p.ranges)
+    M, N = p.num_bins_x, p.num_bins_y
+    out = {"workload": f"{args_config_name(p)}: one band of a {P}-way split on one GPU, rows_forward + gather",
+           "bands": {}}
+    for q in sorted({0, P - 1}):
+        be = EngineShard(M, N, p.xl, p.yl, p.xh, p.yh, P, q, dev)
+        try:
+            RB = be.RB
+            H = 0 if q == P - 1 else halo_rows_for(float(np.max(p.size_x_clamped)), be.bin_size_x)
+            dens = torch.zeros(RB * N, device=dev)
+            t1 = torch.zeros(RB * N, device=dev)
+            fxy = torch.randn((RB + H) * N * 2, device=dev, generator=torch.Generator(device=dev).manual_seed(1))
+            gx = torch.zeros(p.num_nodes, device=dev)
+            gy = torch.zeros(p.num_nodes, device=dev)
+            for _ in range(W):
+                be.rows_forward(cells, dens, t1)
+                be.gather(cells, fxy, H, None, gx, gy)
+            torch.cuda.synchronize(dev)
+            ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K)]
+            for e in ev:
+                flush.zero_()
+                e[0].record()
+                be.rows_forward(cells, dens, t1)
+                e[1].record()
+                flush.zero_()
+                e[2].record()
+                be.gather(cells, fxy, H, None, gx, gy)
+                e[3].record()
+            torch.cuda.synchronize(dev)
+            out["bands"][str(q)] = {
+                "rows_forward_us": 1000.0 * sum(e[0].elapsed_time(e[1]) for e in ev) / K,
+                "gather_us": 1000.0 * sum(e[2].elapsed_time(e[3]) for e in ev) / K,
+                "error_flags": be.error_flags()}
+        finally:
+            be.close()
+    return out
+
+
+def args_config_name(p):
+    return f"{p.num_cells} cells, {p.num_bins_x}x{p.num_bins_y} bins"
+
+
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -705,6 +759,11 @@ def run_sharded(args, p, dev, world, rank):
     """The headline on `world` GPUs, plus the C4 (4096^2, 2.5M cells) item."""
     from dreamplacett_framework_b200 import synth
     flush = _flush_buffer(dev)
+    if args.shard_stages > 1:
+        print(json.dumps({"config": workload_config(args, p),
+                          "shard_stages": shard_stages_item(p, dev, args.shard_stages, flush, K=args.steps,
+                                                            W=args.warmup)}), flush=True)
+        return
     if args.wirelength_only:
         peak, _ = load_peaks()
         print(json.dumps({"config": workload_config(args, p),
@@ -788,6 +847,8 @@ def main():
     ap.add_argument("--no-loop", action="store_true", help="skip the C5 loop and the wirelength line items")
     ap.add_argument("--no-configs", action="store_true", help="skip the C1 / C2 / C4 line items")
     ap.add_argument("--no-c4", action="store_true", help="multi-GPU: skip the C4 item")
+    ap.add_argument("--shard-stages", type=int, default=0, metavar="P",
+                    help="one GPU: time one band's rows_forward and gather of a P-way split (first and last band)")
     ap.add_argument("--wirelength-only", action="store_true",
                     help="one GPU: time only the wirelength op on the workload's netlist and print its item")
     ap.add_argument("--path", default="cell_order", choices=["cell_order", "tiles"],
@@ -826,6 +887,11 @@ def main():
         return
 
     flush = _flush_buffer(dev)
+    if args.shard_stages > 1:
+        print(json.dumps({"config": workload_config(args, p),
+                          "shard_stages": shard_stages_item(p, dev, args.shard_stages, flush, K=args.steps,
+                                                            W=args.warmup)}), flush=True)
+        return
     if args.wirelength_only:
         peak, _ = load_peaks()
         print(json.dumps({"config": workload_config(args, p),

@@ -501,8 +501,8 @@ int band_list_prepare(epb_handle* h, const CellView& v, cudaStream_t st) {
     if (!same_view(h->bl_key, v)) h->bl_force = true;
     const int row1 = h->row0 + h->RB;
     const int64_t nseg = (v.n + kSelChunk - 1) / kSelChunk;
-    k_band_update<<<(unsigned)std::max<int64_t>(nseg, 1), 256, 0, st>>>(v, geom(h), h->row0, row1, h->bl,
-                                                                        h->bl_force ? 1 : 0, h->flags);
+    k_band_update<<<(unsigned)std::max<int64_t>(nseg, 1), kBandThreads, 0, st>>>(v, geom(h), h->row0, row1, h->bl,
+                                                                                 h->bl_force ? 1 : 0, h->flags);
     EPB_LAUNCHED(h, "k_band_update launch");
     h->bl_force = false;
     h->bl_stale = false;

@@ -783,21 +783,23 @@ __device__ __forceinline__ float row_edge(const GridGeom& g, int k) {
     return __fadd_rn(g.xl, __fmul_rn((float)k, g.bsx));
 }
 
-// CTA s checks segment s of the cells (kSelChunk / 256 cells a thread, all
+constexpr int kBandThreads = 512;   // threads of a k_band_update CTA (one segment per CTA)
+
+// CTA s checks segment s of the cells (kSelChunk / kBandThreads cells a thread, all
 // their loads issued first) and lists the segment again when an unlisted cell
 // reaches the band [row0, row1) widened by one row, or when force.  A listing
 // takes the cells that reach the band widened by kBandMargin rows, so a cell
 // must travel that far before it makes its segment list again.  Cells with
 // non-finite x data are flagged (and never listed).
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kBandThreads)
 k_band_update(CellView c, GridGeom g, int row0, int row1, BandList b, int force, unsigned* __restrict__ flags) {
-    constexpr int R = kSelChunk / 256;
+    constexpr int R = kSelChunk / kBandThreads;
     const int64_t seg0 = (int64_t)blockIdx.x * kSelChunk;
     float x[R], ox[R], sx[R];
     unsigned char was[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
-        const int64_t i = seg0 + r * 256 + threadIdx.x;
+        const int64_t i = seg0 + r * kBandThreads + threadIdx.x;
         x[r] = ox[r] = 0.0f;
         sx[r] = 1.0f;
         was[r] = 1;
@@ -818,7 +820,7 @@ k_band_update(CellView c, GridGeom g, int row0, int row1, BandList b, int force,
     unsigned bad = 0;
 #pragma unroll
     for (int r = 0; r < R; ++r) {
-        const int64_t i = seg0 + r * 256 + threadIdx.x;
+        const int64_t i = seg0 + r * kBandThreads + threadIdx.x;
         const float xe = c.ox ? __fadd_rn(x[r], ox[r]) : x[r];
         const bool ok = i < c.n && isfinite(xe) && isfinite(sx[r]);
         bad |= (i < c.n && !ok) ? 1u : 0u;
@@ -828,19 +830,19 @@ k_band_update(CellView c, GridGeom g, int row0, int row1, BandList b, int force,
     if (bad) atomicOr(flags, kFlagNonFinite);
     if (!__syncthreads_or(need || force)) return;
     // list the segment again
-    __shared__ int wtot[8];
+    __shared__ int wtot[kBandThreads / 32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     int run = 0;
 #pragma unroll
     for (int r = 0; r < R; ++r) {
-        const int64_t i = seg0 + r * 256 + threadIdx.x;
+        const int64_t i = seg0 + r * kBandThreads + threadIdx.x;
         if (i < c.n) b.listed[i] = in[r] ? 1 : 0;
         const unsigned m = __ballot_sync(0xffffffffu, in[r]);
         if (lane == 0) wtot[warp] = __popc(m);
         __syncthreads();
         int base = 0, tot = 0;
 #pragma unroll
-        for (int w = 0; w < 8; ++w) {
+        for (int w = 0; w < kBandThreads / 32; ++w) {
             base += w < warp ? wtot[w] : 0;
             tot += wtot[w];
         }
