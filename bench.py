@@ -78,11 +78,11 @@ def sc_ga_bytes(n_cells, bins, with_convert=True):
 # build (the kernel summary under profiles/); ncu flushes caches per launch, so
 # these are cold-cache figures.
 NCU_TRAFFIC_C3 = {
-    "scatter": 72.9e6,
-    "row_fwd": 60.6e6,
+    "scatter": 73.3e6,
+    "row_fwd": 60.4e6,
     "column": 16.9e6,
-    "row_inv": 61.2e6,
-    "gather": 78.7e6,
+    "row_inv": 60.2e6,
+    "gather": 79.5e6,
 }
 
 

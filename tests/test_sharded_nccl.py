@@ -22,7 +22,7 @@ def _free_port():
     return port
 
 
-def _worker(rank, world, port, out_dir, grid, scale, transport):
+def _worker(rank, world, port, out_dir, config, grid, scale, transport):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     from dreamplacett_framework_b200 import synth
     from dreamplacett_framework_b200.engine import CellTensors
@@ -33,7 +33,7 @@ def _worker(rank, world, port, out_dir, grid, scale, transport):
                             timeout=datetime.timedelta(seconds=60), device_id=dev)
     sh = None
     try:
-        p = synth.make_placement("c3", scale=scale, grid=grid)
+        p = synth.make_placement(config, scale=scale, grid=grid)
         t = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dev)
         cells = CellTensors(t(p.x), t(p.y), t(p.size_x_clamped), t(p.size_y_clamped), t(p.offset_x),
                             t(p.offset_y), t(p.ratio), ranges=p.ranges)
@@ -79,15 +79,17 @@ def _worker(rank, world, port, out_dir, grid, scale, transport):
 
 
 @pytest.mark.parametrize("transport", ["nccl", "peer"])
-@pytest.mark.parametrize("grid,scale", [(1024, 0.2), (2048, 1.0)])
-def test_nccl_shards_match_single_gpu(cuda_device, tmp_path, grid, scale, transport):
+@pytest.mark.parametrize("config,grid,scale", [("c3", 1024, 0.2), ("c3", 2048, 1.0), ("c4", None, 1.0)])
+def test_nccl_shards_match_single_gpu(cuda_device, tmp_path, config, grid, scale, transport):
+    """The full C3 (2048²) and C4 (4096², 2.5M cells) steps, and a small C3-like
+    case, on 2 (or 4) GPUs against the one-GPU engine."""
     ngpu = torch.cuda.device_count()
     if ngpu < 2:
         pytest.skip("needs 2+ GPUs")
     world = 4 if ngpu >= 4 else 2
     from dreamplacett_framework_b200 import synth
     from dreamplacett_framework_b200.engine import CellTensors, ElectricPotentialEngine
-    p = synth.make_placement("c3", scale=scale, grid=grid)
+    p = synth.make_placement(config, scale=scale, grid=grid)
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(cuda_device)
     cells = CellTensors(t(p.x), t(p.y), t(p.size_x_clamped), t(p.size_y_clamped), t(p.offset_x), t(p.offset_y),
                         t(p.ratio), ranges=p.ranges)
@@ -96,7 +98,7 @@ def test_nccl_shards_match_single_gpu(cuda_device, tmp_path, grid, scale, transp
         ref = {k: v.cpu().numpy() for k, v in eng.forward(cells).items()}
         rgx, rgy = (a.cpu().numpy() for a in eng.backward(cells))
     port = _free_port()
-    mp.start_processes(_worker, args=(world, port, str(tmp_path), grid, scale, transport), nprocs=world,
+    mp.start_processes(_worker, args=(world, port, str(tmp_path), config, grid, scale, transport), nprocs=world,
                        start_method="spawn")
     parts = [np.load(tmp_path / f"rank{r}.npz") for r in range(world)]
     np.testing.assert_array_equal(np.concatenate([q["density"] for q in parts]), ref["density"])
