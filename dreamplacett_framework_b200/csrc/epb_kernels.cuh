@@ -79,7 +79,7 @@ constexpr int kOyCache = 4;
 #define EPB_SCATTER_MINB 0
 #endif
 #ifndef EPB_SEL_SCATTER_SPLIT
-#define EPB_SEL_SCATTER_SPLIT 8  // shard scatter: CTAs per selection segment times the shard count
+#define EPB_SEL_SCATTER_SPLIT 8  // shard scatter: CTAs per band-list segment times the shard count
 #endif
 #ifndef EPB_GATHER_WAVES
 #define EPB_GATHER_WAVES 1   // whole-grid gather launch: waves of resident CTAs
@@ -784,6 +784,7 @@ __device__ __forceinline__ float row_edge(const GridGeom& g, int k) {
 }
 
 constexpr int kBandThreads = 512;   // threads of a k_band_update CTA (one segment per CTA)
+static_assert(kSelChunk % kBandThreads == 0, "a band-list segment splits evenly over a CTA");
 
 // CTA s checks segment s of the cells (kSelChunk / kBandThreads cells a thread, all
 // their loads issued first) and lists the segment again when an unlisted cell

@@ -196,7 +196,9 @@ int epb_error_flags(epb_handle* h, epb_stream stream, uint32_t* flags);
  * fixed-point density of every bin is the same integer as on one GPU.  The
  * gather computes the cells whose first bin row is in the band and leaves
  * other gradient entries untouched; a footprint reaching past the halo sets
- * EPB_FLAG_HALO and is clipped. */
+ * EPB_FLAG_HALO and is clipped.  The band list's buffers are allocated by the
+ * first call with a given cell count (that call synchronises the stream), so
+ * make one eager call before capturing a step into a CUDA graph. */
 #define EPB_FLAG_HALO 0x4u
 int epb_create_shard(const epb_config* cfg, int32_t num_shards, int32_t shard, epb_handle** out);
 int epb_shard_geometry(const epb_handle* h, int32_t* num_shards, int32_t* shard, int32_t* rows_per_band,
