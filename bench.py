@@ -702,16 +702,18 @@ def measure_sharded(args, p, dev, world, rank, K, W, flush, e2e=True):
     res = {"total_ms": total_ms, "stages": stages, "t_soak0": t_soak0, "t0": t0, "t1": t1,
            "n_soak": int(n_soak.item()), "graph": args.transport == "peer"}
     if e2e:
-        # pinned host pos in, this rank's gradient array and the energy out
+        # pinned host pos [x | y] in and the summed gradient [gx | gy] out through the sharded
+        # API's host-buffer calls: each rank moves its node slice (1/P) over PCIe, and an
+        # all-gather / reduce-scatter over NVLink completes the positions / sums the gradient;
+        # the energy out
         pos_host = torch.empty(2 * n, dtype=torch.float32).pin_memory()
         pos_host.copy_(pos.cpu())
         grad_host = torch.empty(2 * n, dtype=torch.float32).pin_memory()
-        energy_host = torch.empty(1, dtype=torch.float64).pin_memory()
+        energy_host = torch.empty(1, dtype=sh.energy.dtype).pin_memory()
 
         def e2e_step():
-            pos.copy_(pos_host, non_blocking=True)
-            step()
-            grad_host.copy_(grad, non_blocking=True)
+            sh.forward_host(cells, pos_host, out=outs)
+            sh.backward_host(cells, grad_host)
             energy_host.copy_(sh.energy, non_blocking=True)
 
         K_e2e = max(10, min(K, 200))
@@ -819,8 +821,11 @@ def run_sharded(args, p, dev, world, rank):
         "kernels": kern,
         "exchange_us_per_step": 1000.0 * total_ms / K - kernel_us,
         "e2e": {"value": r["K_e2e"] / (e2e_ms / 1000.0), "unit": UNIT, "steps": r["K_e2e"],
-                "h2d_bytes_per_step": world * 2 * n * 4, "d2h_bytes_per_step": world * (2 * n * 4 + 8),
-                "path": "each rank: pinned pos[2n] H2D, sharded forward+backward, grad[2n] + energy D2H"},
+                "h2d_bytes_per_step": 2 * n * 4, "d2h_bytes_per_step": 2 * n * 4 + world * 8,
+                "path": "ShardedElectricPotential.forward_host / backward_host: each rank copies its 1/P node "
+                        "slice of the pinned pos [x | y] H2D and an NCCL all-gather over NVLink completes the "
+                        "positions; the per-rank gradients are summed by a reduce-scatter and each rank stores "
+                        "its slice of grad [gx | gy] D2H; energy D2H on every rank (bytes summed over ranks)"},
         "gpu_launches": launches_per_step * K * world,
         "cuda_graph": ("timed steps replay one captured graph of forward+backward per rank; per-stage times "
                        "from eager profiled steps; e2e is eager API calls") if r["graph"] else

@@ -245,6 +245,56 @@ class ShardedElectricPotential:
             self.be.gather(cells, self.fxy_ext, self.H, grad_out, grad_x, grad_y)
         return grad_x, grad_y
 
+    # ---- positions in and gradients out through host memory, split over the ranks ----
+    def node_slice(self, n):
+        """This rank's node slice [lo, hi) of n nodes (contiguous, 1/P each) and
+        the padded slice length."""
+        chunk = (int(n) + self.P - 1) // self.P
+        lo = min(self.p * chunk, int(n))
+        return lo, min(lo + chunk, int(n)), chunk
+
+    def _host_buffers(self, n):
+        lo, hi, chunk = self.node_slice(n)
+        if getattr(self, "_hb_n", None) != n:
+            f32 = dict(dtype=torch.float32, device=self.device)
+            self._stage = torch.zeros(2, chunk, **f32)            # this rank's slice of x and y
+            self._gathered = torch.zeros(2, self.P * chunk, **f32)
+            self._gpad = torch.zeros(2, self.P * chunk, **f32)    # this rank's gradients, padded
+            self._gslice = torch.zeros(2, chunk, **f32)           # slice r of the summed gradient
+            self._hb_n = n
+        return lo, hi, chunk
+
+    def forward_host(self, cells: CellTensors, host_pos: torch.Tensor, **kw):
+        """The forward with DREAMPlace's positions [x | y] (2n floats) in host
+        memory (pinned for an asynchronous copy).  Rank r copies only node
+        slice r of x and y (1/P of them) to its GPU, and an all-gather over
+        NVLink fills cells.x and cells.y on every rank: each GPU moves 1/P of
+        the positions over PCIe instead of all of them."""
+        n = cells.num_nodes
+        lo, hi, chunk = self._host_buffers(n)
+        self._stage[0, : hi - lo].copy_(host_pos[lo:hi], non_blocking=True)
+        self._stage[1, : hi - lo].copy_(host_pos[n + lo:n + hi], non_blocking=True)
+        for k, dst in ((0, cells.x), (1, cells.y)):
+            dist.all_gather_into_tensor(self._gathered[k], self._stage[k], group=self.group)
+            dst.copy_(self._gathered[k, :n])
+        return self.forward(cells, **kw)
+
+    def backward_host(self, cells: CellTensors, host_grad: torch.Tensor, grad_out: Optional[torch.Tensor] = None):
+        """The backward with the gradient [gx | gy] (2n floats) going to host
+        memory, split over the ranks: the per-rank gradients (each cell's from
+        the band that owns it, zeros elsewhere) are summed by a reduce-scatter
+        over NVLink, and rank r stores node slice r of the sum to host_grad
+        (other entries untouched).  Returns this rank's slice on the device."""
+        n = cells.num_nodes
+        lo, hi, chunk = self._host_buffers(n)
+        self._gpad.zero_()
+        self.backward(cells, grad_out, self._gpad[0, :n], self._gpad[1, :n])
+        for k in (0, 1):
+            dist.reduce_scatter_tensor(self._gslice[k], self._gpad[k], group=self.group)
+        host_grad[lo:hi].copy_(self._gslice[0, : hi - lo], non_blocking=True)
+        host_grad[n + lo:n + hi].copy_(self._gslice[1, : hi - lo], non_blocking=True)
+        return self._gslice[0, : hi - lo], self._gslice[1, : hi - lo]
+
     def close(self):
         if hasattr(self.be, "close"):
             self.be.close()

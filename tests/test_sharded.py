@@ -59,11 +59,25 @@ def _gloo_worker(rank, world, port, out_dir):
                                       float(p.size_x_clamped.max()), device=torch.device("cpu"), backend=be)
         sh.set_initial_density(torch.from_numpy(p.initial_density_norm()))
         cells = _cells_cpu(p)
-        out = sh.forward(cells)
+        out = {k: v.clone() for k, v in sh.forward(cells).items()}
         gx, gy = sh.backward(cells)
+        # the host-buffer path: positions in from [x | y], each rank copying its node slice and an
+        # all-gather completing them; the summed gradient out, each rank storing its slice
+        n = p.num_nodes
+        host_pos = torch.cat([cells.x, cells.y])
+        cells2 = CellTensors(torch.zeros(n), torch.zeros(n), cells.size_x, cells.size_y, cells.offset_x,
+                             cells.offset_y, cells.ratio, ranges=p.ranges)
+        out2 = sh.forward_host(cells2, host_pos)
+        host_grad = torch.full((2 * n,), float("nan"))
+        sh.backward_host(cells2, host_grad)
+        lo, hi, _ = sh.node_slice(n)
+        assert torch.equal(cells2.x, cells.x) and torch.equal(cells2.y, cells.y)
+        for k in ("density", "potential", "field_x", "field_y", "energy"):
+            assert torch.equal(out2[k], out[k]), k
         np.savez(os.path.join(out_dir, f"rank{rank}.npz"), density=out["density"].numpy(),
                  potential=out["potential"].numpy(), field_x=out["field_x"].numpy(),
-                 field_y=out["field_y"].numpy(), energy=out["energy"].numpy(), gx=gx.numpy(), gy=gy.numpy())
+                 field_y=out["field_y"].numpy(), energy=out["energy"].numpy(), gx=gx.numpy(), gy=gy.numpy(),
+                 host_gx=host_grad[lo:hi].numpy(), host_gy=host_grad[n + lo:n + hi].numpy())
     finally:
         dist.destroy_process_group()
 
@@ -92,6 +106,9 @@ def test_gloo_ranks_match_oracle(oracle, tmp_path, world):
     gx = sum(q["gx"] for q in parts)
     gy = sum(q["gy"] for q in parts)
     assert oracle.rel_linf(gx, rx) < 1e-5 and oracle.rel_linf(gy, ry) < 1e-5
+    # the host-buffer path's slices, in rank order, are the summed gradient
+    np.testing.assert_array_equal(np.concatenate([q["host_gx"] for q in parts]), gx)
+    np.testing.assert_array_equal(np.concatenate([q["host_gy"] for q in parts]), gy)
 
 
 @pytest.mark.gpu

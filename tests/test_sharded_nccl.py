@@ -65,11 +65,26 @@ def _worker(rank, world, port, out_dir, config, grid, scale, transport):
                 assert torch.equal(o2c[k], ref[k]), k
             assert torch.equal(g2x, rgx) and torch.equal(g2y, rgy)
             graph = None
+        # the host-buffer calls: positions from pinned [x | y], each rank copying its node slice and an
+        # all-gather completing them; the summed gradient back, each rank storing its slice
+        n = p.num_nodes
+        keep = {k: out[k].clone() for k in ("density", "potential", "field_x", "field_y", "energy")}
+        host_pos = torch.cat([cells.x, cells.y]).cpu().pin_memory()
+        cells2 = CellTensors(torch.zeros_like(cells.x), torch.zeros_like(cells.y), cells.size_x, cells.size_y,
+                             cells.offset_x, cells.offset_y, cells.ratio, ranges=p.ranges)
+        out2 = sh.forward_host(cells2, host_pos)
+        host_grad = torch.full((2 * n,), float("nan")).pin_memory()
+        sh.backward_host(cells2, host_grad)
+        torch.cuda.synchronize(dev)
+        for k in keep:
+            assert torch.equal(out2[k], keep[k]), k
+        lo, hi, _ = sh.node_slice(n)
         flags = sh.be.error_flags()
         torch.cuda.synchronize(dev)
         np.savez(os.path.join(out_dir, f"rank{rank}.npz"),
-                 **{k: out[k].cpu().numpy() for k in ("density", "potential", "field_x", "field_y", "energy")},
-                 gx=gx.cpu().numpy(), gy=gy.cpu().numpy(), flags=np.array(flags))
+                 **{k: keep[k].cpu().numpy() for k in keep},
+                 gx=gx.cpu().numpy(), gy=gy.cpu().numpy(), flags=np.array(flags),
+                 host_gx=host_grad[lo:hi].numpy(), host_gy=host_grad[n + lo:n + hi].numpy())
         dist.barrier()
         torch.cuda.synchronize(dev)
     finally:
@@ -110,3 +125,6 @@ def test_nccl_shards_match_single_gpu(cuda_device, tmp_path, config, grid, scale
         assert int(q["flags"]) == 0
     assert rel(sum(q["gx"] for q in parts), rgx) < 1e-5
     assert rel(sum(q["gy"] for q in parts), rgy) < 1e-5
+    # the host-buffer path: the ranks' slices, in rank order, are the summed gradient
+    np.testing.assert_array_equal(np.concatenate([q["host_gx"] for q in parts]), sum(q["gx"] for q in parts))
+    np.testing.assert_array_equal(np.concatenate([q["host_gy"] for q in parts]), sum(q["gy"] for q in parts))
