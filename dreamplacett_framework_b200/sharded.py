@@ -284,7 +284,9 @@ class ShardedElectricPotential:
         memory, split over the ranks: the per-rank gradients (each cell's from
         the band that owns it, zeros elsewhere) are summed by a reduce-scatter
         over NVLink, and rank r stores node slice r of the sum to host_grad
-        (other entries untouched).  Returns this rank's slice on the device."""
+        (other entries untouched).  The store is asynchronous on the current
+        stream when host_grad is pinned: synchronise before reading it.
+        Returns this rank's slice on the device."""
         n = cells.num_nodes
         lo, hi, chunk = self._host_buffers(n)
         self._gpad.zero_()
