@@ -69,7 +69,11 @@ def gamma_of(params: NesterovParams, overflow: float, bin_w: float, bin_h: float
 
 
 def mu_of(params: NesterovParams, d_hpwl: float) -> float:
-    return min(max(params.mu0 ** (1.0 - d_hpwl / params.hpwl_ref_delta), params.mu_min), params.mu_max)
+    """mu0^(1 - dHPWL / dHPWL_ref) clamped to [mu_min, mu_max].  The exponent
+    is bounded to +-1000 first, so an HPWL change far beyond dHPWL_ref
+    saturates at the clamp instead of overflowing the power."""
+    e = min(max(1.0 - d_hpwl / params.hpwl_ref_delta, -1000.0), 1000.0)
+    return min(max(params.mu0 ** e, params.mu_min), params.mu_max)
 
 
 @dataclass

@@ -36,7 +36,9 @@ def gamma_of(p, overflow, bin_w, bin_h):
 
 
 def mu_of(p, d_hpwl):
-    return min(max(p["mu0"] ** (1.0 - d_hpwl / p["hpwl_ref_delta"]), p["mu_min"]), p["mu_max"])
+    # the exponent bounded first: a change far beyond the reference saturates at the clamp
+    e = min(max(1.0 - d_hpwl / p["hpwl_ref_delta"], -1000.0), 1000.0)
+    return min(max(p["mu0"] ** e, p["mu_min"]), p["mu_max"])
 
 
 PARAMS = dict(iterations=100, target_density=1.0, density_weight=8e-5, gamma=4.0, learning_rate=0.01,

@@ -36,11 +36,13 @@ def test_schedules_closed_forms():
     # mu: mu0 at no change, clamped at both ends
     assert math.isclose(onest.mu_of(P, 0.0), 1.1)
     assert onest.mu_of(P, 1e9) == 0.75 and onest.mu_of(P, -1e9) == 1.1
+    # HPWL changes far beyond the reference (a large design's first iterations) saturate, not overflow
+    assert onest.mu_of(P, 1e13) == 0.75 and onest.mu_of(P, -1e13) == 1.1
     from dreamplacett_framework_b200 import nesterov as dn
     dp = dn.NesterovParams()
     for tau in (0.0, 0.07, 0.5, 1.0):
         assert math.isclose(dn.gamma_of(dp, tau, 9.0, 11.0), onest.gamma_of(P, tau, 9.0, 11.0))
-    for d in (-1e6, 0.0, 3e5, 1e7):
+    for d in (-1e13, -1e6, 0.0, 3e5, 1e7, 1e13):
         assert math.isclose(dn.mu_of(dp, d), onest.mu_of(P, d))
 
 
