@@ -21,6 +21,13 @@ from dreamplacett_framework_b200 import synth
 from dreamplacett_framework_b200.wirelength import synthetic_netlist
 
 
+# C5-size trajectory bars (relative), about twice the measured differences: the first
+# C5_TIGHT iterations per quantity, then the whole 200 for hpwl and overflow
+C5_TIGHT = 20
+C5_TOL_TIGHT = {"hpwl": 5e-3, "overflow": 5e-3, "step": 5e-3, "density_weight": 2e-2, "wirelength": 1e-2}
+C5_TOL_ALL = {"hpwl": 6e-2, "overflow": 1e-2}
+
+
 def _design(scale=0.02, grid=128, seed=4, spread=0.01):
     """A small C1-like design started clustered at the die centre."""
     p = synth.center_init(synth.make_placement("c1", scale=scale, grid=grid, seed=seed), seed=seed, spread=spread)
@@ -107,6 +114,39 @@ def test_device_placer_follows_the_restatement(cuda_device, oracle):
     assert got["overflow"][-1] < 0.07 and ref["overflow"][-1] < 0.07
     assert abs(len(got["hpwl"]) - len(ref["hpwl"])) <= 0.1 * len(ref["hpwl"])
     assert abs(got["hpwl"][-1] / ref["hpwl"][-1] - 1) < 0.05
+
+
+@pytest.mark.gpu
+def test_c5_nesterov_follows_the_restatement(cuda_device):
+    """C5 size: 1.1M movable cells + 300k fillers on 1024² bins, the seeded
+    synthetic netlist (1.1M nets, 4.0M pins), 200 iterations from the C5
+    positions with the stop overflow at 0.  The device placer against the CPU
+    restatement's trajectory (tests/golden/c5_nesterov.npz, made by
+    tests/golden/make_c5_nesterov.py): fp32 device sums against float64.  The
+    first 20 iterations agree within 0.1-0.5% (the density weight within 1%:
+    its update exponent divides HPWL changes of a 2.9e10 HPWL) with equal
+    backtracks, and the whole runs within 3% (hpwl) and 0.2% (overflow).
+    On this random-netlist design the wirelength term dominates both runs:
+    the cells gather (overflow 0.064 -> 0.954) as the HPWL falls 160x."""
+    import torch
+    from dreamplacett_framework_b200.nesterov import NesterovParams, NesterovPlacer
+    ref = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "c5_nesterov.npz"))
+    p = synth.make_placement("c5")
+    nl = synthetic_netlist(p.size_x, p.size_y, np.arange(p.num_movable), p.num_nodes, seed=0)
+    x = torch.from_numpy(p.x.copy()).to(cuda_device)
+    y = torch.from_numpy(p.y.copy()).to(cuda_device)
+    with NesterovPlacer(p, nl, x, y, NesterovParams(iterations=200, stop_overflow=0.0)) as pl:
+        got = pl.run().as_arrays()
+    K = len(ref["hpwl"])
+    assert len(got["hpwl"]) == K
+    n = C5_TIGHT
+    assert np.array_equal(got["backtracks"][:n], ref["backtracks"][:n])
+    for k, tol in C5_TOL_TIGHT.items():
+        rel = np.max(np.abs(got[k][:n] - ref[k][:n]) / np.maximum(np.abs(ref[k][:n]), 1e-12))
+        assert rel < tol, (k, rel)
+    for k, tol in C5_TOL_ALL.items():
+        rel = np.max(np.abs(got[k] - ref[k]) / np.maximum(np.abs(ref[k]), 1e-12))
+        assert rel < tol, (k, rel)
 
 
 @pytest.mark.gpu
