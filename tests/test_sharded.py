@@ -316,6 +316,82 @@ def test_shard_stages_reject_misaligned_buffers(cuda_device):
         be.close()
 
 
+def _shards_vs_one_gpu(p, cells, P, dev):
+    """Every band's density and its gather over the one-GPU field maps, against
+    the one-GPU engine on the same cells: (band densities, summed gradients,
+    one-GPU outputs, one-GPU gradients, the shards' flags, the engine's flags)."""
+    from dreamplacett_framework_b200.engine import ElectricPotentialEngine
+    from dreamplacett_framework_b200.sharded import EngineShard, halo_rows_for
+    M, N, n = p.num_bins_x, p.num_bins_y, p.num_nodes
+    with ElectricPotentialEngine(M, N, p.xl, p.yl, p.xh, p.yh, device=dev) as eng:
+        ref = {k: v.clone() for k, v in eng.forward(cells).items()}
+        rgx, rgy = (g.clone() for g in eng.backward(cells))
+        eflags = eng.error_flags()
+    shards = [EngineShard(M, N, p.xl, p.yl, p.xh, p.yh, P, q, dev) for q in range(P)]
+    try:
+        RB = shards[0].RB
+        H = halo_rows_for(float(np.nanmax(np.asarray(p.size_x_clamped))), shards[0].bin_size_x)
+        dens = torch.zeros(P, RB * N, device=dev)
+        t1 = torch.zeros(P, RB * N, device=dev)
+        gx = torch.zeros(n, device=dev)
+        gy = torch.zeros(n, device=dev)
+        for q, be in enumerate(shards):
+            be.rows_forward(cells, dens[q], t1[q])
+            r0, h = q * RB, (0 if q == P - 1 else H)
+            fxy = torch.stack([ref["field_x"][r0:r0 + RB + h], ref["field_y"][r0:r0 + RB + h]], dim=-1)
+            be.gather(cells, fxy.reshape(-1).contiguous(), h, None, gx, gy)
+        torch.cuda.synchronize()
+        flags = [be.error_flags() for be in shards]
+    finally:
+        for be in shards:
+            be.close()
+    return dens.reshape(M, N), gx, gy, ref, rgx, rgy, flags, eflags
+
+
+@pytest.mark.gpu
+def test_band_lists_edge_cells(cuda_device):
+    """Cells on and across the band edges, beyond the die on every side,
+    non-finite and zero-size, then a larger cell set on the same shards' grid
+    (the band lists grow): every band's density is the one-GPU density bit for
+    bit, the gradients are the one-GPU gradients bit for bit, and the
+    non-finite cells are flagged by the shards as by the one GPU."""
+    P = 2
+    p = synth.make_placement("c1", scale=0.05, grid=256, seed=3)
+    n = p.num_nodes
+    bsx = (p.xh - p.xl) / p.num_bins_x
+    RB = p.num_bins_x // P
+    x = p.x.copy()
+    sx = np.asarray(p.size_x_clamped, np.float32).copy()
+    mov = np.arange(p.num_movable)
+    edge = np.float32(p.xl + RB * bsx)
+    x[mov[0:50]] = edge                          # starting exactly on the band edge
+    x[mov[50:100]] = edge - sx[mov[50:100]]      # ending exactly on it
+    x[mov[100:150]] = edge - 0.5 * sx[mov[100:150]]   # straddling it
+    x[mov[150:160]] = p.xh + 100.0               # beyond the die, both sides
+    x[mov[160:170]] = p.xl - 500.0
+    x[mov[170:175]] = np.nan                     # non-finite
+    x[mov[175:180]] = np.inf
+    sx[mov[180:190]] = 0.0                       # zero width
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(cuda_device)
+    cells = CellTensors(t(x), t(p.y), t(sx), t(p.size_y_clamped), t(p.offset_x), t(p.offset_y), t(p.ratio),
+                        ranges=p.ranges)
+    pe = synth.make_placement("c1", scale=0.05, grid=256, seed=3)
+    pe.size_x_clamped = sx
+    dens, gx, gy, ref, rgx, rgy, flags, eflags = _shards_vs_one_gpu(pe, cells, P, cuda_device)
+    assert torch.equal(dens, ref["density"])
+    assert torch.equal(gx, rgx) and torch.equal(gy, rgy)
+    assert eflags & 0x1 and any(f & 0x1 for f in flags)
+    assert all((f & ~0x1) == 0 for f in flags)
+    # a larger cell set: the lists grow and are made again
+    p2 = synth.make_placement("c1", scale=0.2, grid=256, seed=5)
+    cells2 = CellTensors(t(p2.x), t(p2.y), t(p2.size_x_clamped), t(p2.size_y_clamped), t(p2.offset_x),
+                         t(p2.offset_y), t(p2.ratio), ranges=p2.ranges)
+    dens, gx, gy, ref, rgx, rgy, flags, eflags = _shards_vs_one_gpu(p2, cells2, P, cuda_device)
+    assert torch.equal(dens, ref["density"])
+    assert torch.equal(gx, rgx) and torch.equal(gy, rgy)
+    assert eflags == 0 and all(f == 0 for f in flags)
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("P", [2, 4])
 def test_band_lists_follow_moving_cells(cuda_device, P):
