@@ -215,7 +215,7 @@ void free_all(epb_handle* h) {
     void* ptrs[] = {h->grid, h->grid2, h->init, h->t1, h->g, h->fxy, h->twM, h->qwM,
                     h->twN, h->qwN, h->partials, h->counter, h->energy_d, h->flags,
                     h->ovf_partials, h->ovf_counter, h->linf_bits, h->bl.sel, h->bl.cnt,
-                    h->bl.geo, h->bl.r, h->bl.listed, h->rho, h->tb.cnt, h->tb.cur, h->tb.start, h->tb.nown,
+                    h->bl.geo, h->bl.r, h->bl.listed, h->bl.ext, h->rho, h->tb.cnt, h->tb.cur, h->tb.start, h->tb.nown,
                     h->tb.first_item, h->tb.items, h->tb.arrive, h->tb.part, h->tb.meta, h->tb.stat, h->tb.key,
                     h->tb.geo, h->tb.bins, h->tb.esc_dyn, h->tb.esc_static, h->tb.esc_grid, h->esc_grid0,
                     h->tile_ovf_part, h->tile_ovf_counter};
@@ -474,7 +474,7 @@ int band_list_reserve(epb_handle* h, int64_t n, cudaStream_t st) {
     if (n <= h->bl_cap) return EPB_OK;
     EPB_CUDA(h, cudaStreamSynchronize(st));
     void** bufs[] = {(void**)&h->bl.sel, (void**)&h->bl.cnt, (void**)&h->bl.geo, (void**)&h->bl.r,
-                     (void**)&h->bl.listed};
+                     (void**)&h->bl.listed, (void**)&h->bl.ext};
     for (void** b : bufs) {
         if (*b) cudaFree(*b);
         *b = nullptr;
@@ -486,6 +486,7 @@ int band_list_reserve(epb_handle* h, int64_t n, cudaStream_t st) {
     if (int rc = dev_alloc(h, &h->bl.geo, (size_t)(nseg * kSelChunk))) return rc;
     if (int rc = dev_alloc(h, &h->bl.r, (size_t)(nseg * kSelChunk))) return rc;
     if (int rc = dev_alloc(h, &h->bl.listed, (size_t)n)) return rc;
+    if (int rc = dev_alloc(h, &h->bl.ext, (size_t)n)) return rc;
     EPB_CUDA(h, cudaMemset(h->bl.listed, 0, (size_t)n));
     h->bl_cap = n;
     h->bl_force = true;

@@ -37,6 +37,7 @@
 //   IDXST: IDXST(a)_k = (-1)^k/2 * IDCT(b)_k with b_0 = 0, b_m = a_{L-m}
 #pragma once
 #include <cstdint>
+#include <cuda_fp16.h>
 #include "fft.cuh"
 #include "geometry.cuh"
 
@@ -766,16 +767,39 @@ struct BandList {
     float4* geo;            // [nseg * kSelChunk] sx, sy, ox, oy of the listed cell (0 for absent offsets)
     float* r;               // [nseg * kSelChunk] ratio (1 when absent)
     unsigned char* listed;  // [n] 1 when the cell is in the list
+    unsigned* ext;          // [n] the cell's cached x extent (band_extent)
 };
 
-// Whether a cell's x extent [xe, xe + sx] (offset added, finite) reaches the
-// coordinates (lo_c, hi_c) of a band widened by some rows, or its footprint
-// may be empty (a non-positive width, or a start past the grid's last row):
-// a superset of the cells whose bin rows meet the band (an edge band's outer
-// side is open, as bins clamp cells beyond the die into the first and last
-// rows), decided with two additions and compares instead of bin arithmetic.
-__device__ __forceinline__ bool band_reaches(float xe, float sx, float lo_c, float hi_c, float last_c) {
-    return !(sx > 0.0f) || xe >= last_c || (xe < hi_c && __fadd_rn(xe, sx) > lo_c);
+// A cell's static x extent relative to its position, [x + lo, x + hi] with
+// lo = offset and hi = offset + width, cached per cell as two half-precision
+// values rounded outward (lo down, hi up), so the check reads 4 bytes instead
+// of the offset and the width: the cached extent holds the cell's true extent.
+// A non-positive width caches (-inf, +inf), a cell that may reach any band; a
+// non-finite offset or width caches NaN, a cell that is flagged every check
+// and never listed.
+__device__ __forceinline__ unsigned band_extent(float ox, float sx) {
+    __half lo, hi;
+    if (!isfinite(ox) || !isfinite(sx)) {
+        lo = hi = __ushort_as_half((unsigned short)0x7e00);   // NaN
+    } else if (!(sx > 0.0f)) {
+        lo = __ushort_as_half((unsigned short)0xfc00);        // -inf
+        hi = __ushort_as_half((unsigned short)0x7c00);        // +inf
+    } else {
+        lo = __float2half_rd(ox);
+        hi = __float2half_ru(__fadd_ru(ox, sx));
+    }
+    return (unsigned)__half_as_ushort(lo) | ((unsigned)__half_as_ushort(hi) << 16);
+}
+
+// Whether the cached extent at position x reaches the coordinates (lo_c, hi_c)
+// of a band widened by some rows, or may start past the grid's last row: a
+// superset of the cells whose bin rows meet the band (an edge band's outer side
+// is open, as bins clamp cells beyond the die into the first and last rows),
+// decided with two additions and compares instead of bin arithmetic.
+__device__ __forceinline__ bool band_reaches(float x, unsigned ext, float lo_c, float hi_c, float last_c) {
+    const float xlo = __fadd_rd(x, __half2float(__ushort_as_half((unsigned short)(ext & 0xffffu))));
+    const float xhi = __fadd_ru(x, __half2float(__ushort_as_half((unsigned short)(ext >> 16))));
+    return xlo >= last_c || (xlo < hi_c && xhi > lo_c);
 }
 
 // The coordinate of row k's lower edge, as bin_floor computes it.
@@ -790,26 +814,33 @@ static_assert(kSelChunk % kBandThreads == 0, "a band-list segment splits evenly 
 // their loads issued first) and lists the segment again when an unlisted cell
 // reaches the band [row0, row1) widened by one row, or when force.  A listing
 // takes the cells that reach the band widened by kBandMargin rows, so a cell
-// must travel that far before it makes its segment list again.  Cells with
-// non-finite x data are flagged (and never listed).
+// must travel that far before it makes its segment list again.  With force the
+// cached extents are made from the offsets and widths; otherwise only the
+// positions, the cached extents and the list flags are read.  Cells with
+// non-finite data are flagged (and never listed).
 __global__ void __launch_bounds__(kBandThreads)
 k_band_update(CellView c, GridGeom g, int row0, int row1, BandList b, int force, unsigned* __restrict__ flags) {
     constexpr int R = kSelChunk / kBandThreads;
     const int64_t seg0 = (int64_t)blockIdx.x * kSelChunk;
-    float x[R], ox[R], sx[R];
+    float x[R];
+    unsigned ext[R];
     unsigned char was[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
         const int64_t i = seg0 + r * kBandThreads + threadIdx.x;
-        x[r] = ox[r] = 0.0f;
-        sx[r] = 1.0f;
+        x[r] = 0.0f;
+        ext[r] = 0u;
         was[r] = 1;
         if (i < c.n) {
             const int64_t node = cell_node(c, i);
             was[r] = b.listed[i];
             x[r] = __ldg(c.x + node);
-            ox[r] = c.ox ? __ldg(c.ox + node) : 0.0f;
-            sx[r] = __ldg(c.sx + node);
+            if (force) {
+                ext[r] = band_extent(c.ox ? __ldg(c.ox + node) : 0.0f, __ldg(c.sx + node));
+                b.ext[i] = ext[r];
+            } else {
+                ext[r] = b.ext[i];
+            }
         }
     }
     const float last_c = row_edge(g, g.M - 1);
@@ -822,11 +853,11 @@ k_band_update(CellView c, GridGeom g, int row0, int row1, BandList b, int force,
 #pragma unroll
     for (int r = 0; r < R; ++r) {
         const int64_t i = seg0 + r * kBandThreads + threadIdx.x;
-        const float xe = c.ox ? __fadd_rn(x[r], ox[r]) : x[r];
-        const bool ok = i < c.n && isfinite(xe) && isfinite(sx[r]);
+        const bool nan_ext = (ext[r] & 0x7fffu) > 0x7c00u;     // the cached NaN of a bad offset or width
+        const bool ok = i < c.n && isfinite(x[r]) && !nan_ext;
         bad |= (i < c.n && !ok) ? 1u : 0u;
-        need |= ok && !was[r] && band_reaches(xe, sx[r], lo1, hi1, last_c);
-        in[r] = ok && band_reaches(xe, sx[r], loM, hiM, last_c);
+        need |= ok && !was[r] && band_reaches(x[r], ext[r], lo1, hi1, last_c);
+        in[r] = ok && band_reaches(x[r], ext[r], loM, hiM, last_c);
     }
     if (bad) atomicOr(flags, kFlagNonFinite);
     if (!__syncthreads_or(need || force)) return;
@@ -851,7 +882,8 @@ k_band_update(CellView c, GridGeom g, int row0, int row1, BandList b, int force,
             const int64_t node = cell_node(c, i);
             const int64_t slot = seg0 + run + base + __popc(m & ((1u << lane) - 1u));
             b.sel[slot] = (int)i;
-            b.geo[slot] = make_float4(sx[r], __ldg(c.sy + node), ox[r], c.oy ? __ldg(c.oy + node) : 0.0f);
+            b.geo[slot] = make_float4(__ldg(c.sx + node), __ldg(c.sy + node), c.ox ? __ldg(c.ox + node) : 0.0f,
+                                      c.oy ? __ldg(c.oy + node) : 0.0f);
             b.r[slot] = c.ratio ? __ldg(c.ratio + node) : 1.0f;
         }
         run += tot;
