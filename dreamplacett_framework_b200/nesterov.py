@@ -184,6 +184,12 @@ class NesterovPlacer:
         self.last_ep_ms = self._ev[0].elapsed_time(self._ev[1])
         return g, float(vals[0]), float(vals[1]), float(vals[2]), float(vals[3]) / self.movable_area, gw, ge
 
+    @staticmethod
+    def _norms(a: torch.Tensor, b: torch.Tensor):
+        """(||a||, ||b||) as floats with one device-to-host read."""
+        n = torch.stack([torch.linalg.vector_norm(a), torch.linalg.vector_norm(b)]).tolist()
+        return float(n[0]), float(n[1])
+
     def combine(self, gw: torch.Tensor, ge: torch.Tensor, lam: float) -> torch.Tensor:
         """Preconditioned gradient of W + lam * E from its two parts."""
         pre = torch.clamp(self.deg + lam * self.area, min=1.0)
@@ -212,8 +218,7 @@ class NesterovPlacer:
         a = 1.0
         hp_prev = hp
         for it in range(K):
-            dv = float(torch.linalg.vector_norm(v - v_prev))
-            dg = float(torch.linalg.vector_norm(g - g_prev))
+            dv, dg = self._norms(v - v_prev, g - g_prev)
             alpha = dv / dg if dg > 0 else step0
             bt = 0
             while True:
@@ -221,8 +226,7 @@ class NesterovPlacer:
                 a_new = 0.5 * (1.0 + math.sqrt(4.0 * a * a + 1.0))
                 v_new = self._clamp(u_new + ((a - 1.0) / a_new) * (u_new - u))
                 g_new, wl, hp, en, ovf, gw, ge = self.evaluate(v_new, lam, gamma)
-                dv = float(torch.linalg.vector_norm(v_new - v))
-                dg = float(torch.linalg.vector_norm(g_new - g))
+                dv, dg = self._norms(v_new - v, g_new - g)
                 alpha_hat = dv / dg if dg > 0 else alpha
                 if alpha_hat >= P.backtrack_ratio * alpha or bt >= P.backtrack_limit or alpha_hat == 0.0:
                     break
